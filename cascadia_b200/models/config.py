@@ -1,0 +1,200 @@
+"""Model configurations for the architectures the engine serves.
+
+The field names follow HF ``config.json`` (what the reference reads through
+``load_model_config``, crates/cascadia-engine-openvino/src/rotary.rs:186) so a
+real config can be loaded with :meth:`ModelConfig.from_hf`.
+"""
+from __future__ import annotations
+
+import json
+import math
+from dataclasses import asdict, dataclass, field
+from typing import Optional
+
+import torch
+
+
+@dataclass
+class ModelConfig:
+    arch: str = "llama"  # llama | qwen3_moe | kimi_k2 (deepseek-v3 style MLA + MoE)
+    vocab_size: int = 128256
+    hidden_size: int = 4096
+    num_layers: int = 32
+    num_heads: int = 32
+    num_kv_heads: int = 8
+    head_dim: int = 128
+    intermediate_size: int = 14336
+    rope_theta: float = 500000.0
+    rope_scaling: Optional[dict] = None
+    rms_eps: float = 1e-5
+    tie_word_embeddings: bool = False
+    partial_rotary_factor: float = 1.0
+    max_position: int = 131072
+    group_size: int = 128
+    eos_token_ids: tuple = (128001, 128009)
+    # --- sparse MoE ---
+    num_experts: int = 0
+    num_experts_per_tok: int = 0
+    moe_intermediate_size: int = 0
+    num_shared_experts: int = 0
+    router: str = "softmax"  # softmax | sigmoid
+    norm_topk_prob: bool = True
+    routed_scaling_factor: float = 1.0
+    first_k_dense_replace: int = 0
+    qk_norm: bool = False
+    # --- MLA ---
+    q_lora_rank: int = 0
+    kv_lora_rank: int = 0
+    qk_rope_head_dim: int = 0
+    qk_nope_head_dim: int = 0
+    v_head_dim: int = 0
+
+    @property
+    def is_moe(self) -> bool:
+        return self.num_experts > 0
+
+    @property
+    def is_mla(self) -> bool:
+        return self.kv_lora_rank > 0
+
+    @property
+    def rot_dim(self) -> int:
+        return int(self.head_dim * self.partial_rotary_factor)
+
+    def to_json(self) -> str:
+        return json.dumps(asdict(self), indent=1)
+
+    @staticmethod
+    def from_dict(d: dict) -> "ModelConfig":
+        known = {f for f in ModelConfig.__dataclass_fields__}
+        kw = {k: v for k, v in d.items() if k in known}
+        if "eos_token_ids" in kw and isinstance(kw["eos_token_ids"], list):
+            kw["eos_token_ids"] = tuple(kw["eos_token_ids"])
+        return ModelConfig(**kw)
+
+    @staticmethod
+    def from_hf(d: dict) -> "ModelConfig":
+        """Map a HuggingFace config.json dict (Llama/Qwen3-MoE/DeepSeek-V3)."""
+        d = d.get("text_config", d)
+        heads = d["num_attention_heads"]
+        hidden = d["hidden_size"]
+        c = ModelConfig(
+            vocab_size=d["vocab_size"],
+            hidden_size=hidden,
+            num_layers=d["num_hidden_layers"],
+            num_heads=heads,
+            num_kv_heads=d.get("num_key_value_heads", heads),
+            head_dim=d.get("head_dim") or hidden // heads,
+            intermediate_size=d.get("intermediate_size", 0),
+            rope_theta=float(d.get("rope_theta", 10000.0)),
+            rope_scaling=d.get("rope_scaling"),
+            rms_eps=float(d.get("rms_norm_eps", 1e-5)),
+            tie_word_embeddings=bool(d.get("tie_word_embeddings", False)),
+            partial_rotary_factor=float(d.get("partial_rotary_factor", 1.0)),
+            max_position=int(d.get("max_position_embeddings", 131072)),
+        )
+        eos = d.get("eos_token_id")
+        if eos is not None:
+            c.eos_token_ids = tuple(eos) if isinstance(eos, list) else (eos,)
+        mt = d.get("model_type", "")
+        if d.get("num_experts") or d.get("n_routed_experts"):
+            c.num_experts = d.get("num_experts") or d.get("n_routed_experts")
+            c.num_experts_per_tok = d["num_experts_per_tok"]
+            c.moe_intermediate_size = d["moe_intermediate_size"]
+            c.num_shared_experts = d.get("n_shared_experts", 0) or 0
+            c.norm_topk_prob = bool(d.get("norm_topk_prob", True))
+            c.routed_scaling_factor = float(d.get("routed_scaling_factor", 1.0))
+            c.first_k_dense_replace = int(d.get("first_k_dense_replace", 0))
+            c.router = "sigmoid" if d.get("scoring_func") == "sigmoid" else "softmax"
+            c.arch = "kimi_k2" if d.get("kv_lora_rank") else "qwen3_moe"
+        if d.get("kv_lora_rank"):
+            c.q_lora_rank = d.get("q_lora_rank") or 0
+            c.kv_lora_rank = d["kv_lora_rank"]
+            c.qk_rope_head_dim = d["qk_rope_head_dim"]
+            c.qk_nope_head_dim = d["qk_nope_head_dim"]
+            c.v_head_dim = d["v_head_dim"]
+        if mt.startswith("qwen3"):
+            c.qk_norm = True
+        return c
+
+
+LLAMA3_SCALING = {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                  "high_freq_factor": 4.0, "original_max_position_embeddings": 8192}
+
+PRESETS = {
+    # BASELINE config #2 (north-star).
+    "llama-3.1-8b": ModelConfig(rope_scaling=dict(LLAMA3_SCALING)),
+    # BASELINE config #1 and the spec-decode draft.
+    "llama-3.2-1b": ModelConfig(hidden_size=2048, num_layers=16, num_heads=32, num_kv_heads=8,
+                                head_dim=64, intermediate_size=8192,
+                                rope_scaling=dict(LLAMA3_SCALING, factor=32.0),
+                                tie_word_embeddings=True),
+    # BASELINE config #4.
+    "qwen3-30b-a3b": ModelConfig(arch="qwen3_moe", vocab_size=151936, hidden_size=2048,
+                                 num_layers=48, num_heads=32, num_kv_heads=4, head_dim=128,
+                                 intermediate_size=6144, rope_theta=1000000.0, rms_eps=1e-6,
+                                 num_experts=128, num_experts_per_tok=8, moe_intermediate_size=768,
+                                 router="softmax", norm_topk_prob=True, qk_norm=True,
+                                 eos_token_ids=(151645, 151643)),
+    # BASELINE config #5 (DeepSeek-V3-style MLA + MoE), INT4 group 32.
+    "kimi-k2": ModelConfig(arch="kimi_k2", vocab_size=163840, hidden_size=7168, num_layers=61,
+                           num_heads=64, num_kv_heads=64, head_dim=192, intermediate_size=18432,
+                           rope_theta=50000.0, rms_eps=1e-6, num_experts=384,
+                           num_experts_per_tok=8, moe_intermediate_size=2048,
+                           num_shared_experts=1, router="sigmoid", norm_topk_prob=True,
+                           routed_scaling_factor=2.827, first_k_dense_replace=1,
+                           q_lora_rank=1536, kv_lora_rank=512, qk_rope_head_dim=64,
+                           qk_nope_head_dim=128, v_head_dim=128, group_size=32,
+                           eos_token_ids=(163586,)),
+    # Small shapes for tests (same code paths).
+    "tiny-llama": ModelConfig(vocab_size=512, hidden_size=256, num_layers=2, num_heads=4,
+                              num_kv_heads=2, head_dim=64, intermediate_size=512,
+                              rope_scaling=dict(LLAMA3_SCALING), eos_token_ids=(1,)),
+    "tiny-llama-128": ModelConfig(vocab_size=1024, hidden_size=512, num_layers=2, num_heads=8,
+                                  num_kv_heads=2, head_dim=128, intermediate_size=1024,
+                                  eos_token_ids=(1,)),
+    "tiny-moe": ModelConfig(arch="qwen3_moe", vocab_size=512, hidden_size=256, num_layers=2,
+                            num_heads=4, num_kv_heads=2, head_dim=64, intermediate_size=512,
+                            num_experts=8, num_experts_per_tok=2, moe_intermediate_size=128,
+                            router="softmax", qk_norm=True, eos_token_ids=(1,)),
+    "tiny-mla": ModelConfig(arch="kimi_k2", vocab_size=512, hidden_size=256, num_layers=2,
+                            num_heads=4, num_kv_heads=4, head_dim=96, intermediate_size=512,
+                            num_experts=8, num_experts_per_tok=2, moe_intermediate_size=128,
+                            num_shared_experts=1, router="sigmoid", routed_scaling_factor=2.5,
+                            first_k_dense_replace=1, q_lora_rank=128, kv_lora_rank=128,
+                            qk_rope_head_dim=32, qk_nope_head_dim=64, v_head_dim=64,
+                            group_size=32, eos_token_ids=(1,)),
+}
+
+
+def get_config(name: str) -> ModelConfig:
+    if name not in PRESETS:
+        raise KeyError(f"unknown model preset {name!r}; known: {sorted(PRESETS)}")
+    from copy import deepcopy
+
+    return deepcopy(PRESETS[name])
+
+
+def rope_inv_freq(cfg: ModelConfig, rot: Optional[int] = None) -> torch.Tensor:
+    rot = rot or cfg.rot_dim
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, rot, 2, dtype=torch.float64) / rot))
+    sc = cfg.rope_scaling
+    if sc and sc.get("rope_type", sc.get("type")) == "llama3":
+        # crates/cascadia-engine-openvino/src/rotary.rs:111-140
+        factor = sc["factor"]
+        low, high = sc["low_freq_factor"], sc["high_freq_factor"]
+        old = float(sc["original_max_position_embeddings"])
+        low_wl, high_wl = old / low, old / high
+        wl = 2 * math.pi / inv
+        smooth = (old / wl - low) / (high - low)
+        mid = (1 - smooth) * inv / factor + smooth * inv
+        inv = torch.where(wl < high_wl, inv, torch.where(wl > low_wl, inv / factor, mid))
+    return inv.float()
+
+
+def rope_table(cfg: ModelConfig, max_pos: int, rot: Optional[int] = None,
+               device="cpu") -> torch.Tensor:
+    """[max_pos, rot] fp32: cos in the first rot/2 columns, sin in the rest."""
+    inv = rope_inv_freq(cfg, rot)
+    ang = torch.outer(torch.arange(max_pos, dtype=torch.float32), inv)
+    return torch.cat([ang.cos(), ang.sin()], dim=1).to(device)

@@ -1,0 +1,390 @@
+"""Llama-family INT4 decoder (dense), tensor- and pipeline-parallel aware.
+
+One ``LlamaModel`` holds the layers ``[layer_start, layer_end)`` of one
+pipeline stage, sharded ``tp_size`` ways:
+
+* column-parallel: fused QKV (heads split), fused gate/up (interleaved per
+  128-row tile so the GEMM epilogue applies SiLU(gate)*up);
+* row-parallel: o_proj and down_proj, followed by a sum over the TP group
+  (``TPGroup.all_reduce`` or one of the fused GEMM+collective paths);
+* vocab-parallel LM head with a (value, index) argmax merge.
+
+Math (per layer): pre-norm RMSNorm -> QKV -> RoPE (llama3 scaling) -> paged
+GQA attention -> o_proj (+residual) -> RMSNorm -> SwiGLU -> down (+residual);
+the same decoder the reference exports per stage
+(tools/export_shards.py:657 cached_layer_forward_sdpa, :822-989 stage wrappers).
+
+On CUDA every op is one of our sm_100a kernels; on CPU the forward uses the
+fp32 oracle in ``ops.reference`` (the CPU engine / BASELINE CPU config).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List, Optional, Sequence
+
+import torch
+
+from .. import ops
+from ..ops import reference as ref
+from ..quant import Int4Weight
+from ..runtime.kv_cache import BLOCK_SIZE, KVCache
+from .config import ModelConfig, rope_table
+
+
+class QLinear:
+    """An INT4 weight ready for its device: kernel blob on CUDA, fp32 on CPU."""
+
+    def __init__(self, w: Int4Weight, device, interleave_gate_up: bool = False):
+        self.n, self.k, self.group_size = w.n, w.k, w.group_size
+        self.interleaved = interleave_gate_up
+        device = torch.device(device)
+        if device.type == "cuda":
+            self.blob = w.to(device).blob(interleave_gate_up)
+            self.w_ref = None
+        else:
+            self.blob = None
+            self.w_ref = w.dequant_bf16().float()  # exact kernel values, fp32 storage
+
+    def __call__(self, x, epilogue=ops.EPI_STORE, residual=None, out=None):
+        if self.blob is not None:
+            return ops.w4a16_gemm(x, self.blob, self.n, self.group_size, epilogue, residual, out)
+        y = x.float() @ self.w_ref.t()
+        if epilogue == ops.EPI_SILU:
+            y = ref.silu_mul(y[:, :self.n // 2], y[:, self.n // 2:])
+        elif epilogue == ops.EPI_RESID:
+            y = y + residual.float()
+        y = y.to(torch.bfloat16)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+
+
+@dataclass
+class LayerWeights:
+    in_norm: torch.Tensor
+    post_norm: torch.Tensor
+    qkv: QLinear
+    o: QLinear
+    gate_up: QLinear
+    down: QLinear
+
+
+class TPGroup:
+    """Tensor-parallel communicator used by the models (NCCL baseline path)."""
+
+    def __init__(self, rank: int = 0, size: int = 1, group=None):
+        self.rank, self.size, self.group = rank, size, group
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        if self.size > 1:
+            torch.distributed.all_reduce(x, group=self.group)
+        return x
+
+    def all_gather_rows(self, x: torch.Tensor) -> torch.Tensor:
+        """[n, ...] on each rank -> [size, n, ...]."""
+        if self.size == 1:
+            return x.unsqueeze(0)
+        out = torch.empty((self.size,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+        torch.distributed.all_gather_into_tensor(out, x.contiguous(), group=self.group)
+        return out
+
+
+def _layer_generator(seed: int, layer: int, device) -> torch.Generator:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1000003 + layer * 7919 + 17)
+    return g
+
+
+def random_int4(n: int, k: int, g: torch.Generator, device, std=0.02, group_size=128,
+                scale_dtype=torch.float16) -> Int4Weight:
+    w = torch.randn(n, k, generator=g, device=device) * std
+    return Int4Weight.quantize(w, group_size, scale_dtype)
+
+
+class LlamaModel:
+    def __init__(self, cfg: ModelConfig, device, tp: Optional[TPGroup] = None,
+                 layer_start: int = 0, layer_end: Optional[int] = None,
+                 has_embed: bool = True, has_head: bool = True):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.tp = tp or TPGroup()
+        self.layer_start = layer_start
+        self.layer_end = cfg.num_layers if layer_end is None else layer_end
+        self.has_embed = has_embed
+        self.has_head = has_head
+        t = self.tp.size
+        assert cfg.num_heads % t == 0 and cfg.num_kv_heads % t == 0, "heads must divide TP"
+        self.hq = cfg.num_heads // t
+        self.hkv = cfg.num_kv_heads // t
+        self.d = cfg.head_dim
+        self.inter = cfg.intermediate_size // t
+        self.vocab_shard = cfg.vocab_size // t if cfg.vocab_size % t == 0 else cfg.vocab_size
+        self.layers: List[LayerWeights] = []
+        self.embed: Optional[torch.Tensor] = None
+        self.final_norm: Optional[torch.Tensor] = None
+        self.lm_head: Optional[QLinear] = None
+        self.cos_sin: Optional[torch.Tensor] = None
+        self.kv: Optional[KVCache] = None
+        self.scale = 1.0 / math.sqrt(self.d)
+
+    @property
+    def num_local_layers(self) -> int:
+        return self.layer_end - self.layer_start
+
+    # ------------------------------------------------------------ weights
+    def init_random(self, seed: int = 0, std: float = 0.02, gen_device=None):
+        """Random N(0, std) weights, INT4 sym group-quantised, generated per
+        layer on the device with a layer-keyed seed so every TP/PP split of the
+        same (seed, config) holds slices of the same full model."""
+        cfg, t, r = self.cfg, self.tp.size, self.tp.rank
+        # Generate where asked (CPU keeps CPU/GPU parity tests bit-identical),
+        # then move every finished tensor to the model's device.
+        dev = torch.device(gen_device) if gen_device is not None else self.device
+        gs = cfg.group_size
+        h, d = cfg.hidden_size, cfg.head_dim
+        self.cos_sin = rope_table(cfg, min(cfg.max_position, 1 << 16), device=self.device)
+        if self.has_embed or (self.has_head and cfg.tie_word_embeddings):
+            g = _layer_generator(seed, 100000, dev)
+            self.embed = (torch.randn(cfg.vocab_size, h, generator=g, device=dev) * std).to(
+                torch.bfloat16).to(self.device)
+        for li in range(self.layer_start, self.layer_end):
+            g = _layer_generator(seed, li, dev)
+            q = random_int4(cfg.num_heads * d, h, g, dev, std, gs)
+            k = random_int4(cfg.num_kv_heads * d, h, g, dev, std, gs)
+            v = random_int4(cfg.num_kv_heads * d, h, g, dev, std, gs)
+            o = random_int4(h, cfg.num_heads * d, g, dev, std, gs)
+            gate = random_int4(cfg.intermediate_size, h, g, dev, std, gs)
+            up = random_int4(cfg.intermediate_size, h, g, dev, std, gs)
+            down = random_int4(h, cfg.intermediate_size, g, dev, std, gs)
+            self.layers.append(self._shard_layer(
+                q, k, v, o, gate, up, down,
+                torch.ones(h, dtype=torch.bfloat16, device=dev),
+                torch.ones(h, dtype=torch.bfloat16, device=dev)))
+            del q, k, v, o, gate, up, down
+        if self.has_head:
+            self.final_norm = torch.ones(h, dtype=torch.bfloat16, device=self.device)
+            if cfg.tie_word_embeddings:
+                head = Int4Weight.quantize(self.embed.to(dev).float(), gs)
+            else:
+                g = _layer_generator(seed, 100001, dev)
+                head = random_int4(cfg.vocab_size, h, g, dev, std, gs)
+            self.lm_head = QLinear(self._vocab_shard(head), self.device)
+        return self
+
+    def _vocab_shard(self, w: Int4Weight) -> Int4Weight:
+        t, r = self.tp.size, self.tp.rank
+        if t == 1 or self.cfg.vocab_size % t:
+            return w
+        vs = self.cfg.vocab_size // t
+        return w.rows(r * vs, (r + 1) * vs)
+
+    def _shard_layer(self, q, k, v, o, gate, up, down, in_norm, post_norm) -> LayerWeights:
+        t, r, d = self.tp.size, self.tp.rank, self.cfg.head_dim
+        hq, hkv, it = self.hq, self.hkv, self.inter
+        qkv = Int4Weight.cat_rows([q.rows(r * hq * d, (r + 1) * hq * d),
+                                   k.rows(r * hkv * d, (r + 1) * hkv * d),
+                                   v.rows(r * hkv * d, (r + 1) * hkv * d)])
+        gu = Int4Weight.cat_rows([gate.rows(r * it, (r + 1) * it), up.rows(r * it, (r + 1) * it)])
+        dev = self.device
+        return LayerWeights(
+            in_norm=in_norm.to(dev), post_norm=post_norm.to(dev),
+            qkv=QLinear(qkv, dev),
+            o=QLinear(o.cols(r * hq * d, (r + 1) * hq * d), dev),
+            gate_up=QLinear(gu, dev, interleave_gate_up=True),
+            down=QLinear(down.cols(r * it, (r + 1) * it), dev))
+
+    def load_layer(self, li: int, tensors: dict, group_size: int):
+        """Install one layer from a shard's tensors (canonical INT4 form)."""
+        def w(name):
+            return Int4Weight(tensors[name + ".packed"], tensors[name + ".scales"], group_size)
+        self.layers.append(self._shard_layer(
+            w("q_proj"), w("k_proj"), w("v_proj"), w("o_proj"), w("gate_proj"), w("up_proj"),
+            w("down_proj"), tensors["input_layernorm"].to(torch.bfloat16),
+            tensors["post_attention_layernorm"].to(torch.bfloat16)))
+
+    # ------------------------------------------------------------ KV cache
+    def allocate_kv(self, num_blocks: int) -> KVCache:
+        self.kv = KVCache(self.num_local_layers, num_blocks, self.hkv, self.d, self.device)
+        return self.kv
+
+    def kv_bytes_per_block(self) -> int:
+        return KVCache.bytes_per_block(self.num_local_layers, self.hkv, self.d)
+
+    # ------------------------------------------------------------ forward
+    def embed_tokens(self, ids: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty(ids.shape[0], self.cfg.hidden_size, dtype=torch.bfloat16,
+                              device=self.device)
+        if self.device.type == "cuda":
+            ops.embedding(ids, self.embed, out)
+        else:
+            out.copy_(self.embed[ids.long()])
+        return out
+
+    def _norm(self, x, w, out, residual=None):
+        if self.device.type == "cuda":
+            return ops.rmsnorm(x, w, out, self.cfg.rms_eps, residual=residual)
+        if residual is not None:
+            residual.copy_((x.float() + residual.float()).to(torch.bfloat16))
+            x = residual
+        out.copy_(ref.rmsnorm(x, w, self.cfg.rms_eps).to(torch.bfloat16))
+        return out
+
+    def forward(self, batch: "Batch", hidden: torch.Tensor) -> torch.Tensor:
+        """Run this stage's layers on `hidden` ([T, H] bf16, the residual
+        stream) in place; returns the residual stream (pre final-norm)."""
+        cfg = self.cfg
+        T = hidden.shape[0]
+        h = torch.empty_like(hidden)
+        pending: Optional[torch.Tensor] = None  # TP partial sum not yet added
+        tp1 = self.tp.size == 1
+        for i, lw in enumerate(self.layers):
+            self._norm(pending if pending is not None else hidden, lw.in_norm, h,
+                       residual=hidden if pending is not None else None)
+            qkv = lw.qkv(h)
+            attn = self._attention(i, qkv, batch)
+            if tp1:
+                lw.o(attn, ops.EPI_RESID, residual=hidden, out=hidden)
+                self._norm(hidden, lw.post_norm, h)
+            else:
+                part = self.tp.all_reduce(lw.o(attn))
+                self._norm(part, lw.post_norm, h, residual=hidden)
+            act = lw.gate_up(h, ops.EPI_SILU)
+            if tp1:
+                lw.down(act, ops.EPI_RESID, residual=hidden, out=hidden)
+                pending = None
+            else:
+                pending = self.tp.all_reduce(lw.down(act))
+        if pending is not None:
+            hidden.copy_((hidden.float() + pending.float()).to(torch.bfloat16)) \
+                if self.device.type != "cuda" else hidden.add_(pending)
+        return hidden
+
+    def _attention(self, li: int, qkv: torch.Tensor, batch: "Batch") -> torch.Tensor:
+        hq, hkv, d = self.hq, self.hkv, self.d
+        kv = self.kv
+        T = qkv.shape[0]
+        if self.device.type == "cuda":
+            ops.rope_kv_write(qkv, batch.positions, self.cos_sin, batch.slots, kv.k, kv.v, li,
+                              hq, hkv, d, self.cfg.rot_dim)
+            out = torch.empty(T, hq * d, dtype=torch.bfloat16, device=self.device)
+            q = qkv[:, :hq * d]
+            if batch.is_decode:
+                ops.attn_decode(q, kv.k, kv.v, batch.block_tables, batch.seq_lens, out, li,
+                                batch.num_splits, batch.blocks_per_split, batch.part_o,
+                                batch.part_ml, self.scale)
+            else:
+                ops.attn_prefill(q, kv.k, kv.v, batch.block_tables, batch.tiles, out, li,
+                                 self.scale)
+            return out
+        # CPU oracle path.
+        x = qkv.float().view(T, hq + 2 * hkv, d)
+        pos = batch.positions.long()
+        q = ref.apply_rope(x[:, :hq], pos, self.cos_sin, self.cfg.rot_dim)
+        k = ref.apply_rope(x[:, hq:hq + hkv], pos, self.cos_sin, self.cfg.rot_dim)
+        v = x[:, hq + hkv:]
+        slots = batch.slots.long()
+        valid = slots >= 0
+        sb, so = slots[valid] // BLOCK_SIZE, slots[valid] % BLOCK_SIZE
+        kv.k[li, sb, :, so] = k[valid].to(torch.bfloat16)
+        kv.v[li, sb, :, so] = v[valid].to(torch.bfloat16)
+        out = torch.empty(T, hq * d, dtype=torch.float32)
+        row = 0
+        for sid, ql in zip(batch.seq_ids, batch.q_lens):
+            kk, vv = kv.gather(li, sid)
+            ctx = int(batch.ctx_len_of(sid))
+            o = ref.attention(q[row:row + ql], kk[:ctx], vv[:ctx], pos[row:row + ql], self.scale)
+            out[row:row + ql] = o.reshape(ql, hq * d)
+            row += ql
+        return out.to(torch.bfloat16)
+
+    def head(self, hidden_last: torch.Tensor) -> torch.Tensor:
+        """Final norm + (vocab-sharded) LM head: bf16 logits [B, V/tp]."""
+        h = torch.empty_like(hidden_last)
+        self._norm(hidden_last, self.final_norm, h)
+        return self.lm_head(h)
+
+    def greedy(self, logits: torch.Tensor) -> torch.Tensor:
+        """Argmax over the full vocabulary (merging vocab shards)."""
+        B = logits.shape[0]
+        if self.device.type != "cuda":
+            return ref.argmax(logits)
+        idx = torch.empty(B, dtype=torch.int32, device=self.device)
+        if self.tp.size == 1 or self.vocab_shard == self.cfg.vocab_size:
+            return ops.argmax(logits, idx)
+        val = torch.empty(B, dtype=torch.float32, device=self.device)
+        ops.argmax(logits, idx, val, idx_offset=self.tp.rank * self.vocab_shard)
+        pair = torch.stack([val, idx.float()], dim=1)  # exact for idx < 2^24
+        allp = self.tp.all_gather_rows(pair)  # [tp, B, 2]
+        best = torch.argmax(allp[:, :, 0], dim=0)  # first (lowest rank) wins ties
+        return allp[best, torch.arange(B, device=self.device), 1].to(torch.int32)
+
+    def full_logits(self, logits: torch.Tensor) -> torch.Tensor:
+        if self.tp.size == 1 or self.vocab_shard == self.cfg.vocab_size:
+            return logits
+        allp = self.tp.all_gather_rows(logits)  # [tp, B, V/tp]
+        return allp.permute(1, 0, 2).reshape(logits.shape[0], -1)
+
+
+@dataclass
+class Batch:
+    """Inputs of one forward of a stage (prefill or decode)."""
+    seq_ids: List[str]
+    q_lens: List[int]
+    ctx_lens: List[int]           # total context after this step, per sequence
+    positions: torch.Tensor       # int32 [T]
+    slots: torch.Tensor           # int32 [T]
+    block_tables: torch.Tensor    # int32 [B, W]
+    seq_lens: torch.Tensor        # int32 [B] (= ctx_lens on device)
+    is_decode: bool
+    tiles: Optional[torch.Tensor] = None
+    num_splits: int = 1
+    blocks_per_split: int = 1
+    part_o: Optional[torch.Tensor] = None
+    part_ml: Optional[torch.Tensor] = None
+
+    def ctx_len_of(self, sid: str) -> int:
+        return self.ctx_lens[self.seq_ids.index(sid)]
+
+    @property
+    def last_rows(self) -> List[int]:
+        out, r = [], 0
+        for ql in self.q_lens:
+            r += ql
+            out.append(r - 1)
+        return out
+
+
+def build_batch(model: LlamaModel, seq_ids: Sequence[str], q_lens: Sequence[int],
+                positions_start: Sequence[int], decode: bool, device=None,
+                width: Optional[int] = None) -> Batch:
+    """Reserve KV for the new tokens and build the device inputs."""
+    kv = model.kv
+    device = device or model.device
+    pos, slots, ctx = [], [], []
+    for sid, ql, p0 in zip(seq_ids, q_lens, positions_start):
+        kv.reserve(sid, p0 + ql)
+        s = kv.seqs[sid]
+        s.length = max(s.length, p0 + ql)
+        pos.extend(range(p0, p0 + ql))
+        slots.extend(s.slots(p0, p0 + ql))
+        ctx.append(p0 + ql)
+    maxb = max((len(kv.seqs[s].blocks) for s in seq_ids), default=1)
+    width = max(width or 0, maxb)
+    b = Batch(seq_ids=list(seq_ids), q_lens=list(q_lens), ctx_lens=ctx,
+              positions=torch.tensor(pos, dtype=torch.int32).to(device),
+              slots=torch.tensor(slots, dtype=torch.int32).to(device),
+              block_tables=kv.block_table(list(seq_ids), width, device),
+              seq_lens=torch.tensor(ctx, dtype=torch.int32).to(device), is_decode=decode)
+    if torch.device(device).type == "cuda":
+        if decode:
+            b.num_splits, b.blocks_per_split = ops.decode_split_plan(len(seq_ids), model.hkv, maxb)
+            g = model.hq // model.hkv
+            n = len(seq_ids) * model.hkv * b.num_splits * g
+            b.part_o = torch.empty(n * model.d, dtype=torch.float32, device=device)
+            b.part_ml = torch.empty(n * 2, dtype=torch.float32, device=device)
+        else:
+            b.tiles = ops.prefill_tiles(q_lens, ctx, device)
+    return b

@@ -1,0 +1,241 @@
+"""Device ops: thin wrappers over the sm_100a kernels in ``cascadia_b200._C``.
+
+Every function takes CUDA tensors and launches one of our own kernels on the
+current stream.  There is no silent fallback: if the extension is missing on a
+machine with a GPU, ``ext()`` raises.  The CPU reference implementations of
+the same math (used by the CPU engine and as test oracles) live in
+:mod:`cascadia_b200.ops.reference` and are only used for CPU tensors.
+"""
+from __future__ import annotations
+
+import math
+import threading
+from typing import Optional
+
+import torch
+
+_EXT = None
+_EXT_ERR: Optional[BaseException] = None
+_LOCK = threading.Lock()
+
+
+def ext():
+    """Return the compiled extension module or raise a clear error."""
+    global _EXT, _EXT_ERR
+    if _EXT is not None:
+        return _EXT
+    with _LOCK:
+        if _EXT is None:
+            try:
+                from cascadia_b200 import _C  # type: ignore
+
+                _EXT = _C
+            except BaseException as e:  # pragma: no cover - depends on build
+                _EXT_ERR = e
+                raise RuntimeError(
+                    "cascadia_b200 CUDA extension is not built; run "
+                    "`python setup.py build_ext --inplace` (sm_100a)") from e
+    return _EXT
+
+
+def ext_available() -> bool:
+    try:
+        ext()
+        return True
+    except RuntimeError:
+        return False
+
+
+# ----------------------------------------------------------------- launch count
+class LaunchCounter:
+    """Counts our own kernel launches issued through this module (e.g. while a
+    CUDA graph is captured, to know how many kernels one replay runs)."""
+
+    def __init__(self):
+        self.count = 0
+        self.active = False
+
+    def reset(self):
+        self.count = 0
+        self.active = False
+
+    def start(self):
+        self.count = 0
+        self.active = True
+
+    def stop(self) -> int:
+        self.active = False
+        return self.count
+
+    def add(self, n: int = 1):
+        if self.active:
+            self.count += n
+
+
+LAUNCHES = LaunchCounter()
+
+
+# ----------------------------------------------------------------- status word
+_STATUS: dict = {}
+
+
+def status_buffer(device: torch.device) -> torch.Tensor:
+    """Per-device int32 status word written by bounded device-side waits."""
+    key = torch.device(device).index or 0
+    buf = _STATUS.get(key)
+    if buf is None:
+        buf = torch.zeros(1, dtype=torch.int32, device=device)
+        _STATUS[key] = buf
+    return buf
+
+
+def read_status(device: torch.device, clear: bool = True) -> int:
+    buf = status_buffer(device)
+    v = int(buf.item())
+    if clear and v != 0:
+        buf.zero_()
+    return v
+
+
+# ----------------------------------------------------------------- GEMM
+EPI_STORE, EPI_SILU, EPI_RESID = 0, 1, 2
+
+
+class GemmWorkspace:
+    """Split-K scratch (fp32 partials + per-tile counters) for one stream.
+
+    The counters return to zero at the end of every GEMM, so a workspace can
+    be reused by any number of back-to-back launches on the same stream (and
+    inside CUDA graphs).  Concurrent streams need their own workspace.
+    """
+
+    def __init__(self, device, max_floats: int = 1 << 24, max_counters: int = 1 << 16):
+        self.device = torch.device(device)
+        self.ws = torch.empty(max(1, max_floats), dtype=torch.float32, device=self.device)
+        self.counters = torch.zeros(max_counters, dtype=torch.int32, device=self.device)
+        # Buffers replaced by a larger one stay alive: a captured CUDA graph
+        # may still point at them.
+        self._retired = []
+
+    def ensure(self, floats: int, counters: int):
+        if floats > self.ws.numel():
+            self._retired.append(self.ws)
+            self.ws = torch.empty(floats, dtype=torch.float32, device=self.device)
+        if counters > self.counters.numel():
+            self._retired.append(self.counters)
+            self.counters = torch.zeros(counters, dtype=torch.int32, device=self.device)
+
+
+_WS: dict = {}
+
+
+def default_workspace(device) -> GemmWorkspace:
+    key = (torch.device(device).index or 0, torch.cuda.current_stream(device).cuda_stream)
+    ws = _WS.get(key)
+    if ws is None:
+        ws = GemmWorkspace(device)
+        _WS[key] = ws
+    return ws
+
+
+def w4a16_gemm(x: torch.Tensor, blob: torch.Tensor, n: int, group_size: int = 128,
+               epilogue: int = EPI_STORE, residual: Optional[torch.Tensor] = None,
+               out: Optional[torch.Tensor] = None, workspace: Optional[GemmWorkspace] = None,
+               splits: int = 0) -> torch.Tensor:
+    """Y = X @ dequant(W)^T with a fused epilogue, on tcgen05 tensor cores."""
+    m, k = x.shape
+    e = ext()
+    n_out = n // 2 if epilogue == EPI_SILU else n
+    if out is None:
+        out = torch.empty(m, n_out, dtype=torch.bfloat16, device=x.device)
+    ws = workspace or default_workspace(x.device)
+    ws.ensure(e.w4a16_workspace_floats(m, n, k, splits), e.w4a16_counter_count(m, n))
+    e.w4a16_gemm(x, blob, out, n, group_size, epilogue, residual, ws.ws, ws.counters,
+                 status_buffer(x.device), splits)
+    LAUNCHES.add(1)
+    return out
+
+
+def w4a16_plan(m: int, n: int, k: int, splits: int = 0):
+    return ext().w4a16_plan(m, n, k, splits)
+
+
+# ----------------------------------------------------------------- attention
+def attn_decode(q, k_cache, v_cache, block_tables, seq_lens, out, layer: int, num_splits: int,
+                blocks_per_split: int, part_o, part_ml, scale: float):
+    ext().attn_decode(q, k_cache, v_cache, block_tables, seq_lens, out, layer, num_splits,
+                      blocks_per_split, part_o, part_ml, scale, status_buffer(q.device))
+    LAUNCHES.add(2 if num_splits > 1 else 1)
+    return out
+
+
+def attn_prefill(q, k_cache, v_cache, block_tables, tiles, out, layer: int, scale: float):
+    ext().attn_prefill(q, k_cache, v_cache, block_tables, tiles, out, layer, scale,
+                       status_buffer(q.device))
+    LAUNCHES.add(1)
+    return out
+
+
+def decode_split_plan(batch: int, kv_heads: int, max_blocks: int, num_sms: int = 148):
+    """Split the context so batch*kv_heads*splits fills about two waves of SMs."""
+    pairs = max(1, batch * kv_heads)
+    want = max(1, math.ceil(2 * num_sms / pairs))
+    splits = max(1, min(want, max(1, max_blocks // 4)))
+    bps = max(1, math.ceil(max_blocks / splits))
+    splits = max(1, math.ceil(max_blocks / bps))
+    return splits, bps
+
+
+def prefill_tiles(q_lens, ctx_lens, device) -> torch.Tensor:
+    """Per 64-row query tile: (seq, first packed row, first position, rows)."""
+    tiles = []
+    row = 0
+    for b, (ql, cl) in enumerate(zip(q_lens, ctx_lens)):
+        start_pos = cl - ql
+        for t0 in range(0, ql, 64):
+            tiles.append((b, row + t0, start_pos + t0, min(64, ql - t0)))
+        row += ql
+    # Longest (most KV) tiles first: better tail behaviour for causal work.
+    tiles.sort(key=lambda t: -(t[2] + t[3]))
+    if not tiles:
+        return torch.zeros(0, 4, dtype=torch.int32, device=device)
+    return torch.tensor(tiles, dtype=torch.int32, device=device)
+
+
+# ----------------------------------------------------------------- small ops
+def embedding(ids, table, out, vocab_lo: int = 0):
+    ext().embedding(ids, table, out, vocab_lo)
+    LAUNCHES.add(1)
+    return out
+
+
+def rmsnorm(x, w, out, eps: float, residual=None):
+    """out = rmsnorm(x + residual) * w; residual (if given) is updated in place."""
+    ext().rmsnorm(x, residual, w, out, eps)
+    LAUNCHES.add(1)
+    return out
+
+
+def rope_kv_write(qkv, positions, cos_sin, slots, k_cache, v_cache, layer, hq, hkv, d, rot,
+                  interleaved=False):
+    ext().rope_kv_write(qkv, positions, cos_sin, slots, k_cache, v_cache, layer, hq, hkv, d, rot,
+                        interleaved)
+    LAUNCHES.add(1)
+
+
+def argmax(logits, out_idx, out_val=None, idx_offset: int = 0):
+    ext().argmax(logits, out_idx, out_val, idx_offset)
+    LAUNCHES.add(1)
+    return out_idx
+
+
+def sample(logits, params, history, hist_len, work, seeds, offsets, out):
+    ext().sample(logits, params, history, hist_len, work, seeds, offsets, out)
+    LAUNCHES.add(1)
+    return out
+
+
+def spec_verify(target, draft, out):
+    ext().spec_verify(target, draft, out)
+    LAUNCHES.add(1)
+    return out

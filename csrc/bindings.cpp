@@ -1,0 +1,52 @@
+// Python bindings of the cascadia_b200 sm_100a kernels (module `_C`).
+#include <torch/extension.h>
+
+#include <vector>
+
+namespace cb {
+// gemm_w4a16.cu
+void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t N,
+                int64_t group_size, int64_t epilogue, c10::optional<torch::Tensor> residual,
+                torch::Tensor ws, torch::Tensor counters, torch::Tensor status,
+                int64_t forced_splits);
+int64_t w4a16_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t forced_splits);
+int64_t w4a16_counter_count(int64_t M, int64_t N);
+std::vector<int64_t> w4a16_plan(int64_t M, int64_t N, int64_t K, int64_t forced_splits);
+// attention.cu
+void attn_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                 torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
+                 int64_t layer, int64_t num_splits, int64_t blocks_per_split,
+                 torch::Tensor part_o, torch::Tensor part_ml, double scale, torch::Tensor status);
+void attn_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                  torch::Tensor block_tables, torch::Tensor tiles, torch::Tensor out, int64_t layer,
+                  double scale, torch::Tensor status);
+// elementwise.cu
+void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t vocab_lo);
+void rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tensor w,
+             torch::Tensor out, double eps);
+void rope_kv_write(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin,
+                   torch::Tensor slots, torch::Tensor k_cache, torch::Tensor v_cache, int64_t layer,
+                   int64_t Hq, int64_t Hkv, int64_t D, int64_t rot, bool interleaved);
+void argmax(torch::Tensor logits, torch::Tensor out_idx, c10::optional<torch::Tensor> out_val,
+            int64_t idx_offset);
+void sample(torch::Tensor logits, torch::Tensor params, c10::optional<torch::Tensor> history,
+            c10::optional<torch::Tensor> hist_len, torch::Tensor work, torch::Tensor seeds,
+            torch::Tensor offsets, torch::Tensor out);
+void spec_verify(torch::Tensor target, torch::Tensor draft, torch::Tensor out);
+}  // namespace cb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "cascadia_b200 sm_100a kernels";
+  m.def("w4a16_gemm", &cb::w4a16_gemm);
+  m.def("w4a16_workspace_floats", &cb::w4a16_workspace_floats);
+  m.def("w4a16_counter_count", &cb::w4a16_counter_count);
+  m.def("w4a16_plan", &cb::w4a16_plan);
+  m.def("attn_decode", &cb::attn_decode);
+  m.def("attn_prefill", &cb::attn_prefill);
+  m.def("embedding", &cb::embedding);
+  m.def("rmsnorm", &cb::rmsnorm);
+  m.def("rope_kv_write", &cb::rope_kv_write);
+  m.def("argmax", &cb::argmax);
+  m.def("sample", &cb::sample);
+  m.def("spec_verify", &cb::spec_verify);
+}

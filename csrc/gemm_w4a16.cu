@@ -1,0 +1,505 @@
+// W4A16 GEMM for sm_100a: Y[M, N] = X[M, K] (bf16) * dequant(W[N, K])^T.
+//
+// W is symmetric INT4 with one bf16 scale per `GS` (128 or 32) consecutive
+// K values of a row: value = (q - 8) * scale.  This is the weight format of
+// the reference's `cascadia shard` INT4_SYM group-128 layers
+// (tools/export_shards.py:1432-1438, crates/cascadia-ov-genai-shim/cpp/gemv_offload.cpp:1-8)
+// and of its group-32 expert files (crates/cascadia-int4-gemm/src/kernel.rs:46-70).
+//
+// Design (swap-AB, tcgen05):
+//   * The MMA computes D^T[128 weight rows, MT tokens] = W_tile * X_tile^T with
+//     the dequantised weight tile as operand A (M=128) and the activations as
+//     operand B (N=MT in 16..256), so decode batches of 1..64 tokens map onto
+//     narrow N instead of wasting a 128-row M.
+//   * Weights live in a pre-tiled "blob" layout: for each (128-row tile,
+//     128-wide k-block) one contiguous 8 KiB block of packed nibbles followed by
+//     its scales, fetched with one cp.async.bulk.  Activations are fetched with
+//     a 2-D TMA tensor map (128-byte swizzle) straight into the UMMA layout.
+//   * Warp roles: warp 0 issues TMA, warp 1 owns TMEM and issues tcgen05.mma,
+//     warps 2..9 dequantise nibbles into the 128B-swizzled bf16 A tile and
+//     later run the epilogue (tcgen05.ld from TMEM).
+//   * Split-K over k-blocks fills the 148 SMs for decode shapes.  Partials go
+//     to an fp32 workspace; the last CTA of a tile (per-tile counter) sums the
+//     splits in a fixed order, so results are deterministic run to run.
+//   * Fused epilogues: plain store, SiLU(gate)*up for interleaved gate/up tiles,
+//     and residual add.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "host_utils.h"
+
+namespace cb {
+
+enum Epilogue : int { kEpiStore = 0, kEpiSilu = 1, kEpiResid = 2 };
+
+constexpr int kThreads = 320;  // 10 warps
+constexpr int kDequantThreads = 256;
+constexpr int kABytes = 128 * 128 * 2;  // one dequantised 128x128 bf16 tile
+
+template <int GS>
+struct BlobInfo {
+  static constexpr int kPacked = 128 * 64;                 // 128 rows x 128 nibbles
+  static constexpr int kScales = 128 * (128 / GS) * 2;     // bf16
+  static constexpr int kBytes = kPacked + kScales;
+};
+
+template <int MT>
+struct Stages {
+  static constexpr int value = MT <= 16 ? 8 : MT <= 32 ? 8 : MT <= 64 ? 6 : MT <= 128 ? 3 : 2;
+};
+
+template <int MT, int GS>
+struct SmemPlan {
+  static constexpr int kXBytes = 2 * MT * 128;  // two 64-wide K sub-tiles
+  static constexpr int kStageRaw = kXBytes + BlobInfo<GS>::kBytes;
+  static constexpr int kStage = (kStageRaw + 1023) / 1024 * 1024;
+  static constexpr int kSL = Stages<MT>::value;
+  static constexpr int kAOff = 0;
+  static constexpr int kLOff = 2 * kABytes;
+  static constexpr int kBarOff = kLOff + kSL * kStage;
+  static constexpr int kTileBytes = 128 * (MT + 1) * 4;
+  static_assert(kTileBytes <= kBarOff, "epilogue tile must fit in the stage area");
+  static constexpr int kTotal = kBarOff + 1024 + 1024;  // barriers + alignment slack
+};
+
+struct GemmArgs {
+  const uint8_t* wblob;
+  __nv_bfloat16* out;
+  const __nv_bfloat16* residual;
+  float* ws;
+  int* counters;
+  int* status;
+  int M, N, K;
+  int ldo, ldr;
+  int kb_per_split, splits;
+};
+
+template <int MT, int GS, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    w4a16_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs args) {
+  using Plan = SmemPlan<MT, GS>;
+  constexpr int SL = Plan::kSL;
+  constexpr int BLOB = BlobInfo<GS>::kBytes;
+  constexpr uint32_t kTmemCols = MT < 32 ? 32 : MT;
+  constexpr uint32_t kIdesc = umma_idesc_bf16(128, MT);
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // Align the dynamic smem base to 1024 bytes (128B-swizzle atoms).
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* a_smem = smem + Plan::kAOff;
+  uint8_t* l_smem = smem + Plan::kLOff;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Plan::kBarOff);
+  uint64_t* full_l = bars;
+  uint64_t* empty_l = bars + SL;
+  uint64_t* full_a = bars + 2 * SL;
+  uint64_t* empty_a = bars + 2 * SL + 2;
+  uint64_t* acc_full = bars + 2 * SL + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * SL + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* is_last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  float* tile = reinterpret_cast<float*>(smem);  // reused after the main loop
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int rt = blockIdx.x;     // 128-row weight tile
+  const int split = blockIdx.y;  // k split
+  const int tt = blockIdx.z;     // token tile
+  const int KB = args.K / 128;
+  const int kb0 = split * args.kb_per_split;
+  const int kb1 = min(KB, kb0 + args.kb_per_split);
+  const int nkb = kb1 - kb0;
+
+  if (tid == 0) {
+    for (int s = 0; s < SL; ++s) {
+      mbar_init(&full_l[s], 1);
+      mbar_init(&empty_l[s], 8 + 1);  // 8 dequant warps + MMA commit
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&full_a[a], 8);
+      mbar_init(&empty_a[a], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    *is_last_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tmap_x);
+      const uint8_t* wsrc = args.wblob + ((size_t)rt * KB + kb0) * BLOB;
+      int issued = 0;
+      for (int it = 0; it < nkb; ++it) {
+        const int s = it % SL;
+        const uint32_t ph = (it / SL) & 1;
+        if (!mbar_wait(&empty_l[s], ph ^ 1, args.status, kStatusGemmLoadTimeout, abort_flag)) break;
+        uint8_t* st = l_smem + s * Plan::kStage;
+        mbar_arrive_expect_tx(&full_l[s], Plan::kXBytes + BLOB);
+        bulk_g2s(st + Plan::kXBytes, wsrc + (size_t)it * BLOB, BLOB, &full_l[s]);
+        const int k = (kb0 + it) * 128;
+        tma_load_2d(st, &tmap_x, k, tt * MT, &full_l[s]);
+        tma_load_2d(st + MT * 128, &tmap_x, k + 64, tt * MT, &full_l[s]);
+        ++issued;
+      }
+      // Drain: never leave the CTA while our copies still write into smem.
+      for (int it = max(0, issued - SL); it < issued; ++it) {
+        mbar_wait(&full_l[it % SL], (it / SL) & 1, nullptr, 0, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      for (int it = 0; it < nkb; ++it) {
+        const int s = it % SL;
+        const uint32_t phl = (it / SL) & 1;
+        const int a = it & 1;
+        const uint32_t pha = (it >> 1) & 1;
+        if (!mbar_wait(&full_a[a], pha, args.status, kStatusGemmMmaTimeout, abort_flag)) break;
+        if (!mbar_wait(&full_l[s], phl, args.status, kStatusGemmMmaTimeout, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(a_smem + a * kABytes);
+        const uint32_t x_addr = smem_u32(l_smem + s * Plan::kStage);
+#pragma unroll
+        for (int sub = 0; sub < 2; ++sub) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t da = umma_desc_sw128(a_addr + sub * (128 * 128) + kk * 32);
+            const uint64_t db = umma_desc_sw128(x_addr + sub * (MT * 128) + kk * 32);
+            mma_bf16_ss(tmem_base, da, db, kIdesc, (it > 0 || sub > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        mma_commit(&empty_a[a]);
+        mma_commit(&empty_l[s]);
+      }
+      mma_commit(acc_full);
+    }
+  } else {
+    // ------------------------------------------------------------ dequant
+    const int t = tid - 64;
+    const int c = t & 3;
+    const __nv_bfloat162 k136 = __floats2bfloat162_rn(136.0f, 136.0f);
+    bool ok = true;
+    for (int it = 0; it < nkb && ok; ++it) {
+      const int s = it % SL;
+      const uint32_t phl = (it / SL) & 1;
+      const int a = it & 1;
+      const uint32_t pha = (it >> 1) & 1;
+      if (!mbar_wait(&full_l[s], phl, args.status, kStatusGemmDequantTimeout, abort_flag)) {
+        ok = false;
+        break;
+      }
+      if (!mbar_wait(&empty_a[a], pha ^ 1, args.status, kStatusGemmDequantTimeout, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* wb = l_smem + s * Plan::kStage + Plan::kXBytes;
+      const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(wb + BlobInfo<GS>::kPacked);
+      uint8_t* ab = a_smem + a * kABytes;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int r = (t >> 2) + 64 * j;
+        const uint4 p = *reinterpret_cast<const uint4*>(wb + r * 64 + c * 16);
+        const uint32_t words[4] = {p.x, p.y, p.z, p.w};
+        const __nv_bfloat16 sv = (GS == 128) ? sc[r] : sc[r * (128 / GS) + (c * 32) / GS];
+        const __nv_bfloat162 s2 = __halves2bfloat162(sv, sv);
+        uint8_t* rowp = ab + (c >> 1) * (128 * 128) + r * 128;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int wi = (i + c) & 3;  // rotation keeps the 16B stores bank-conflict free
+          const uint32_t w = words[wi];
+          uint32_t o[4];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            uint32_t v = ((w >> (4 * h)) & 0x000F000Fu) | 0x43004300u;  // bf16 (128 + q)
+            __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
+            b = __hmul2(__hsub2(b, k136), s2);                         // (q - 8) * scale
+            o[h] = *reinterpret_cast<uint32_t*>(&b);
+          }
+          const int chunk = (((c & 1) * 4 + wi) ^ (r & 7));
+          *reinterpret_cast<uint4*>(rowp + chunk * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&full_a[a]);
+        mbar_arrive(&empty_l[s]);
+      }
+    }
+
+    // ------------------------------------------------------------ epilogue
+    const bool have_acc =
+        ok && nkb > 0 && mbar_wait(acc_full, 0, args.status, kStatusGemmEpiTimeout, abort_flag);
+    const int q = warp & 3;               // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;     // which half of the MT columns
+    const int row = q * 32 + lane;        // weight row inside the tile
+    const int n0 = rt * 128;
+    const int m_base = tt * MT;
+    const int Mpad = gridDim.z * MT;
+    constexpr int HALF = MT / 2;
+    tc_fence_after();
+
+    // Phase 1: TMEM -> (workspace | smem tile).  Each thread owns one row.
+    float* dst_ws = args.ws;
+    if (have_acc) {
+      const uint32_t lane_addr = tmem_base + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+      for (int c0 = half * HALF; c0 < (half + 1) * HALF; c0 += (HALF >= 16 ? 16 : 8)) {
+        float v[16];
+        if constexpr (HALF >= 16) {
+          tmem_ld16(lane_addr + c0, v);
+        } else {
+          float v8[8];
+          tmem_ld8(lane_addr + c0, v8);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = v8[i];
+        }
+        constexpr int CW = HALF >= 16 ? 16 : 8;
+        if (args.splits == 1) {
+#pragma unroll
+          for (int i = 0; i < CW; ++i) tile[row * (MT + 1) + c0 + i] = v[i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < CW; ++i)
+            dst_ws[((size_t)split * Mpad + m_base + c0 + i) * args.N + n0 + row] = v[i];
+        }
+      }
+    }
+    tc_fence_before();
+    named_bar_sync(1, kDequantThreads);
+    if (!have_acc && args.splits == 1) {
+      // Nothing to write (error path); leave outputs untouched.
+    } else {
+      bool do_final = true;
+      if (args.splits > 1) {
+        __threadfence();
+        named_bar_sync(1, kDequantThreads);
+        if (t == 0) {
+          const int tile_id = tt * gridDim.x + rt;
+          const int old = atomicAdd(&args.counters[tile_id], 1);
+          const int last = (old == args.splits - 1) ? 1 : 0;
+          if (last) args.counters[tile_id] = 0;  // ready for the next launch
+          *is_last_flag = last;
+        }
+        named_bar_sync(1, kDequantThreads);
+        do_final = *is_last_flag != 0;
+        if (do_final) {
+          __threadfence();
+          for (int idx = t; idx < 128 * MT; idx += kDequantThreads) {
+            const int r = idx & 127;
+            const int m = idx >> 7;
+            float acc = 0.f;
+            for (int sp = 0; sp < args.splits; ++sp)
+              acc += __ldcg(&dst_ws[((size_t)sp * Mpad + m_base + m) * args.N + n0 + r]);
+            tile[r * (MT + 1) + m] = acc;
+          }
+          named_bar_sync(1, kDequantThreads);
+        }
+      }
+      // Phase 2: smem tile -> global with the fused epilogue.
+      if (do_final) {
+        if constexpr (EPI == kEpiSilu) {
+          for (int idx = t; idx < 64 * MT; idx += kDequantThreads) {
+            const int j = idx & 63;
+            const int m = idx >> 6;
+            const int gm = m_base + m;
+            if (gm < args.M) {
+              const float g = tile[j * (MT + 1) + m];
+              const float u = tile[(64 + j) * (MT + 1) + m];
+              const float y = g / (1.f + __expf(-g)) * u;
+              args.out[(size_t)gm * args.ldo + rt * 64 + j] = __float2bfloat16(y);
+            }
+          }
+        } else {
+          for (int idx = t; idx < 128 * MT; idx += kDequantThreads) {
+            const int r = idx & 127;
+            const int m = idx >> 7;
+            const int gm = m_base + m;
+            if (gm < args.M) {
+              float y = tile[r * (MT + 1) + m];
+              if constexpr (EPI == kEpiResid)
+                y += __bfloat162float(args.residual[(size_t)gm * args.ldr + n0 + r]);
+              args.out[(size_t)gm * args.ldo + n0 + r] = __float2bfloat16(y);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+template <int MT, int GS, int EPI>
+void launch_w4a16(const CUtensorMap& tmap, const GemmArgs& a, dim3 grid, cudaStream_t stream) {
+  using Plan = SmemPlan<MT, GS>;
+  static bool configured = false;  // per instantiation; attribute is per-function
+  if (!configured) {
+    CB_CUDA_CHECK(cudaFuncSetAttribute(w4a16_gemm_kernel<MT, GS, EPI>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, Plan::kTotal));
+    configured = true;
+  }
+  w4a16_gemm_kernel<MT, GS, EPI><<<grid, kThreads, Plan::kTotal, stream>>>(tmap, a);
+  CB_CUDA_CHECK(cudaGetLastError());
+}
+
+template <int GS, int EPI>
+void dispatch_mt(int MT, const CUtensorMap& tmap, const GemmArgs& a, dim3 grid, cudaStream_t s) {
+  switch (MT) {
+    case 16: launch_w4a16<16, GS, EPI>(tmap, a, grid, s); break;
+    case 32: launch_w4a16<32, GS, EPI>(tmap, a, grid, s); break;
+    case 64: launch_w4a16<64, GS, EPI>(tmap, a, grid, s); break;
+    case 128: launch_w4a16<128, GS, EPI>(tmap, a, grid, s); break;
+    default: launch_w4a16<256, GS, EPI>(tmap, a, grid, s); break;
+  }
+}
+
+static int pick_mt(int M) {
+  if (M <= 16) return 16;
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128) return 128;
+  return 256;
+}
+
+// Number of k-splits: fill the SMs with whole waves of CTAs while keeping at
+// least 4 k-blocks per CTA so the pipeline has something to overlap.
+static int pick_splits(int tiles, int KB, int num_sms) {
+  if (tiles >= num_sms) return 1;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int s = 1; s <= KB; ++s) {
+    const int kbps = (KB + s - 1) / s;
+    if (kbps < 4 && s > 1) break;
+    const int real_s = (KB + kbps - 1) / kbps;
+    const long ctas = (long)tiles * real_s;
+    const long waves = (ctas + num_sms - 1) / num_sms;
+    const double eff = (double)ctas / (double)(waves * num_sms);
+    // Prefer more parallelism when efficiency ties (more bytes in flight).
+    if (eff > best_eff + 1e-9 || (std::abs(eff - best_eff) < 1e-9 && waves == 1)) {
+      best_eff = eff;
+      best = real_s;
+    }
+    if (waves > 1 && eff < best_eff) break;
+  }
+  return best;
+}
+
+struct GemmPlanInfo {
+  int MT, splits, kbps, token_tiles, row_tiles;
+};
+
+static GemmPlanInfo plan_gemm(int M, int N, int K, int forced_splits) {
+  GemmPlanInfo p;
+  p.MT = pick_mt(M);
+  p.token_tiles = (M + p.MT - 1) / p.MT;
+  p.row_tiles = N / 128;
+  const int KB = K / 128;
+  int splits = forced_splits > 0 ? forced_splits
+                                  : pick_splits(p.row_tiles * p.token_tiles, KB, num_sms());
+  splits = std::max(1, std::min(splits, KB));
+  p.kbps = (KB + splits - 1) / splits;
+  p.splits = (KB + p.kbps - 1) / p.kbps;
+  return p;
+}
+
+// Workspace floats needed for a GEMM of this shape (0 when no split).
+int64_t w4a16_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t forced_splits) {
+  GemmPlanInfo p = plan_gemm((int)M, (int)N, (int)K, (int)forced_splits);
+  if (p.splits == 1) return 0;
+  return (int64_t)p.splits * p.token_tiles * p.MT * N;
+}
+
+int64_t w4a16_counter_count(int64_t M, int64_t N) {
+  const int MT = pick_mt((int)M);
+  return (int64_t)((M + MT - 1) / MT) * (N / 128);
+}
+
+// x: [M, K] bf16 (row stride K).  wblob: uint8 blob.  out: [M, ldo] bf16.
+// epilogue: 0 store, 1 silu(gate)*up (out has N/2 columns), 2 residual add.
+void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t N,
+                int64_t group_size, int64_t epilogue, c10::optional<torch::Tensor> residual,
+                torch::Tensor ws, torch::Tensor counters, torch::Tensor status,
+                int64_t forced_splits) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16, "x must be cuda bf16");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be 2-D with unit inner stride");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1, "out must be bf16");
+  const int M = (int)x.size(0);
+  const int K = (int)x.size(1);
+  TORCH_CHECK(K % 128 == 0 && N % 128 == 0, "K and N must be multiples of 128");
+  TORCH_CHECK(group_size == 128 || group_size == 32, "group size must be 128 or 32");
+  TORCH_CHECK((x.stride(0) * 2) % 16 == 0, "x row stride must be 16-byte aligned");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "x must be 16-byte aligned");
+  const int64_t blob_bytes =
+      (int64_t)(N / 128) * (K / 128) * (8192 + 128 * (128 / group_size) * 2);
+  TORCH_CHECK(wblob.numel() == blob_bytes, "weight blob has wrong size");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(x.device());
+  GemmPlanInfo p = plan_gemm(M, (int)N, K, (int)forced_splits);
+  if (p.splits > 1) {
+    TORCH_CHECK(ws.numel() >= (int64_t)p.splits * p.token_tiles * p.MT * N, "workspace too small");
+    TORCH_CHECK(counters.numel() >= (int64_t)p.token_tiles * p.row_tiles, "counters too small");
+  }
+  GemmArgs a;
+  a.wblob = wblob.data_ptr<uint8_t>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.residual = residual.has_value()
+                   ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr())
+                   : nullptr;
+  a.ldr = residual.has_value() ? (int)residual->stride(0) : 0;
+  a.ws = p.splits > 1 ? ws.data_ptr<float>() : nullptr;
+  a.counters = p.splits > 1 ? counters.data_ptr<int>() : nullptr;
+  a.status = status.data_ptr<int>();
+  a.M = M;
+  a.N = (int)N;
+  a.K = K;
+  a.ldo = (int)out.stride(0);
+  a.kb_per_split = p.kbps;
+  a.splits = p.splits;
+  TORCH_CHECK(epilogue != kEpiResid || residual.has_value(), "residual epilogue needs residual");
+
+  CUtensorMap tmap = make_tmap_2d_bf16(x.data_ptr(), (uint64_t)K, (uint64_t)M,
+                                       (uint64_t)x.stride(0) * 2, 64, (uint32_t)p.MT,
+                                       CU_TENSOR_MAP_SWIZZLE_128B);
+  dim3 grid(p.row_tiles, p.splits, p.token_tiles);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (group_size == 128) {
+    if (epilogue == kEpiStore) dispatch_mt<128, kEpiStore>(p.MT, tmap, a, grid, stream);
+    else if (epilogue == kEpiSilu) dispatch_mt<128, kEpiSilu>(p.MT, tmap, a, grid, stream);
+    else dispatch_mt<128, kEpiResid>(p.MT, tmap, a, grid, stream);
+  } else {
+    if (epilogue == kEpiStore) dispatch_mt<32, kEpiStore>(p.MT, tmap, a, grid, stream);
+    else if (epilogue == kEpiSilu) dispatch_mt<32, kEpiSilu>(p.MT, tmap, a, grid, stream);
+    else dispatch_mt<32, kEpiResid>(p.MT, tmap, a, grid, stream);
+  }
+}
+
+std::vector<int64_t> w4a16_plan(int64_t M, int64_t N, int64_t K, int64_t forced_splits) {
+  GemmPlanInfo p = plan_gemm((int)M, (int)N, (int)K, (int)forced_splits);
+  return {p.MT, p.splits, p.kbps, p.token_tiles, p.row_tiles};
+}
+
+}  // namespace cb

@@ -1,0 +1,73 @@
+// Host-side helpers shared by the cascadia_b200 extension sources.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+#define CB_CUDA_CHECK(expr)                                                              \
+  do {                                                                                   \
+    cudaError_t _e = (expr);                                                             \
+    if (_e != cudaSuccess) {                                                             \
+      throw std::runtime_error(std::string("CUDA error: ") + cudaGetErrorString(_e) +   \
+                               " at " + __FILE__ + ":" + std::to_string(__LINE__));     \
+    }                                                                                    \
+  } while (0)
+
+namespace cb {
+
+inline int num_sms() {
+  static int n = [] {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v > 0 ? v : 148;
+  }();
+  return n;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point, so the
+// extension does not link libcuda directly.
+inline EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    CB_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    if (p == nullptr || q != cudaDriverEntryPointSuccess)
+      throw std::runtime_error("cuTensorMapEncodeTiled unavailable");
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// 2-D bf16 tensor map: inner dimension `inner` (elements), outer `outer` rows,
+// row pitch `row_bytes`; box {box_inner, box_outer}.
+inline CUtensorMap make_tmap_2d_bf16(void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                                     uint32_t box_inner, uint32_t box_outer,
+                                     CUtensorMapSwizzle swizzle) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    throw std::runtime_error("cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+  }
+  return m;
+}
+
+}  // namespace cb
