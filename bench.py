@@ -145,7 +145,7 @@ def main():
     torch.cuda.synchronize()
     load_s = time.time() - t0
     B, P = args.batch, args.prompt_len
-    total_len = P + args.warmup + args.steps + 2
+    total_len = P + args.warmup + 2 * args.steps + 4
     width = -(-total_len // BLOCK_SIZE)
     model.allocate_kv(B * width + 16 + width * (args.ttft_reps + 1))
     gen = BatchGenerator(model, use_graph=not args.no_graph)

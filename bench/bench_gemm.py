@@ -1,0 +1,84 @@
+"""W4A16 GEMM microbenchmark on the Llama-3.1-8B layer shapes.
+
+    python bench/bench_gemm.py [--m 64] [--shapes qkv,o,gate_up,down,lm_head] [--reps 20]
+
+Times each GEMM with CUDA events (after warm-up; the weight set of all shapes
+rotates so each launch reads its weights from HBM, not L2) and reports
+achieved HBM bandwidth of the weight stream against MEASURED_PEAKS.json.
+``--reps 1 --shapes gate_up`` gives a single launch for an ncu capture.
+"""
+import argparse
+import json
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+import torch  # noqa: E402
+
+from cascadia_b200 import ops  # noqa: E402
+from cascadia_b200.quant import Int4Weight, blob_bytes  # noqa: E402
+
+SHAPES = {  # name: (N, K, epilogue)
+    "qkv": (6144, 4096, ops.EPI_STORE),
+    "o": (4096, 4096, ops.EPI_RESID),
+    "gate_up": (28672, 4096, ops.EPI_SILU),
+    "down": (4096, 14336, ops.EPI_RESID),
+    "lm_head": (128256, 4096, ops.EPI_STORE),
+}
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--m", type=int, default=64)
+    p.add_argument("--shapes", default="qkv,o,gate_up,down,lm_head")
+    p.add_argument("--reps", type=int, default=20)
+    p.add_argument("--copies", type=int, default=4, help="weight copies rotated per shape")
+    p.add_argument("--splits", type=int, default=0)
+    a = p.parse_args()
+    dev = torch.device("cuda", 0)
+    peak = 6543.4
+    pk = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                      "MEASURED_PEAKS.json")
+    if os.path.exists(pk):
+        peak = json.load(open(pk)).get("hbm_gbs", peak)
+    res = {}
+    for name in a.shapes.split(","):
+        n, k, epi = SHAPES[name]
+        g = torch.Generator(device=dev).manual_seed(0)
+        copies = a.copies if a.reps > 1 else 1
+        blobs = [Int4Weight.random(n, k, generator=g, device=dev).blob(epi == ops.EPI_SILU)
+                 for _ in range(copies)]
+        x = torch.randn(a.m, k, device=dev).to(torch.bfloat16)
+        resid = torch.randn(a.m, n, device=dev).to(torch.bfloat16)
+        outs = torch.empty(a.m, n, dtype=torch.bfloat16, device=dev)
+
+        def run(i):
+            kw = {}
+            if epi == ops.EPI_RESID:
+                kw = dict(residual=resid, out=outs)
+            return ops.w4a16_gemm(x, blobs[i % copies], n, 128, epi, splits=a.splits, **kw)
+
+        for i in range(min(3, a.reps)):
+            run(i)
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(a.reps)]
+        for i in range(a.reps):
+            ev[i][0].record()
+            run(i)
+            ev[i][1].record()
+        torch.cuda.synchronize()
+        ts = sorted(s.elapsed_time(e) * 1000 for s, e in ev)
+        med = ts[len(ts) // 2]
+        nbytes = blob_bytes(n, k, 128) + a.m * k * 2 + a.m * n * 2
+        plan = ops.w4a16_plan(a.m, n, k, a.splits)
+        res[name] = {"us": round(med, 2), "GBps": round(nbytes / med / 1e3, 1),
+                     "frac_of_measured_hbm": round(nbytes / med / 1e3 / peak, 3),
+                     "plan[MT,splits,kbps,tt,rt]": plan}
+        print(name, json.dumps(res[name]), flush=True)
+    print("status", ops.read_status(dev))
+
+
+if __name__ == "__main__":
+    main()

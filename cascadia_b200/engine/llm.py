@@ -1,0 +1,365 @@
+"""The dense GPU serving engine (Llama-family INT4), single stage.
+
+This is the B200 counterpart of the reference's ``ov-runtime`` /
+``ov-genai --cb`` engines (crates/cascadia-engine-openvino/src/runtime.rs,
+genai.rs:597-915): one ``step()`` = one continuous-batching iteration:
+
+1. admit waiting requests and run one chunked-prefill pass (packed ragged
+   prompts, paged KV, prefix-cache hits skipped);
+2. run one decode step for every running sequence through a captured CUDA
+   graph (batch padded to a bucket: padded rows write no KV);
+3. pick tokens on device (greedy argmax in the graph, or the sampling kernel
+   for rows with temperature > 0), detokenize incrementally, finish on EOS /
+   ``max_tokens``, free KV.
+
+Chunks follow the reference conventions: one token chunk per generated token,
+``prompt_tokens`` on the final chunk, ``finish_reason`` stop/length.
+"""
+from __future__ import annotations
+
+import logging
+import math
+import time
+from typing import Dict, Iterable, List, Optional
+
+import numpy as np
+import torch
+
+from .. import metrics, ops
+from ..api.templates import ByteTokenizer, IncrementalDecoder
+from ..models.llama import build_batch
+from ..ops import reference as ref
+from ..runtime.generator import DecodeGraph
+from ..runtime.kv_cache import BLOCK_SIZE
+from ..runtime.scheduler import PrefixCache, SchedulerState, Sequence
+from ..types import Chunk, FinishReason, GenerationTask, LoadProgress, PeerLayout, ShardSpec
+from .base import Builder, Engine, EngineError, InvalidConfig, NotLoaded, PromptTooLong, QueueFull
+
+log = logging.getLogger("cascadia.engine")
+
+BATCH_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256)
+
+
+def _bucket(n: int, buckets=BATCH_BUCKETS) -> int:
+    for b in buckets:
+        if n <= b:
+            return b
+    return n
+
+
+class LLMEngine(Engine):
+    def __init__(self, model, tokenizer=None, max_running: int = 64,
+                 max_prefill_tokens: int = 8192, max_model_len: int = 8192,
+                 use_graph: bool = True, prefix_cache_blocks: int = 0, model_id: str = "llm",
+                 max_queue: int = 1024):
+        self.model = model
+        self.dev = model.device
+        self.cfg = model.cfg
+        self.tok = tokenizer or ByteTokenizer(vocab_size=model.cfg.vocab_size,
+                                              eos_id=model.cfg.eos_token_ids[0])
+        self.eos = set(model.cfg.eos_token_ids)
+        if getattr(self.tok, "eos_id", None) is not None:
+            self.eos.add(self.tok.eos_id)
+        self.max_model_len = max_model_len
+        self.max_queue = max_queue
+        pc = PrefixCache(model.kv, f"{model_id}", prefix_cache_blocks) \
+            if prefix_cache_blocks > 0 else None
+        self.sched = SchedulerState(model.kv, max_running, max_prefill_tokens, pc, max_queue)
+        self.use_graph = use_graph and self.dev.type == "cuda"
+        self.graphs: Dict[tuple, DecodeGraph] = {}
+        self.decoders: Dict[str, IncrementalDecoder] = {}
+        self.model_id = model_id
+        self._seq_counter = 0
+        self.last_step_ms = 0.0
+
+    # ------------------------------------------------------------ Engine API
+    def warmup(self) -> None:
+        if self.dev.type != "cuda":
+            return
+        t = GenerationTask("__warmup__", "warm", max_tokens=2, prompt_ids=[1, 2, 3, 4])
+        self.submit(t)
+        for _ in range(8):
+            out = self.step()
+            if any(c.is_final for _, c in out):
+                break
+        self.cancel("__warmup__")
+        torch.cuda.synchronize(self.dev)
+
+    def has_work(self) -> bool:
+        return bool(self.sched.waiting or self.sched.running)
+
+    def submit(self, task: GenerationTask) -> None:
+        if task.task_id in self.sched.by_id:
+            return
+        if len(self.sched.waiting) >= self.max_queue:
+            raise QueueFull(len(self.sched.waiting), self.max_queue)
+        ids = list(task.prompt_ids) if task.prompt_ids else self.tok.encode(task.prompt)
+        if not ids:
+            ids = [0]
+        if any(i < 0 or i >= self.cfg.vocab_size for i in ids):
+            raise InvalidConfig("prompt token id out of range")
+        if len(ids) + 1 > self.max_model_len:
+            raise PromptTooLong(f"{len(ids)} tokens > window {self.max_model_len - 1}")
+        blocks_needed = -(-(len(ids) + 1) // BLOCK_SIZE)
+        if blocks_needed > self.model.kv.num_blocks:
+            raise PromptTooLong(f"{len(ids)} tokens exceed the KV cache")
+        seq = Sequence(task=task, prompt_ids=ids, seq_id=task.task_id)
+        self.sched.add(seq)
+        self.decoders[task.task_id] = IncrementalDecoder(self.tok)
+
+    def cancel(self, task_id: str) -> None:
+        self.sched.remove(task_id)
+        self.decoders.pop(task_id, None)
+
+    def close(self) -> None:
+        for sid in list(self.sched.by_id):
+            self.cancel(sid)
+        self.graphs.clear()
+
+    def step(self) -> List[tuple]:
+        out: List[tuple] = []
+        t0 = time.perf_counter()
+        work = self.sched.admit()
+        if work:
+            self._prefill(work, out)
+        dec = self.sched.decode_set()
+        # Sequences whose first token came from this step's prefill are not
+        # decoded again in the same iteration.
+        just = {s.seq_id for s, st, n in work}
+        dec = [s for s in dec if s.seq_id not in just]
+        if dec:
+            self._decode(dec, out)
+        self.last_step_ms = (time.perf_counter() - t0) * 1000
+        kv = self.model.kv
+        metrics.KV_BLOCKS_USED.labels(model=self.model_id).set(
+            kv.num_blocks - kv.allocator.num_free)
+        metrics.KV_BLOCKS_TOTAL.labels(model=self.model_id).set(kv.num_blocks)
+        return out
+
+    # ------------------------------------------------------------ prefill
+    def _prefill(self, work, out):
+        m = self.model
+        seq_ids = [s.seq_id for s, _, _ in work]
+        q_lens = [n for _, _, n in work]
+        starts = [st for _, st, _ in work]
+        batch = build_batch(m, seq_ids, q_lens, starts, decode=False)
+        ids = torch.tensor([t for s, st, n in work for t in s.prompt_ids[st:st + n]],
+                           dtype=torch.int32).to(self.dev, non_blocking=True)
+        hidden = m.embed_tokens(ids)
+        m.forward(batch, hidden)
+        finishing = []
+        for (s, st, n), row in zip(work, batch.last_rows):
+            s.prefilled = st + n
+            if not s.in_prefill:
+                finishing.append((s, row))
+        if not finishing:
+            return
+        rows = torch.tensor([r for _, r in finishing], dtype=torch.long, device=self.dev)
+        logits = m.head(hidden.index_select(0, rows).contiguous())
+        toks = self._pick([s for s, _ in finishing], logits)
+        for (s, _), t in zip(finishing, toks):
+            self._emit(s, int(t), out)
+
+    # ------------------------------------------------------------ decode
+    def _graph_for(self, b: int, width: int) -> DecodeGraph:
+        key = (b, width)
+        g = self.graphs.get(key)
+        if g is None:
+            g = DecodeGraph(self.model, b, width, self.use_graph)
+            self.graphs[key] = g
+        return g
+
+    def _decode(self, seqs: List[Sequence], out):
+        m = self.model
+        kv = m.kv
+        if self.dev.type != "cuda":
+            starts = [kv.seqs[s.seq_id].length for s in seqs]
+            batch = build_batch(m, [s.seq_id for s in seqs], [1] * len(seqs), starts, True)
+            hidden = m.embed_tokens(torch.tensor([s.output_ids[-1] for s in seqs],
+                                                 dtype=torch.int32))
+            m.forward(batch, hidden)
+            logits = m.head(hidden)
+            for s, t in zip(seqs, self._pick(seqs, logits)):
+                self._emit(s, int(t), out)
+            return
+        n = len(seqs)
+        B = _bucket(n)
+        maxlen = max(s.total_len for s in seqs) + 1
+        width = 1 << max(4, math.ceil(math.log2(-(-maxlen // BLOCK_SIZE))))
+        g = self._graph_for(B, width)
+        ids = np.zeros(B, np.int32)
+        pos = np.zeros(B, np.int32)
+        slots = np.full(B, -1, np.int32)
+        lens = np.zeros(B, np.int32)
+        table = np.zeros((B, width), np.int32)
+        for i, s in enumerate(seqs):
+            kv.reserve(s.seq_id, s.total_len)
+            st = kv.seqs[s.seq_id]
+            p = s.total_len - 1  # position of the token being fed
+            st.length = p + 1
+            ids[i] = s.output_ids[-1]
+            pos[i] = p
+            slots[i] = st.blocks[p // BLOCK_SIZE] * BLOCK_SIZE + p % BLOCK_SIZE
+            lens[i] = p + 1
+            table[i, :len(st.blocks)] = st.blocks
+        g.fill(ids, pos, slots, lens, table)
+        g.upload()
+        if g.use_graph and g.graph is None:
+            g.capture()
+        g.run()
+        if all(s.task.temperature <= 0 and not self._has_penalty(s) for s in seqs):
+            g.download()
+            torch.cuda.current_stream(self.dev).synchronize()
+            toks = [int(t) for t in g.out_host[:n]]
+        else:
+            toks = self._pick(seqs, g.logits[:n])
+        for s, t in zip(seqs, toks):
+            self._emit(s, int(t), out)
+
+    # ------------------------------------------------------------ sampling
+    def _pick(self, seqs: List[Sequence], logits: torch.Tensor) -> List[int]:
+        m = self.model
+        if all(s.task.temperature <= 0 and not self._has_penalty(s) for s in seqs):
+            return [int(t) for t in m.greedy(logits).tolist()]
+        full = m.full_logits(logits)
+        if self.dev.type != "cuda":
+            outs = []
+            for s, row in zip(seqs, full):
+                sp = s.task.sampling
+                if not hasattr(s, "_rng"):
+                    s._rng = ref.init_rng(sp.seed)
+                outs.append(ref.sample(row, s.prompt_ids + s.output_ids, s.task.temperature,
+                                       sp.top_p, sp.top_k, sp.frequency_penalty,
+                                       sp.presence_penalty, 1.0, 0, s._rng))
+            return outs
+        B, V = full.shape
+        params = torch.zeros(B, 8)
+        hist_len = []
+        hist = []
+        seeds, offs = [], []
+        for i, s in enumerate(seqs):
+            sp = s.task.sampling
+            params[i] = torch.tensor([s.task.temperature, sp.top_p, sp.top_k,
+                                      sp.frequency_penalty, sp.presence_penalty, 1.0, 0, 0])
+            h = s.prompt_ids + s.output_ids if self._has_penalty(s) else []
+            hist.append(h)
+            hist_len.append(len(h))
+            seed = sp.seed if sp.seed is not None else (hash(s.seq_id) & 0x7FFFFFFF)
+            seeds.append(seed)
+            offs.append(s.rng_offset)
+            s.rng_offset += 1
+        hmax = max(1, max(hist_len))
+        ht = torch.zeros(B, hmax, dtype=torch.int32)
+        for i, h in enumerate(hist):
+            if h:
+                ht[i, :len(h)] = torch.tensor(h, dtype=torch.int32)
+        work = torch.empty(B * V, dtype=torch.float32, device=self.dev)
+        outt = torch.empty(B, dtype=torch.int32, device=self.dev)
+        ops.sample(full.contiguous(), params.to(self.dev), ht.to(self.dev),
+                   torch.tensor(hist_len, dtype=torch.int32, device=self.dev), work,
+                   torch.tensor(seeds, dtype=torch.int64, device=self.dev),
+                   torch.tensor(offs, dtype=torch.int64, device=self.dev), outt)
+        return [int(t) for t in outt.tolist()]
+
+    @staticmethod
+    def _has_penalty(s: Sequence) -> bool:
+        sp = s.task.sampling
+        return sp.frequency_penalty != 0.0 or sp.presence_penalty != 0.0
+
+    # ------------------------------------------------------------ emission
+    def _emit(self, s: Sequence, tok: int, out):
+        s.output_ids.append(tok)
+        if s.first_token_at is None:
+            s.first_token_at = time.monotonic()
+        tid = s.task.task_id
+        finish = None
+        if tok in self.eos:
+            finish = FinishReason.STOP
+        elif len(s.output_ids) >= max(1, s.task.max_tokens):
+            finish = FinishReason.LENGTH
+        elif s.total_len + 1 >= self.max_model_len:
+            finish = FinishReason.LENGTH
+        dec = self.decoders.get(tid)
+        text = "" if (dec is None or tok in self.eos) else dec.push([tok])
+        if finish is None:
+            out.append((tid, Chunk.token(tid, tok, text)))
+            return
+        if text:
+            out.append((tid, Chunk.token(tid, tok, text)))
+        fin = Chunk.final_marker(tid, "").with_finish_reason(finish).with_prompt_tokens(
+            len(s.prompt_ids))
+        out.append((tid, fin))
+        s.finished = True
+        self.sched.remove(s.seq_id)
+        self.decoders.pop(tid, None)
+
+
+class LLMBuilder(Builder):
+    """Builds an LLMEngine from a model preset (random init) or a shard dir."""
+
+    def __init__(self, model: str, device: str = "cuda", kv_blocks: int = 0,
+                 kv_fraction: float = 0.5, max_running: int = 64, max_model_len: int = 8192,
+                 prefix_cache_blocks: int = 0, use_graph: bool = True, seed: int = 0,
+                 tp=None, tokenizer_path: Optional[str] = None):
+        self.model_name = model
+        self.device = device
+        self.kv_blocks = kv_blocks
+        self.kv_fraction = kv_fraction
+        self.max_running = max_running
+        self.max_model_len = max_model_len
+        self.prefix_cache_blocks = prefix_cache_blocks
+        self.use_graph = use_graph
+        self.seed = seed
+        self.tp = tp
+        self.tokenizer_path = tokenizer_path
+        self.model = None
+        self.tokenizer = None
+
+    def connect(self, peers: PeerLayout) -> None:
+        pass
+
+    def load(self, shard: ShardSpec) -> Iterable[LoadProgress]:
+        import os
+
+        from ..api.templates import load_tokenizer
+        from ..models.config import get_config
+        from ..models.llama import LlamaModel
+
+        yield LoadProgress.msg(f"loading {self.model_name}")
+        if os.path.isdir(self.model_name):
+            from ..shard.format import load_stage_model
+
+            self.model = load_stage_model(self.model_name, shard, self.device, tp=self.tp)
+            tok_dir = self.tokenizer_path or os.path.join(os.path.dirname(
+                os.path.abspath(self.model_name.rstrip("/"))), "tokenizer")
+            if not os.path.isdir(tok_dir):
+                tok_dir = os.path.join(self.model_name, "tokenizer")
+        else:
+            cfg = get_config(self.model_name)
+            self.model = LlamaModel(cfg, self.device, tp=self.tp,
+                                    layer_start=shard.layer_start,
+                                    layer_end=shard.layer_end,
+                                    has_embed=shard.is_first_stage,
+                                    has_head=shard.is_last_stage).init_random(seed=self.seed)
+            tok_dir = self.tokenizer_path
+        cfg = self.model.cfg
+        self.tokenizer = load_tokenizer(tok_dir, cfg.vocab_size, cfg.eos_token_ids[0])
+        blocks = self.kv_blocks
+        if blocks <= 0:
+            per = self.model.kv_bytes_per_block()
+            if torch.device(self.device).type == "cuda":
+                free, _ = torch.cuda.mem_get_info(torch.device(self.device))
+                blocks = max(64, int(free * self.kv_fraction) // per)
+            else:
+                blocks = max(64, (self.max_running * self.max_model_len) // BLOCK_SIZE // 4)
+        self.model.allocate_kv(blocks)
+        yield LoadProgress.msg(f"kv cache: {blocks} blocks")
+        yield LoadProgress.done()
+
+    def build(self) -> Engine:
+        if self.model is None:
+            raise NotLoaded()
+        return LLMEngine(self.model, self.tokenizer, max_running=self.max_running,
+                         max_model_len=self.max_model_len, use_graph=self.use_graph,
+                         prefix_cache_blocks=self.prefix_cache_blocks,
+                         model_id=self.model_name)

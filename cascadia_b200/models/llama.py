@@ -86,9 +86,10 @@ class TPGroup:
         """[n, ...] on each rank -> [size, n, ...]."""
         if self.size == 1:
             return x.unsqueeze(0)
-        out = torch.empty((self.size,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+        out = torch.empty((self.size * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype,
+                          device=x.device)
         torch.distributed.all_gather_into_tensor(out, x.contiguous(), group=self.group)
-        return out
+        return out.view((self.size,) + tuple(x.shape))
 
 
 def _layer_generator(seed: int, layer: int, device) -> torch.Generator:

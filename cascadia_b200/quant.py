@@ -14,7 +14,8 @@ Kernel ("blob") form, produced once at load time by :func:`pack_blob`: for
 every (128-row tile, 128-wide k-block) an 8 KiB block of packed rows (64 bytes
 per row, nibble order within each 32-bit word ``c0,c2,c4,c6`` in the low
 half-words and ``c1,c3,c5,c7`` in the high ones so that one shift+mask yields a
-bf16x2 pair) followed by that block's bf16 scales.  The GEMM kernel fetches
+bf16x2 pair; the four 16-byte chunks of row ``r`` XOR-swizzled by
+``(r >> 1) & 3``) followed by that block's bf16 scales.  The GEMM kernel fetches
 one such block with a single bulk TMA copy.
 """
 from __future__ import annotations
@@ -141,7 +142,15 @@ def pack_blob(q: torch.Tensor, scales: torch.Tensor, group_size: int,
         word |= qt[..., 2 * h] << (4 * h)
         word |= qt[..., 2 * h + 1] << (16 + 4 * h)
     word = torch.where(word >= 2**31, word - 2**32, word).to(torch.int32)
-    packed_bytes = word.contiguous().view(torch.uint8).reshape(rt, kb, 128 * 64)
+    # Swizzle the four 16-byte chunks of each 64-byte row: chunk c of row r is
+    # stored at position c ^ ((r >> 1) & 3), which makes the kernel's 16-byte
+    # shared-memory loads (8 consecutive rows per phase) bank-conflict free.
+    word = word.view(rt, kb, 128, 4, 4)
+    rows = torch.arange(128, device=q.device)
+    perm = (torch.arange(4, device=q.device)[None, :] ^ ((rows[:, None] >> 1) & 3))  # [128, 4]
+    sw = torch.empty_like(word)
+    sw[:, :, rows[:, None], perm] = word[:, :, rows[:, None], torch.arange(4, device=q.device)[None, :]]
+    packed_bytes = sw.contiguous().view(torch.uint8).reshape(rt, kb, 128 * 64)
     gpr = 128 // group_size
     s = sc.view(rt, 128, kb, gpr).permute(0, 2, 1, 3).contiguous()
     s_bytes = s.view(torch.uint8).reshape(rt, kb, 128 * gpr * 2)

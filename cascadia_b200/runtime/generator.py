@@ -57,6 +57,7 @@ class DecodeGraph:
                                 num_splits=num_splits, blocks_per_split=bps, part_o=self.part_o,
                                 part_ml=self.part_ml)
         self.next_ids = None
+        self.logits = None
         self.graph = None
         self.launches = 0
         self.use_graph = use_graph and dev.type == "cuda"
@@ -65,8 +66,8 @@ class DecodeGraph:
         m = self.model
         m.embed_tokens(self.ids, out=self.hidden)
         m.forward(self.batch_view, self.hidden)
-        logits = m.head(self.hidden)
-        self.next_ids = m.greedy(logits)
+        self.logits = m.head(self.hidden)
+        self.next_ids = m.greedy(self.logits)
         return self.next_ids
 
     def capture(self, warmup: int = 2):

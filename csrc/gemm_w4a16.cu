@@ -15,9 +15,16 @@
 //     128-wide k-block) one contiguous 8 KiB block of packed nibbles followed by
 //     its scales, fetched with one cp.async.bulk.  Activations are fetched with
 //     a 2-D TMA tensor map (128-byte swizzle) straight into the UMMA layout.
+//     All of shared memory is this load ring (3..16 stages), so >= 48 KiB of
+//     weights are in flight per SM.
+//   * The dequantised A tiles live in TENSOR memory: four dequant groups (4
+//     warps each, one row per thread, ~2 instructions per weight) write
+//     (q - 8) * scale as bf16 with tcgen05.st into four 64-column A buffers, and
+//     the MMA reads A from TMEM (tcgen05.mma ... [a_tmem], b_desc).  Four
+//     buffers let dequantisation run up to four k-blocks ahead of the MMA, so
+//     MMA completion latency never stalls the weight stream.
 //   * Warp roles: warp 0 issues TMA, warp 1 owns TMEM and issues tcgen05.mma,
-//     warps 2..9 dequantise nibbles into the 128B-swizzled bf16 A tile and
-//     later run the epilogue (tcgen05.ld from TMEM).
+//     warps 2..17 dequantise and later run the epilogue (tcgen05.ld).
 //   * Split-K over k-blocks fills the 148 SMs for decode shapes.  Partials go
 //     to an fp32 workspace; the last CTA of a tile (per-tile counter) sums the
 //     splits in a fixed order, so results are deterministic run to run.
@@ -37,9 +44,12 @@ namespace cb {
 
 enum Epilogue : int { kEpiStore = 0, kEpiSilu = 1, kEpiResid = 2 };
 
-constexpr int kThreads = 320;  // 10 warps
-constexpr int kDequantThreads = 256;
-constexpr int kABytes = 128 * 128 * 2;  // one dequantised 128x128 bf16 tile
+constexpr int kGroups = 4;                 // dequant groups (A buffers in TMEM)
+constexpr int kDequantWarps = 4 * kGroups; // each group: 4 warps = 128 rows
+constexpr int kDequantThreads = kDequantWarps * 32;
+constexpr int kThreads = 64 + kDequantThreads;  // + producer warp + MMA warp
+constexpr uint32_t kACols = 64;            // TMEM columns of one 128x128 bf16 A tile
+constexpr uint32_t kAccCol = kGroups * kACols;  // accumulator starts after the A buffers
 
 template <int GS>
 struct BlobInfo {
@@ -48,21 +58,18 @@ struct BlobInfo {
   static constexpr int kBytes = kPacked + kScales;
 };
 
-template <int MT>
-struct Stages {
-  static constexpr int value = MT <= 16 ? 8 : MT <= 32 ? 8 : MT <= 64 ? 6 : MT <= 128 ? 3 : 2;
-};
-
 template <int MT, int GS>
 struct SmemPlan {
   static constexpr int kXBytes = 2 * MT * 128;  // two 64-wide K sub-tiles
   static constexpr int kStageRaw = kXBytes + BlobInfo<GS>::kBytes;
   static constexpr int kStage = (kStageRaw + 1023) / 1024 * 1024;
-  static constexpr int kSL = Stages<MT>::value;
-  static constexpr int kAOff = 0;
-  static constexpr int kLOff = 2 * kABytes;
-  static constexpr int kBarOff = kLOff + kSL * kStage;
+  static constexpr int kBudget = 210 * 1024;
+  static constexpr int kSLraw = kBudget / kStage;
+  static constexpr int kSL = kSLraw > 16 ? 16 : kSLraw;
+  static constexpr int kLOff = 0;
+  static constexpr int kBarOff = kSL * kStage;
   static constexpr int kTileBytes = 128 * (MT + 1) * 4;
+  static_assert(kSL >= 2, "need at least two load stages");
   static_assert(kTileBytes <= kBarOff, "epilogue tile must fit in the stage area");
   static constexpr int kTotal = kBarOff + 1024 + 1024;  // barriers + alignment slack
 };
@@ -85,22 +92,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   using Plan = SmemPlan<MT, GS>;
   constexpr int SL = Plan::kSL;
   constexpr int BLOB = BlobInfo<GS>::kBytes;
-  constexpr uint32_t kTmemCols = MT < 32 ? 32 : MT;
+  constexpr uint32_t kTmemCols = 512;
   constexpr uint32_t kIdesc = umma_idesc_bf16(128, MT);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // Align the dynamic smem base to 1024 bytes (128B-swizzle atoms).
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* a_smem = smem + Plan::kAOff;
   uint8_t* l_smem = smem + Plan::kLOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Plan::kBarOff);
   uint64_t* full_l = bars;
   uint64_t* empty_l = bars + SL;
   uint64_t* full_a = bars + 2 * SL;
-  uint64_t* empty_a = bars + 2 * SL + 2;
-  uint64_t* acc_full = bars + 2 * SL + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * SL + 5);
+  uint64_t* empty_a = bars + 2 * SL + kGroups;
+  uint64_t* acc_full = bars + 2 * SL + 2 * kGroups;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * SL + 2 * kGroups + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* is_last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
   float* tile = reinterpret_cast<float*>(smem);  // reused after the main loop
@@ -119,11 +125,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < SL; ++s) {
       mbar_init(&full_l[s], 1);
-      mbar_init(&empty_l[s], 8 + 1);  // 8 dequant warps + MMA commit
+      mbar_init(&empty_l[s], 4 + 1);  // the consuming dequant group's 4 warps + MMA commit
     }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&full_a[a], 8);
-      mbar_init(&empty_a[a], 1);
+    for (int g = 0; g < kGroups; ++g) {
+      mbar_init(&full_a[g], 4);
+      mbar_init(&empty_a[g], 1);
     }
     mbar_init(acc_full, 1);
     *abort_flag = 0;
@@ -138,6 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_acc = tmem_base + kAccCol;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -168,109 +175,122 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int it = 0; it < nkb; ++it) {
         const int s = it % SL;
         const uint32_t phl = (it / SL) & 1;
-        const int a = it & 1;
-        const uint32_t pha = (it >> 1) & 1;
-        if (!mbar_wait(&full_a[a], pha, args.status, kStatusGemmMmaTimeout, abort_flag)) break;
+        const int g = it % kGroups;
+        const uint32_t pha = (it / kGroups) & 1;
+        if (!mbar_wait(&full_a[g], pha, args.status, kStatusGemmMmaTimeout, abort_flag)) break;
         if (!mbar_wait(&full_l[s], phl, args.status, kStatusGemmMmaTimeout, abort_flag)) break;
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(a_smem + a * kABytes);
+        const uint32_t a_tm = tmem_base + g * kACols;
         const uint32_t x_addr = smem_u32(l_smem + s * Plan::kStage);
 #pragma unroll
-        for (int sub = 0; sub < 2; ++sub) {
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t da = umma_desc_sw128(a_addr + sub * (128 * 128) + kk * 32);
-            const uint64_t db = umma_desc_sw128(x_addr + sub * (MT * 128) + kk * 32);
-            mma_bf16_ss(tmem_base, da, db, kIdesc, (it > 0 || sub > 0 || kk > 0) ? 1u : 0u);
-          }
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t db = umma_desc_sw128(x_addr + (kk >> 2) * (MT * 128) + (kk & 3) * 32);
+          mma_bf16_ts(tmem_acc, a_tm + kk * 8, db, kIdesc, (it > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(&empty_a[a]);
+        mma_commit(&empty_a[g]);
         mma_commit(&empty_l[s]);
       }
       mma_commit(acc_full);
     }
   } else {
     // ------------------------------------------------------------ dequant
+    // Group g (warps 2+4g .. 5+4g) handles k-blocks it = g, g+4, ...; inside a
+    // group the warp's TMEM lane quarter q picks rows 32q..32q+31, one row per
+    // thread.  The thread reads its row's 64 packed bytes (chunk c of row r is
+    // stored at c ^ ((r >> 1) & 3): bank-conflict free for 8 consecutive
+    // rows), converts 128 nibbles to bf16 (q - 8) * scale and writes the 64
+    // bf16x2 columns of its lane into the group's A buffer in TMEM.
     const int t = tid - 64;
-    const int c = t & 3;
+    const int grp = t >> 7;
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
     const __nv_bfloat162 k136 = __floats2bfloat162_rn(136.0f, 136.0f);
+    const uint32_t l_base = smem_u32(l_smem) + Plan::kXBytes;
+    const uint32_t a_tm = tmem_base + grp * kACols + ((uint32_t)(q * 32) << 16);
     bool ok = true;
-    for (int it = 0; it < nkb && ok; ++it) {
+    for (int it = grp; it < nkb && ok; it += kGroups) {
       const int s = it % SL;
       const uint32_t phl = (it / SL) & 1;
-      const int a = it & 1;
-      const uint32_t pha = (it >> 1) & 1;
+      const uint32_t pha = (it / kGroups) & 1;
       if (!mbar_wait(&full_l[s], phl, args.status, kStatusGemmDequantTimeout, abort_flag)) {
         ok = false;
         break;
       }
-      if (!mbar_wait(&empty_a[a], pha ^ 1, args.status, kStatusGemmDequantTimeout, abort_flag)) {
+      const uint32_t wb = l_base + s * Plan::kStage;
+      uint4 p[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) p[c] = lds128(wb + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+      __nv_bfloat162 s2[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int si = GS == 128 ? r : r * (128 / GS) + (c * 32) / GS;
+        const uint16_t sraw = lds16(wb + BlobInfo<GS>::kPacked + si * 2);
+        s2[c] = __halves2bfloat162(__ushort_as_bfloat16(sraw), __ushort_as_bfloat16(sraw));
+      }
+      // The W part of the stage has been read: release it (the MMA still
+      // needs the X part; it commits to the same barrier).
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_l[s]);
+      if (!mbar_wait(&empty_a[grp], pha ^ 1, args.status, kStatusGemmDequantTimeout, abort_flag)) {
         ok = false;
         break;
       }
-      const uint8_t* wb = l_smem + s * Plan::kStage + Plan::kXBytes;
-      const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(wb + BlobInfo<GS>::kPacked);
-      uint8_t* ab = a_smem + a * kABytes;
+      tc_fence_after();
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int r = (t >> 2) + 64 * j;
-        const uint4 p = *reinterpret_cast<const uint4*>(wb + r * 64 + c * 16);
-        const uint32_t words[4] = {p.x, p.y, p.z, p.w};
-        const __nv_bfloat16 sv = (GS == 128) ? sc[r] : sc[r * (128 / GS) + (c * 32) / GS];
-        const __nv_bfloat162 s2 = __halves2bfloat162(sv, sv);
-        uint8_t* rowp = ab + (c >> 1) * (128 * 128) + r * 128;
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t words[4] = {p[c].x, p[c].y, p[c].z, p[c].w};
+        uint32_t o[16];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int wi = (i + c) & 3;  // rotation keeps the 16B stores bank-conflict free
+        for (int wi = 0; wi < 4; ++wi) {
           const uint32_t w = words[wi];
-          uint32_t o[4];
 #pragma unroll
           for (int h = 0; h < 4; ++h) {
             uint32_t v = ((w >> (4 * h)) & 0x000F000Fu) | 0x43004300u;  // bf16 (128 + q)
             __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
-            b = __hmul2(__hsub2(b, k136), s2);                         // (q - 8) * scale
-            o[h] = *reinterpret_cast<uint32_t*>(&b);
+            b = __hmul2(__hsub2(b, k136), s2[c]);                      // (q - 8) * scale
+            o[wi * 4 + h] = *reinterpret_cast<uint32_t*>(&b);
           }
-          const int chunk = (((c & 1) * 4 + wi) ^ (r & 7));
-          *reinterpret_cast<uint4*>(rowp + chunk * 16) = make_uint4(o[0], o[1], o[2], o[3]);
         }
+        tmem_st16(a_tm + c * 16, o);
       }
-      fence_proxy_async_smem();
+      tmem_st_wait();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&full_a[a]);
-        mbar_arrive(&empty_l[s]);
-      }
+      if (lane == 0) mbar_arrive(&full_a[grp]);
     }
 
     // ------------------------------------------------------------ epilogue
     const bool have_acc =
         ok && nkb > 0 && mbar_wait(acc_full, 0, args.status, kStatusGemmEpiTimeout, abort_flag);
-    const int q = warp & 3;               // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;     // which half of the MT columns
-    const int row = q * 32 + lane;        // weight row inside the tile
+    const int cg = grp;                   // which quarter of the MT columns
+    const int row = r;                    // weight row inside the tile
     const int n0 = rt * 128;
     const int m_base = tt * MT;
     const int Mpad = gridDim.z * MT;
-    constexpr int HALF = MT / 2;
+    constexpr int CQ = MT / 4;            // columns per warp
     tc_fence_after();
 
     // Phase 1: TMEM -> (workspace | smem tile).  Each thread owns one row.
     float* dst_ws = args.ws;
     if (have_acc) {
-      const uint32_t lane_addr = tmem_base + ((uint32_t)(q * 32) << 16);
+      const uint32_t lane_addr = tmem_acc + ((uint32_t)(q * 32) << 16);
+      constexpr int CW = CQ >= 16 ? 16 : CQ;
 #pragma unroll 1
-      for (int c0 = half * HALF; c0 < (half + 1) * HALF; c0 += (HALF >= 16 ? 16 : 8)) {
+      for (int c0 = cg * CQ; c0 < (cg + 1) * CQ; c0 += CW) {
         float v[16];
-        if constexpr (HALF >= 16) {
+        if constexpr (CW == 16) {
           tmem_ld16(lane_addr + c0, v);
-        } else {
+        } else if constexpr (CW == 8) {
           float v8[8];
           tmem_ld8(lane_addr + c0, v8);
 #pragma unroll
           for (int i = 0; i < 8; ++i) v[i] = v8[i];
+        } else {
+          float v4[4];
+          tmem_ld4(lane_addr + c0, v4);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v[i] = v4[i];
         }
-        constexpr int CW = HALF >= 16 ? 16 : 8;
         if (args.splits == 1) {
 #pragma unroll
           for (int i = 0; i < CW; ++i) tile[row * (MT + 1) + c0 + i] = v[i];
@@ -302,12 +322,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (do_final) {
           __threadfence();
           for (int idx = t; idx < 128 * MT; idx += kDequantThreads) {
-            const int r = idx & 127;
+            const int rr = idx & 127;
             const int m = idx >> 7;
             float acc = 0.f;
             for (int sp = 0; sp < args.splits; ++sp)
-              acc += __ldcg(&dst_ws[((size_t)sp * Mpad + m_base + m) * args.N + n0 + r]);
-            tile[r * (MT + 1) + m] = acc;
+              acc += __ldcg(&dst_ws[((size_t)sp * Mpad + m_base + m) * args.N + n0 + rr]);
+            tile[rr * (MT + 1) + m] = acc;
           }
           named_bar_sync(1, kDequantThreads);
         }
@@ -328,14 +348,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else {
           for (int idx = t; idx < 128 * MT; idx += kDequantThreads) {
-            const int r = idx & 127;
+            const int rr = idx & 127;
             const int m = idx >> 7;
             const int gm = m_base + m;
             if (gm < args.M) {
-              float y = tile[r * (MT + 1) + m];
+              float y = tile[rr * (MT + 1) + m];
               if constexpr (EPI == kEpiResid)
-                y += __bfloat162float(args.residual[(size_t)gm * args.ldr + n0 + r]);
-              args.out[(size_t)gm * args.ldo + n0 + r] = __float2bfloat16(y);
+                y += __bfloat162float(args.residual[(size_t)gm * args.ldr + n0 + rr]);
+              args.out[(size_t)gm * args.ldo + n0 + rr] = __float2bfloat16(y);
             }
           }
         }

@@ -37,7 +37,11 @@ def _decode_blob(blob, n, k, gs, interleave):
     for r in range(rt):
         for c in range(kb):
             blk = b[r, c]
-            words = blk[:8192].contiguous().view(torch.int32).view(128, 16).to(torch.int64) & 0xFFFFFFFF
+            phys = blk[:8192].contiguous().view(torch.int32).view(128, 4, 4)
+            rows = torch.arange(128)
+            # undo the chunk swizzle: logical chunk c lives at c ^ ((r >> 1) & 3)
+            logical = torch.stack([phys[rows, (c ^ ((rows >> 1) & 3))] for c in range(4)], 1)
+            words = logical.reshape(128, 16).to(torch.int64) & 0xFFFFFFFF
             sc = blk[8192:].contiguous().view(torch.bfloat16).view(128, 128 // gs).float()
             vals = torch.zeros(128, 128)
             for wi in range(16):
