@@ -281,11 +281,13 @@ class LLMEngine(Engine):
             finish = FinishReason.LENGTH
         dec = self.decoders.get(tid)
         text = "" if (dec is None or tok in self.eos) else dec.push([tok])
+        # n_tokens is set on every token chunk: a token whose text is still
+        # an incomplete UTF-8 sequence (empty text) must still be counted.
         if finish is None:
-            out.append((tid, Chunk.token(tid, tok, text)))
+            out.append((tid, Chunk.token(tid, tok, text).with_n_tokens(1)))
             return
-        if text:
-            out.append((tid, Chunk.token(tid, tok, text)))
+        if tok not in self.eos:
+            out.append((tid, Chunk.token(tid, tok, text).with_n_tokens(1)))
         fin = Chunk.final_marker(tid, "").with_finish_reason(finish).with_prompt_tokens(
             len(s.prompt_ids))
         out.append((tid, fin))

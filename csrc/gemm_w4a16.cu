@@ -64,12 +64,20 @@ struct SmemPlan {
   static constexpr int kStageRaw = kXBytes + BlobInfo<GS>::kBytes;
   static constexpr int kStage = (kStageRaw + 1023) / 1024 * 1024;
   static constexpr int kBudget = 210 * 1024;
-  static constexpr int kSLraw = kBudget / kStage;
+  // Stage count: a multiple of the number of dequant groups, so that every
+  // use of a stage is consumed by the same group (a group then never waits on
+  // a barrier more than one phase ahead of what it observed, which the
+  // mbarrier parity test could not tell apart).
+  static constexpr int kSLraw = (kBudget / kStage) / 4 * 4;
   static constexpr int kSL = kSLraw > 16 ? 16 : kSLraw;
+  // Independent TMEM accumulators the MMAs rotate over (dependent MMAs into
+  // one accumulator serialise on its read-modify-write latency).
+  static constexpr int kNAcc = MT <= 32 ? 8 : MT <= 64 ? 4 : 2;
   static constexpr int kLOff = 0;
   static constexpr int kBarOff = kSL * kStage;
   static constexpr int kTileBytes = 128 * (MT + 1) * 4;
-  static_assert(kSL >= 2, "need at least two load stages");
+  static_assert(kSL >= 4 && kSL % 4 == 0, "load stages must be a positive multiple of 4");
+  static_assert(kNAcc * MT <= 256, "accumulators must fit next to the A buffers in TMEM");
   static_assert(kTileBytes <= kBarOff, "epilogue tile must fit in the stage area");
   static constexpr int kTotal = kBarOff + 1024 + 1024;  // barriers + alignment slack
 };
@@ -185,7 +193,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t db = umma_desc_sw128(x_addr + (kk >> 2) * (MT * 128) + (kk & 3) * 32);
-          mma_bf16_ts(tmem_acc, a_tm + kk * 8, db, kIdesc, (it > 0 || kk > 0) ? 1u : 0u);
+          const int j = it * 8 + kk;                 // global MMA index
+          const int acc = j % Plan::kNAcc;
+          mma_bf16_ts(tmem_acc + acc * MT, a_tm + kk * 8, db, kIdesc, j >= Plan::kNAcc ? 1u : 0u);
         }
         mma_commit(&empty_a[g]);
         mma_commit(&empty_l[s]);
@@ -278,18 +288,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int c0 = cg * CQ; c0 < (cg + 1) * CQ; c0 += CW) {
         float v[16];
-        if constexpr (CW == 16) {
-          tmem_ld16(lane_addr + c0, v);
-        } else if constexpr (CW == 8) {
-          float v8[8];
-          tmem_ld8(lane_addr + c0, v8);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = v8[i];
-        } else {
-          float v4[4];
-          tmem_ld4(lane_addr + c0, v4);
+        for (int i = 0; i < 16; ++i) v[i] = 0.f;
+        // Only accumulators that received at least one MMA hold data.
+        const int nacc = min(Plan::kNAcc, nkb * 8);
+#pragma unroll 1
+        for (int ai = 0; ai < nacc; ++ai) {
+          const uint32_t ad = lane_addr + ai * MT + c0;
+          if constexpr (CW == 16) {
+            float u[16];
+            tmem_ld16(ad, u);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) v[i] = v4[i];
+            for (int i = 0; i < 16; ++i) v[i] += u[i];
+          } else if constexpr (CW == 8) {
+            float u[8];
+            tmem_ld8(ad, u);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] += u[i];
+          } else {
+            float u[4];
+            tmem_ld4(ad, u);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] += u[i];
+          }
         }
         if (args.splits == 1) {
 #pragma unroll
@@ -392,8 +413,7 @@ void dispatch_mt(int MT, const CUtensorMap& tmap, const GemmArgs& a, dim3 grid, 
     case 16: launch_w4a16<16, GS, EPI>(tmap, a, grid, s); break;
     case 32: launch_w4a16<32, GS, EPI>(tmap, a, grid, s); break;
     case 64: launch_w4a16<64, GS, EPI>(tmap, a, grid, s); break;
-    case 128: launch_w4a16<128, GS, EPI>(tmap, a, grid, s); break;
-    default: launch_w4a16<256, GS, EPI>(tmap, a, grid, s); break;
+    default: launch_w4a16<128, GS, EPI>(tmap, a, grid, s); break;
   }
 }
 
@@ -401,8 +421,7 @@ static int pick_mt(int M) {
   if (M <= 16) return 16;
   if (M <= 32) return 32;
   if (M <= 64) return 64;
-  if (M <= 128) return 128;
-  return 256;
+  return 128;
 }
 
 // Number of k-splits: fill the SMs with whole waves of CTAs while keeping at
