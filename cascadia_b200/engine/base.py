@@ -122,6 +122,13 @@ class DeviceFault(EngineError):
         self.code = code
 
 
+class ShutdownRequested(EngineError):
+    """The upstream stage asked this stage to stop (clean relay-loop exit)."""
+
+    def __init__(self):
+        super().__init__("pipeline shutdown requested")
+
+
 class TaskError(EngineError):
     def __init__(self, task_id: TaskId, source: EngineError):
         super().__init__(f"task {task_id}: {source}")

@@ -71,6 +71,9 @@ class LLMEngine(Engine):
         self.model_id = model_id
         self._seq_counter = 0
         self.last_step_ms = 0.0
+        # Set for the first stage of a pipeline (parallel.pp.PipelineHead):
+        # the model forward then relays through the downstream stages.
+        self.pipeline = None
 
     # ------------------------------------------------------------ Engine API
     def warmup(self) -> None:
@@ -145,20 +148,32 @@ class LLMEngine(Engine):
         batch = build_batch(m, seq_ids, q_lens, starts, decode=False)
         ids = torch.tensor([t for s, st, n in work for t in s.prompt_ids[st:st + n]],
                            dtype=torch.int32).to(self.dev, non_blocking=True)
-        hidden = m.embed_tokens(ids)
-        m.forward(batch, hidden)
-        finishing = []
-        for (s, st, n), row in zip(work, batch.last_rows):
+        for s, st, n in work:
             s.prefilled = st + n
+        seqs = [s for s, _, _ in work]
+        toks = self._run_model(batch, ids, seqs)
+        for s, t in zip(seqs, toks):
             if not s.in_prefill:
-                finishing.append((s, row))
-        if not finishing:
-            return
-        rows = torch.tensor([r for _, r in finishing], dtype=torch.long, device=self.dev)
-        logits = m.head(hidden.index_select(0, rows).contiguous())
-        toks = self._pick([s for s, _ in finishing], logits)
-        for (s, _), t in zip(finishing, toks):
-            self._emit(s, int(t), out)
+                self._emit(s, int(t), out)
+
+    def _run_model(self, batch, ids, seqs: List[Sequence]) -> List[int]:
+        """Forward the batch and pick one token per sequence (its last row)."""
+        m = self.model
+        hidden = m.embed_tokens(ids)
+        if self.pipeline is None:
+            m.forward(batch, hidden)
+            rows = torch.tensor(batch.last_rows, dtype=torch.long, device=self.dev)
+            logits = m.head(hidden.index_select(0, rows).contiguous())
+            return self._pick(seqs, logits)
+        want = [i for i, s in enumerate(seqs)
+                if not s.in_prefill and (s.task.temperature > 0 or self._has_penalty(s))]
+        toks, logits = self.pipeline.forward_tokens(batch, hidden, want)
+        toks = list(toks)
+        if want:
+            picked = self._pick_full([seqs[i] for i in want], logits.to(self.dev))
+            for i, t in zip(want, picked):
+                toks[i] = t
+        return toks
 
     # ------------------------------------------------------------ decode
     def _graph_for(self, b: int, width: int) -> DecodeGraph:
@@ -172,14 +187,11 @@ class LLMEngine(Engine):
     def _decode(self, seqs: List[Sequence], out):
         m = self.model
         kv = m.kv
-        if self.dev.type != "cuda":
-            starts = [kv.seqs[s.seq_id].length for s in seqs]
+        if self.dev.type != "cuda" or self.pipeline is not None:
+            starts = [s.total_len - 1 for s in seqs]
             batch = build_batch(m, [s.seq_id for s in seqs], [1] * len(seqs), starts, True)
-            hidden = m.embed_tokens(torch.tensor([s.output_ids[-1] for s in seqs],
-                                                 dtype=torch.int32))
-            m.forward(batch, hidden)
-            logits = m.head(hidden)
-            for s, t in zip(seqs, self._pick(seqs, logits)):
+            ids = torch.tensor([s.output_ids[-1] for s in seqs], dtype=torch.int32).to(self.dev)
+            for s, t in zip(seqs, self._run_model(batch, ids, seqs)):
                 self._emit(s, int(t), out)
             return
         n = len(seqs)
@@ -221,7 +233,10 @@ class LLMEngine(Engine):
         m = self.model
         if all(s.task.temperature <= 0 and not self._has_penalty(s) for s in seqs):
             return [int(t) for t in m.greedy(logits).tolist()]
-        full = m.full_logits(logits)
+        return self._pick_full(seqs, m.full_logits(logits))
+
+    def _pick_full(self, seqs: List[Sequence], full: torch.Tensor) -> List[int]:
+        """Sample from full-vocabulary logits (penalties use the history)."""
         if self.dev.type != "cuda":
             outs = []
             for s, row in zip(seqs, full):

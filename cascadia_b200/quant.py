@@ -117,13 +117,15 @@ def unpack_nibbles(packed: torch.Tensor) -> torch.Tensor:
 
 
 def interleave_rows(x: torch.Tensor) -> torch.Tensor:
-    """[2I, ...] = [gate; up] -> per 128-row tile: 64 gate rows then 64 up rows."""
+    """[2I, ...] = [gate; up] -> rows alternate gate_j, up_j.
+
+    Every 128-row tile then holds 64 (gate, up) pairs in adjacent rows, i.e.
+    adjacent TMEM lanes, so the GEMM epilogue forms SiLU(gate) * up with one
+    lane shuffle."""
     two_i = x.shape[0]
     i = two_i // 2
     assert i % 64 == 0, "intermediate size must be a multiple of 64"
-    g = x[:i].reshape(i // 64, 64, *x.shape[1:])
-    u = x[i:].reshape(i // 64, 64, *x.shape[1:])
-    return torch.stack([g, u], dim=1).reshape(two_i, *x.shape[1:])
+    return torch.stack([x[:i], x[i:]], dim=1).reshape(two_i, *x.shape[1:])
 
 
 def pack_blob(q: torch.Tensor, scales: torch.Tensor, group_size: int,

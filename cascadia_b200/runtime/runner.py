@@ -32,7 +32,7 @@ import time
 from typing import AsyncIterator, Deque, Dict, Iterator, Optional, Set
 
 from .. import metrics
-from ..engine.base import Builder, Engine, EngineError, classify_exception
+from ..engine.base import Builder, Engine, EngineError, ShutdownRequested, classify_exception
 from ..types import Chunk, FinishReason, GenerationTask, PeerLayout, ShardSpec, TaskId
 
 log = logging.getLogger("cascadia.runner")
@@ -321,6 +321,8 @@ class Runner:
             try:
                 with self._lock:
                     self.engine.step()
+            except ShutdownRequested:
+                return RelayExit.SLOT_EMPTY
             except BaseException as e:  # noqa: BLE001
                 err = classify_exception(e)
                 if err.is_connection_fatal():

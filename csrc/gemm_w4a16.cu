@@ -34,6 +34,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -92,6 +93,12 @@ struct GemmArgs {
   int M, N, K;
   int ldo, ldr;
   int kb_per_split, splits;
+  // Diagnostics only (CASCADIA_GEMM_DIAG): bit 0 skips the dequant math,
+  // bit 1 skips issuing the MMAs.  Results are wrong in those modes; the
+  // pipeline, barriers and memory traffic are unchanged.
+  int diag;
+  // Persistent (stream-K) kernel only.
+  int row_tiles, units, ub, ur, max_contrib;
 };
 
 template <int MT, int GS, int EPI>
@@ -192,6 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t x_addr = smem_u32(l_smem + s * Plan::kStage);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
+          if (args.diag & 2) break;
           const uint64_t db = umma_desc_sw128(x_addr + (kk >> 2) * (MT * 128) + (kk & 3) * 32);
           const int j = it * 8 + kk;                 // global MMA index
           const int acc = j % Plan::kNAcc;
@@ -248,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
+        if (args.diag & 1) break;
         const uint32_t words[4] = {p[c].x, p[c].y, p[c].z, p[c].w};
         uint32_t o[16];
 #pragma unroll
@@ -361,8 +370,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int m = idx >> 6;
             const int gm = m_base + m;
             if (gm < args.M) {
-              const float g = tile[j * (MT + 1) + m];
-              const float u = tile[(64 + j) * (MT + 1) + m];
+              const float g = tile[(2 * j) * (MT + 1) + m];
+              const float u = tile[(2 * j + 1) * (MT + 1) + m];
               const float y = g / (1.f + __expf(-g)) * u;
               args.out[(size_t)gm * args.ldo + rt * 64 + j] = __float2bfloat16(y);
             }
@@ -392,6 +401,323 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------------
+// Persistent stream-K variant (decode, MT <= 64).
+//
+// One CTA per SM; the (tile, k-block) units of the whole GEMM are split into
+// equal contiguous ranges, one per CTA, so there is no wave quantisation and
+// the TMA ring streams across tile boundaries without refilling.  The MMA
+// warp alternates between two TMEM accumulators (one per tile segment), four
+// dedicated epilogue warps drain the previous segment while the next one
+// streams.  A tile split across CTAs reduces through the fp32 workspace in
+// contributor order (deterministic); the last contributor applies the fused
+// epilogue.  Gate/up rows alternate (gate_j, up_j), so SiLU(gate) * up is one
+// lane shuffle.
+constexpr int kEpiWarps = 4;
+constexpr int kPThreads = 64 + kDequantThreads + kEpiWarps * 32;
+
+__device__ __forceinline__ int unit_begin(int c, int ub, int ur) { return c * ub + min(c, ur); }
+__device__ __forceinline__ int unit_owner(int u, int ub, int ur) {
+  const int t = ur * (ub + 1);
+  return u < t ? u / (ub + 1) : ur + (u - t) / ub;
+}
+
+template <int MT, int GS, int EPI>
+__device__ __forceinline__ void persist_final(const GemmArgs& args, const float (&v)[MT], int rt,
+                                              int row, int m_base, int lane) {
+  const int n = rt * 128 + row;
+  if constexpr (EPI == kEpiSilu) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const float up = __shfl_xor_sync(0xffffffffu, v[m], 1);
+      const int gm = m_base + m;
+      if ((lane & 1) == 0 && gm < args.M) {
+        const float g = v[m];
+        args.out[(size_t)gm * args.ldo + rt * 64 + (row >> 1)] =
+            __float2bfloat16(g / (1.f + __expf(-g)) * up);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const int gm = m_base + m;
+      if (gm < args.M) {
+        float y = v[m];
+        if constexpr (EPI == kEpiResid)
+          y += __bfloat162float(args.residual[(size_t)gm * args.ldr + n]);
+        args.out[(size_t)gm * args.ldo + n] = __float2bfloat16(y);
+      }
+    }
+  }
+}
+
+template <int MT, int GS, int EPI>
+__global__ void __launch_bounds__(kPThreads, 1)
+    w4a16_persistent_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs args) {
+  using Plan = SmemPlan<MT, GS>;
+  constexpr int SL = Plan::kSL;
+  constexpr int BLOB = BlobInfo<GS>::kBytes;
+  constexpr uint32_t kTmemCols = 512;
+  constexpr uint32_t kIdesc = umma_idesc_bf16(128, MT);
+  static_assert(MT <= 64, "persistent kernel is for decode token tiles");
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* l_smem = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Plan::kBarOff);
+  uint64_t* full_l = bars;
+  uint64_t* empty_l = bars + SL;
+  uint64_t* full_a = bars + 2 * SL;
+  uint64_t* empty_a = bars + 2 * SL + kGroups;
+  uint64_t* acc_full = bars + 2 * SL + 2 * kGroups;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* epi_bar = acc_empty + 2;  // bounded sync of the 4 epilogue warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* is_last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int KB = args.K / 128;
+  const int cta = blockIdx.x;
+  const int u_begin = unit_begin(cta, args.ub, args.ur);
+  const int n_units = unit_begin(cta + 1, args.ub, args.ur) - u_begin;
+
+  if (tid == 0) {
+    for (int s = 0; s < SL; ++s) {
+      mbar_init(&full_l[s], 1);
+      mbar_init(&empty_l[s], 4 + 1);
+    }
+    for (int g = 0; g < kGroups; ++g) {
+      mbar_init(&full_a[g], 4);
+      mbar_init(&empty_a[g], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpiWarps);
+    }
+    mbar_init(epi_bar, kEpiWarps * 32);
+    *abort_flag = 0;
+    *is_last_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_acc = tmem_base + kAccCol;  // two buffers of MT columns
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tmap(&tmap_x);
+      int issued = 0;
+      for (int i = 0; i < n_units; ++i) {
+        const int u = u_begin + i;
+        const int tile = u / KB, kb = u % KB;
+        const int rt = tile % args.row_tiles, tt = tile / args.row_tiles;
+        const int s = i % SL;
+        const uint32_t ph = (i / SL) & 1;
+        if (!mbar_wait(&empty_l[s], ph ^ 1, args.status, kStatusGemmLoadTimeout, abort_flag)) break;
+        uint8_t* st = l_smem + s * Plan::kStage;
+        mbar_arrive_expect_tx(&full_l[s], Plan::kXBytes + BLOB);
+        bulk_g2s(st + Plan::kXBytes, args.wblob + ((size_t)rt * KB + kb) * BLOB, BLOB,
+                 &full_l[s]);
+        tma_load_2d(st, &tmap_x, kb * 128, tt * MT, &full_l[s]);
+        tma_load_2d(st + MT * 128, &tmap_x, kb * 128 + 64, tt * MT, &full_l[s]);
+        ++issued;
+      }
+      for (int it = max(0, issued - SL); it < issued; ++it)
+        mbar_wait(&full_l[it % SL], (it / SL) & 1, nullptr, 0, nullptr);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int seg = 0;
+      bool ok = true;
+      for (int i = 0; i < n_units && ok; ++i) {
+        const int u = u_begin + i;
+        const int kb = u % KB;
+        const bool first = (i == 0) || (kb == 0);
+        const bool last = (i == n_units - 1) || (kb == KB - 1);
+        const int buf = seg & 1;
+        if (first) {
+          ok = mbar_wait(&acc_empty[buf], ((seg >> 1) & 1) ^ 1, args.status,
+                         kStatusGemmMmaTimeout, abort_flag);
+          if (!ok) break;
+        }
+        const int s = i % SL;
+        const int g = i % kGroups;
+        if (!mbar_wait(&full_a[g], (i / kGroups) & 1, args.status, kStatusGemmMmaTimeout,
+                       abort_flag) ||
+            !mbar_wait(&full_l[s], (i / SL) & 1, args.status, kStatusGemmMmaTimeout,
+                       abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_tm = tmem_base + g * kACols;
+        const uint32_t x_addr = smem_u32(l_smem + s * Plan::kStage);
+        const uint32_t d_tm = tmem_acc + buf * MT;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          if (args.diag & 2) break;
+          const uint64_t db = umma_desc_sw128(x_addr + (kk >> 2) * (MT * 128) + (kk & 3) * 32);
+          mma_bf16_ts(d_tm, a_tm + kk * 8, db, kIdesc, (first && kk == 0) ? 0u : 1u);
+        }
+        mma_commit(&empty_a[g]);
+        mma_commit(&empty_l[s]);
+        if (last) {
+          mma_commit(&acc_full[buf]);
+          ++seg;
+        }
+      }
+    }
+  } else if (warp < 2 + kDequantWarps) {
+    // ------------------------------------------------------------ dequant
+    const int t = tid - 64;
+    const int grp = t >> 7;
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const __nv_bfloat162 k136 = __floats2bfloat162_rn(136.0f, 136.0f);
+    const uint32_t l_base = smem_u32(l_smem) + Plan::kXBytes;
+    const uint32_t a_tm = tmem_base + grp * kACols + ((uint32_t)(q * 32) << 16);
+    for (int it = grp; it < n_units; it += kGroups) {
+      const int s = it % SL;
+      if (!mbar_wait(&full_l[s], (it / SL) & 1, args.status, kStatusGemmDequantTimeout,
+                     abort_flag))
+        break;
+      const uint32_t wb = l_base + s * Plan::kStage;
+      uint4 p[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) p[c] = lds128(wb + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+      __nv_bfloat162 s2[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int si = GS == 128 ? r : r * (128 / GS) + (c * 32) / GS;
+        const uint16_t sraw = lds16(wb + BlobInfo<GS>::kPacked + si * 2);
+        s2[c] = __halves2bfloat162(__ushort_as_bfloat16(sraw), __ushort_as_bfloat16(sraw));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_l[s]);
+      if (!mbar_wait(&empty_a[grp], ((it / kGroups) & 1) ^ 1, args.status,
+                     kStatusGemmDequantTimeout, abort_flag))
+        break;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (args.diag & 1) break;
+        const uint32_t words[4] = {p[c].x, p[c].y, p[c].z, p[c].w};
+        uint32_t o[16];
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+          const uint32_t w = words[wi];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            uint32_t v = ((w >> (4 * h)) & 0x000F000Fu) | 0x43004300u;  // bf16 (128 + q)
+            __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
+            b = __hmul2(__hsub2(b, k136), s2[c]);                      // (q - 8) * scale
+            o[wi * 4 + h] = *reinterpret_cast<uint32_t*>(&b);
+          }
+        }
+        tmem_st16(a_tm + c * 16, o);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full_a[grp]);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int et = tid - (64 + kDequantThreads);  // 0..127
+    int seg = 0;
+    uint32_t epi_phase = 0;
+    bool epi_ok = true;
+    // All 128 epilogue threads arrive, then wait (bounded) for the phase.
+    auto epi_sync = [&]() {
+      mbar_arrive(epi_bar);
+      if (!mbar_wait(epi_bar, epi_phase & 1, args.status, kStatusGemmEpiTimeout, abort_flag))
+        epi_ok = false;
+      ++epi_phase;
+    };
+    for (int i = 0; i < n_units;) {
+      const int u = u_begin + i;
+      const int tile = u / KB;
+      const int kb0 = u % KB;
+      const int len = min(KB - kb0, n_units - i);
+      const int buf = seg & 1;
+      const int rt = tile % args.row_tiles, tt = tile / args.row_tiles;
+      if (!mbar_wait(&acc_full[buf], (seg >> 1) & 1, args.status, kStatusGemmEpiTimeout,
+                     abort_flag))
+        break;
+      tc_fence_after();
+      float v[MT];
+      const uint32_t lane_addr = tmem_acc + buf * MT + ((uint32_t)(q * 32) << 16);
+#pragma unroll
+      for (int c0 = 0; c0 < MT; c0 += 16) {
+        float u16[16];
+        tmem_ld16(lane_addr + c0, u16);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[c0 + k] = u16[k];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      const bool whole = (kb0 == 0 && len == KB);
+      if (whole) {
+        persist_final<MT, GS, EPI>(args, v, rt, row, tt * MT, lane);
+      } else {
+        const int c_first = unit_owner(tile * KB, args.ub, args.ur);
+        const int c_last = unit_owner(tile * KB + KB - 1, args.ub, args.ur);
+        const int slot = cta - c_first;
+        const int ncontrib = c_last - c_first + 1;
+        float* wsp = args.ws + ((size_t)tile * args.max_contrib) * MT * 128;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) wsp[((size_t)slot * MT + m) * 128 + row] = v[m];
+        __threadfence();
+        epi_sync();
+        if (et == 0) {
+          const int old = atomicAdd(&args.counters[tile], 1);
+          const int lst = (old == ncontrib - 1) ? 1 : 0;
+          if (lst) args.counters[tile] = 0;
+          *is_last_flag = lst;
+        }
+        epi_sync();
+        const bool lst = *is_last_flag != 0;
+        epi_sync();  // flag read before the next segment rewrites it
+        if (!epi_ok) break;
+        if (lst) {
+          __threadfence();
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            float acc = 0.f;
+            for (int j = 0; j < ncontrib; ++j) acc += __ldcg(&wsp[((size_t)j * MT + m) * 128 + row]);
+            v[m] = acc;
+          }
+          persist_final<MT, GS, EPI>(args, v, rt, row, tt * MT, lane);
+        }
+      }
+      ++seg;
+      i += len;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
 // ---------------------------------------------------------------- host side
 
 template <int MT, int GS, int EPI>
@@ -405,6 +731,29 @@ void launch_w4a16(const CUtensorMap& tmap, const GemmArgs& a, dim3 grid, cudaStr
   }
   w4a16_gemm_kernel<MT, GS, EPI><<<grid, kThreads, Plan::kTotal, stream>>>(tmap, a);
   CB_CUDA_CHECK(cudaGetLastError());
+}
+
+template <int MT, int GS, int EPI>
+void launch_persistent(const CUtensorMap& tmap, const GemmArgs& a, int ctas, cudaStream_t stream) {
+  using Plan = SmemPlan<MT, GS>;
+  static bool configured = false;
+  if (!configured) {
+    CB_CUDA_CHECK(cudaFuncSetAttribute(w4a16_persistent_kernel<MT, GS, EPI>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, Plan::kTotal));
+    configured = true;
+  }
+  w4a16_persistent_kernel<MT, GS, EPI><<<ctas, kPThreads, Plan::kTotal, stream>>>(tmap, a);
+  CB_CUDA_CHECK(cudaGetLastError());
+}
+
+template <int GS, int EPI>
+void dispatch_persistent(int MT, const CUtensorMap& tmap, const GemmArgs& a, int ctas,
+                         cudaStream_t s) {
+  switch (MT) {
+    case 16: launch_persistent<16, GS, EPI>(tmap, a, ctas, s); break;
+    case 32: launch_persistent<32, GS, EPI>(tmap, a, ctas, s); break;
+    default: launch_persistent<64, GS, EPI>(tmap, a, ctas, s); break;
+  }
 }
 
 template <int GS, int EPI>
@@ -449,6 +798,8 @@ static int pick_splits(int tiles, int KB, int num_sms) {
 
 struct GemmPlanInfo {
   int MT, splits, kbps, token_tiles, row_tiles;
+  bool persistent;
+  int ctas, units, ub, ur, max_contrib;
 };
 
 static GemmPlanInfo plan_gemm(int M, int N, int K, int forced_splits) {
@@ -462,12 +813,25 @@ static GemmPlanInfo plan_gemm(int M, int N, int K, int forced_splits) {
   splits = std::max(1, std::min(splits, KB));
   p.kbps = (KB + splits - 1) / splits;
   p.splits = (KB + p.kbps - 1) / p.kbps;
+  // Decode-sized token tiles use the persistent stream-K kernel.
+  static const bool no_persist = [] {
+    const char* e = std::getenv("CASCADIA_GEMM_NO_PERSIST");
+    return e != nullptr && std::atoi(e) != 0;
+  }();
+  p.persistent = p.MT <= 64 && forced_splits <= 0 && !no_persist;
+  p.units = p.row_tiles * p.token_tiles * KB;
+  p.ctas = std::min(num_sms(), p.units);
+  p.ub = p.units / p.ctas;
+  p.ur = p.units % p.ctas;
+  p.max_contrib = (KB + p.ub - 1) / p.ub + 1;
   return p;
 }
 
 // Workspace floats needed for a GEMM of this shape (0 when no split).
 int64_t w4a16_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t forced_splits) {
   GemmPlanInfo p = plan_gemm((int)M, (int)N, (int)K, (int)forced_splits);
+  if (p.persistent)
+    return (int64_t)p.row_tiles * p.token_tiles * p.max_contrib * p.MT * 128;
   if (p.splits == 1) return 0;
   return (int64_t)p.splits * p.token_tiles * p.MT * N;
 }
@@ -498,7 +862,11 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
   if (M == 0) return;
   const c10::cuda::CUDAGuard guard(x.device());
   GemmPlanInfo p = plan_gemm(M, (int)N, K, (int)forced_splits);
-  if (p.splits > 1) {
+  if (p.persistent) {
+    TORCH_CHECK(ws.numel() >= (int64_t)p.row_tiles * p.token_tiles * p.max_contrib * p.MT * 128,
+                "workspace too small");
+    TORCH_CHECK(counters.numel() >= (int64_t)p.token_tiles * p.row_tiles, "counters too small");
+  } else if (p.splits > 1) {
     TORCH_CHECK(ws.numel() >= (int64_t)p.splits * p.token_tiles * p.MT * N, "workspace too small");
     TORCH_CHECK(counters.numel() >= (int64_t)p.token_tiles * p.row_tiles, "counters too small");
   }
@@ -509,8 +877,13 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
                    ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr())
                    : nullptr;
   a.ldr = residual.has_value() ? (int)residual->stride(0) : 0;
-  a.ws = p.splits > 1 ? ws.data_ptr<float>() : nullptr;
-  a.counters = p.splits > 1 ? counters.data_ptr<int>() : nullptr;
+  a.ws = (p.splits > 1 || p.persistent) ? ws.data_ptr<float>() : nullptr;
+  a.counters = (p.splits > 1 || p.persistent) ? counters.data_ptr<int>() : nullptr;
+  a.row_tiles = p.row_tiles;
+  a.units = p.units;
+  a.ub = p.ub;
+  a.ur = p.ur;
+  a.max_contrib = p.max_contrib;
   a.status = status.data_ptr<int>();
   a.M = M;
   a.N = (int)N;
@@ -518,6 +891,11 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
   a.ldo = (int)out.stride(0);
   a.kb_per_split = p.kbps;
   a.splits = p.splits;
+  static const int diag = [] {
+    const char* e = std::getenv("CASCADIA_GEMM_DIAG");
+    return e ? std::atoi(e) : 0;
+  }();
+  a.diag = diag;
   TORCH_CHECK(epilogue != kEpiResid || residual.has_value(), "residual epilogue needs residual");
 
   CUtensorMap tmap = make_tmap_2d_bf16(x.data_ptr(), (uint64_t)K, (uint64_t)M,
@@ -525,6 +903,18 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
                                        CU_TENSOR_MAP_SWIZZLE_128B);
   dim3 grid(p.row_tiles, p.splits, p.token_tiles);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (p.persistent) {
+    if (group_size == 128) {
+      if (epilogue == kEpiStore) dispatch_persistent<128, kEpiStore>(p.MT, tmap, a, p.ctas, stream);
+      else if (epilogue == kEpiSilu) dispatch_persistent<128, kEpiSilu>(p.MT, tmap, a, p.ctas, stream);
+      else dispatch_persistent<128, kEpiResid>(p.MT, tmap, a, p.ctas, stream);
+    } else {
+      if (epilogue == kEpiStore) dispatch_persistent<32, kEpiStore>(p.MT, tmap, a, p.ctas, stream);
+      else if (epilogue == kEpiSilu) dispatch_persistent<32, kEpiSilu>(p.MT, tmap, a, p.ctas, stream);
+      else dispatch_persistent<32, kEpiResid>(p.MT, tmap, a, p.ctas, stream);
+    }
+    return;
+  }
   if (group_size == 128) {
     if (epilogue == kEpiStore) dispatch_mt<128, kEpiStore>(p.MT, tmap, a, grid, stream);
     else if (epilogue == kEpiSilu) dispatch_mt<128, kEpiSilu>(p.MT, tmap, a, grid, stream);
@@ -538,7 +928,8 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
 
 std::vector<int64_t> w4a16_plan(int64_t M, int64_t N, int64_t K, int64_t forced_splits) {
   GemmPlanInfo p = plan_gemm((int)M, (int)N, (int)K, (int)forced_splits);
-  return {p.MT, p.splits, p.kbps, p.token_tiles, p.row_tiles};
+  return {p.MT, p.persistent ? -p.ctas : p.splits, p.persistent ? p.ub : p.kbps, p.token_tiles,
+          p.row_tiles};
 }
 
 }  // namespace cb

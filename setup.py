@@ -11,7 +11,8 @@ import os
 # Keep torch from adding its own multi-arch -gencode list.
 os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
 
-from setuptools import setup  # noqa: E402
+import pybind11  # noqa: E402
+from setuptools import Extension, setup  # noqa: E402
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -50,7 +51,15 @@ def main():
                 sources=[os.path.join("csrc", s) for s in SOURCES],
                 include_dirs=[CSRC],
                 extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
-            )
+            ),
+            # Native runtime (no CUDA): TCP stage transport, KV block allocator.
+            Extension(
+                name="cascadia_b200._runtime",
+                sources=[os.path.join("csrc", "runtime", "runtime.cpp")],
+                include_dirs=[pybind11.get_include()],
+                extra_compile_args=["-O2", "-std=c++17", "-fvisibility=hidden"],
+                language="c++",
+            ),
         ],
         cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
     )
