@@ -1,0 +1,267 @@
+"""Command line: ``python -m cascadia_b200 <command>``.
+
+Commands and flag names follow the reference CLI where the semantics carry
+over (crates/cascadia-cli/src/lib.rs:144-770): ``worker`` (one stage / rank,
+``--rank --total --layer-start --layer-end --model --listen --next --api
+--engine``), ``run`` (single-process server), ``shard`` (write the per-stage
+INT4 layout), ``engines``, ``doctor`` (CUDA / sm_100 / NCCL / NVLink checks)
+and ``place`` (choose a PP x TP x EP split for the GPUs of one box).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import logging
+import os
+import signal
+import sys
+import threading
+
+ENGINES = {
+    "mock": "word-echo engine for tests (no weights)",
+    "llama": "dense Llama-family INT4 engine (continuous batching, paged KV, TP, PP)",
+    "moe": "sparse-MoE INT4 engine (Qwen3-MoE / Kimi-K2 shapes, expert parallel)",
+    "spec": "distributed speculative decoding (draft stage + target stages)",
+}
+
+
+def _init_logging(level: str):
+    logging.basicConfig(level=getattr(logging, level.upper(), logging.INFO),
+                        format="%(asctime)s %(levelname)s %(name)s: %(message)s")
+
+
+def _parse_hostport(s: str, default_host="127.0.0.1"):
+    if s is None:
+        return None
+    host, _, port = s.rpartition(":")
+    return (host or default_host), int(port)
+
+
+def _common(p: argparse.ArgumentParser):
+    p.add_argument("--model", required=False, default="tiny-llama",
+                   help="shard directory or model preset (random-init weights)")
+    p.add_argument("--served-model-name", default=None)
+    p.add_argument("--engine", default="llama", choices=sorted(ENGINES))
+    p.add_argument("--device", default="cuda")
+    p.add_argument("--max-model-len", type=int, default=8192)
+    p.add_argument("--max-running", type=int, default=64)
+    p.add_argument("--kv-blocks", type=int, default=0)
+    p.add_argument("--kv-fraction", type=float, default=0.5)
+    p.add_argument("--kv-prefix-cache-size", type=int, default=0,
+                   help="blocks kept for prefix reuse (0 disables)")
+    p.add_argument("--no-cuda-graph", action="store_true")
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--tokenizer", default=None)
+    p.add_argument("--log-level", default="info")
+    p.add_argument("--max-concurrent", type=int, default=16)
+
+
+def _serve(runner, api: str, model_name: str, max_concurrent: int):
+    import uvicorn
+
+    from .api.server import ApiConfig, make_app
+
+    host, port = _parse_hostport(api, "0.0.0.0")
+    app = make_app(runner, ApiConfig(model_name=model_name,
+                                     max_concurrent_requests=max_concurrent))
+    uvicorn.run(app, host=host, port=port, log_level="warning")
+
+
+def _builder(args, tp=None):
+    from .engine.llm import LLMBuilder
+    from .engine.mock import MockBuilder
+
+    if args.engine == "mock":
+        return MockBuilder()
+    if args.engine == "moe":
+        from .engine.moe import MoEBuilder
+
+        return MoEBuilder(args.model, device=args.device, kv_blocks=args.kv_blocks,
+                          max_running=args.max_running, max_model_len=args.max_model_len,
+                          seed=args.seed)
+    return LLMBuilder(args.model, device=args.device, kv_blocks=args.kv_blocks,
+                      kv_fraction=args.kv_fraction, max_running=args.max_running,
+                      max_model_len=args.max_model_len,
+                      prefix_cache_blocks=args.kv_prefix_cache_size,
+                      use_graph=not args.no_cuda_graph, seed=args.seed, tp=tp,
+                      tokenizer_path=args.tokenizer)
+
+
+def cmd_run(args):
+    """Single-process server: the whole model on one device."""
+    from .runtime.runner import Runner
+    from .types import PeerLayout, ShardSpec
+
+    _init_logging(args.log_level)
+    name = args.served_model_name or os.path.basename(str(args.model).rstrip("/"))
+    runner = Runner(_builder(args), model_id=name, device=args.device)
+    nl = _num_layers(args.model)
+    runner.start(PeerLayout(), ShardSpec(name, 0, nl, nl, args.device, True, True))
+    try:
+        _serve(runner, args.api, name, args.max_concurrent)
+    finally:
+        runner.close()
+
+
+def _num_layers(model: str) -> int:
+    if os.path.isdir(model):
+        from .shard.format import read_pipeline
+
+        return read_pipeline(model)["num_layers"]
+    from .models.config import PRESETS
+
+    return PRESETS[model].num_layers if model in PRESETS else 1
+
+
+def cmd_worker(args):
+    """One pipeline stage.  Rank 0 serves the API (or a stdin prompt loop);
+    other ranks run the relay loop and exit non-zero on a dead link so a
+    supervisor (systemd Restart=on-failure) rebuilds the stage."""
+    from .engine.llm import LLMBuilder
+    from .parallel.pp import PipelineHead, PipelineWorker, TcpChannel
+    from .runtime.runner import RelayExit, Runner
+    from .transport.tcp import TensorLink
+    from .types import PeerLayout, ShardPlan, ShardSpec
+
+    _init_logging(args.log_level)
+    if args.rank >= args.total:
+        raise SystemExit(f"--rank {args.rank} must be < --total {args.total}")
+    name = args.served_model_name or os.path.basename(str(args.model).rstrip("/"))
+    nl = _num_layers(args.model)
+    if args.layer_start is not None and args.layer_end is not None:
+        ls, le = args.layer_start, args.layer_end
+    else:
+        st = ShardPlan.uniform(name, nl, 1, 1, 1, args.total).stages[args.rank]
+        ls, le = st.layer_start, st.layer_end
+    first, last = args.rank == 0, args.rank == args.total - 1
+    shard = ShardSpec(name, ls, le, nl, args.device, first, last)
+    builder = LLMBuilder(args.model, device=args.device, kv_blocks=args.kv_blocks or 2048,
+                         max_running=args.max_running, max_model_len=args.max_model_len,
+                         use_graph=False, seed=args.seed)
+    # Links: listen for upstream first (downstream stages start first), then dial.
+    up = down = None
+    if not first:
+        srv = TensorLink.listen(*_parse_hostport(args.listen, "0.0.0.0"))
+        logging.info("rank %d listening on %s", args.rank, args.listen)
+        up = TensorLink.accept(srv, timeout_s=args.connect_timeout)
+    if not last:
+        down = TensorLink.connect(*_parse_hostport(args.next), total_s=args.connect_timeout)
+    for p in builder.load(shard):
+        logging.info("load: %s", p.message)
+    model = builder.model
+    if not first:
+        worker = PipelineWorker(model, TcpChannel(up=up, down=down), is_last=last)
+        r = Runner(None, model_id=name, device=args.device)
+        r.start_with_engine(worker, drive=False)
+        code = r.run_relay_loop()
+        logging.info("relay loop exit: %s", code.value)
+        sys.exit(1 if code is RelayExit.CONNECTION_FATAL else 0)
+    engine = builder.build()
+    if not last:
+        engine.pipeline = PipelineHead(model, TcpChannel(down=down))
+    runner = Runner(None, model_id=name, device=args.device)
+    runner.start_with_engine(engine)
+    if args.api:
+        try:
+            _serve(runner, args.api, name, args.max_concurrent)
+        finally:
+            if engine.pipeline is not None:
+                engine.pipeline.shutdown()
+            runner.close()
+    else:
+        from .types import GenerationTask
+
+        import uuid
+        for line in sys.stdin:
+            if not line.strip():
+                continue
+            s = runner.generate(GenerationTask("stdin-" + uuid.uuid4().hex[:8], line.strip(),
+                                               max_tokens=args.max_tokens))
+            print(s.collect(), flush=True)
+        if engine.pipeline is not None:
+            engine.pipeline.shutdown()
+        runner.close()
+
+
+def cmd_shard(args):
+    from .models.config import get_config
+    from .shard.format import write_random_shards
+
+    cfg = get_config(args.model)
+    split = [int(x) for x in args.layer_split.split(",")] if args.layer_split else None
+    meta = write_random_shards(cfg, args.output_dir, args.num_stages, args.model,
+                               seed=args.seed, layer_split=split, device=args.device,
+                               tokenizer_dir=args.tokenizer)
+    print(json.dumps(meta, indent=1))
+
+
+def cmd_engines(args):
+    for k, v in ENGINES.items():
+        print(f"{k:6s} {v}")
+
+
+def cmd_doctor(args):
+    from .utils.doctor import run_doctor
+
+    report = run_doctor()
+    print(json.dumps(report, indent=1))
+    sys.exit(0 if report.get("ok") else 1)
+
+
+def cmd_place(args):
+    from .utils.placement import choose_parallelism
+
+    print(json.dumps(choose_parallelism(args.model, args.gpus, args.batch, args.context,
+                                        gpu_mem_gb=args.gpu_mem_gb), indent=1))
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser(prog="cascadia_b200")
+    sub = p.add_subparsers(dest="cmd", required=True)
+
+    r = sub.add_parser("run", help="serve the whole model from one process")
+    _common(r)
+    r.add_argument("--api", default="0.0.0.0:8000")
+    r.set_defaults(fn=cmd_run)
+
+    w = sub.add_parser("worker", help="run one pipeline stage")
+    _common(w)
+    w.add_argument("--rank", type=int, required=True)
+    w.add_argument("--total", type=int, required=True)
+    w.add_argument("--layer-start", type=int, default=None)
+    w.add_argument("--layer-end", type=int, default=None)
+    w.add_argument("--listen", default=None, help="host:port for the upstream stage")
+    w.add_argument("--next", default=None, help="host:port of the downstream stage")
+    w.add_argument("--api", default=None, help="rank 0: serve the OpenAI API here")
+    w.add_argument("--connect-timeout", type=float, default=30.0)
+    w.add_argument("--max-tokens", type=int, default=256)
+    w.set_defaults(fn=cmd_worker)
+
+    s = sub.add_parser("shard", help="write the per-stage INT4 shard layout")
+    s.add_argument("--model", required=True, help="model preset (random-init weights)")
+    s.add_argument("--output-dir", required=True)
+    s.add_argument("--num-stages", type=int, default=1)
+    s.add_argument("--layer-split", default=None, help="comma-separated layers per stage")
+    s.add_argument("--seed", type=int, default=0)
+    s.add_argument("--device", default="cpu")
+    s.add_argument("--tokenizer", default=None)
+    s.set_defaults(fn=cmd_shard)
+
+    sub.add_parser("engines", help="list engines").set_defaults(fn=cmd_engines)
+    sub.add_parser("doctor", help="check CUDA / NCCL / NVLink").set_defaults(fn=cmd_doctor)
+
+    pl = sub.add_parser("place", help="choose a PP x TP x EP split")
+    pl.add_argument("--model", required=True)
+    pl.add_argument("--gpus", type=int, default=8)
+    pl.add_argument("--batch", type=int, default=64)
+    pl.add_argument("--context", type=int, default=4096)
+    pl.add_argument("--gpu-mem-gb", type=float, default=180.0)
+    pl.set_defaults(fn=cmd_place)
+
+    args = p.parse_args(argv)
+    signal.signal(signal.SIGTERM, lambda *a: sys.exit(0))
+    args.fn(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -94,7 +94,8 @@ struct GemmArgs {
   int ldo, ldr;
   int kb_per_split, splits;
   // Diagnostics only (CASCADIA_GEMM_DIAG): bit 0 skips the dequant math,
-  // bit 1 skips issuing the MMAs.  Results are wrong in those modes; the
+  // bit 1 skips issuing the MMAs, bit 2 skips the activation loads and bit 3
+  // the dequant warps' shared-memory reads (persistent kernel).  Results are wrong in those modes; the
   // pipeline, barriers and memory traffic are unchanged.
   int diag;
   // Persistent (stream-K) kernel only.
@@ -456,21 +457,27 @@ __global__ void __launch_bounds__(kPThreads, 1)
     w4a16_persistent_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs args) {
   using Plan = SmemPlan<MT, GS>;
   constexpr int SL = Plan::kSL;
+  constexpr int R = SL / kGroups;  // rounds resident in the ring
   constexpr int BLOB = BlobInfo<GS>::kBytes;
   constexpr uint32_t kTmemCols = 512;
   constexpr uint32_t kIdesc = umma_idesc_bf16(128, MT);
   static_assert(MT <= 64, "persistent kernel is for decode token tiles");
 
+  // Synchronisation (per "round" of 4 units, one per dequant group):
+  //   full_l[s]        TMA landed W + X of the unit in stage s
+  //   full_a[g]        group g wrote its unit's A tile into TMEM (4 warps)
+  //   round_done[r%R]  one tcgen05.commit after the round's MMAs: the round's
+  //                    4 stages and 4 A buffers are free again (MMA completion
+  //                    implies the dequant warps finished reading them).
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* l_smem = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Plan::kBarOff);
   uint64_t* full_l = bars;
-  uint64_t* empty_l = bars + SL;
-  uint64_t* full_a = bars + 2 * SL;
-  uint64_t* empty_a = bars + 2 * SL + kGroups;
-  uint64_t* acc_full = bars + 2 * SL + 2 * kGroups;
+  uint64_t* round_done = bars + SL;
+  uint64_t* full_a = round_done + R;
+  uint64_t* acc_full = full_a + kGroups;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* epi_bar = acc_empty + 2;  // bounded sync of the 4 epilogue warps
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 1);
@@ -486,14 +493,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
   const int n_units = unit_begin(cta + 1, args.ub, args.ur) - u_begin;
 
   if (tid == 0) {
-    for (int s = 0; s < SL; ++s) {
-      mbar_init(&full_l[s], 1);
-      mbar_init(&empty_l[s], 4 + 1);
-    }
-    for (int g = 0; g < kGroups; ++g) {
-      mbar_init(&full_a[g], 4);
-      mbar_init(&empty_a[g], 1);
-    }
+    for (int s = 0; s < SL; ++s) mbar_init(&full_l[s], 1);
+    for (int r = 0; r < R; ++r) mbar_init(&round_done[r], 1);
+    for (int g = 0; g < kGroups; ++g) mbar_init(&full_a[g], 4);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], kEpiWarps);
@@ -523,14 +525,20 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const int tile = u / KB, kb = u % KB;
         const int rt = tile % args.row_tiles, tt = tile / args.row_tiles;
         const int s = i % SL;
-        const uint32_t ph = (i / SL) & 1;
-        if (!mbar_wait(&empty_l[s], ph ^ 1, args.status, kStatusGemmLoadTimeout, abort_flag)) break;
+        const int rho = i / kGroups;
+        if ((i % kGroups) == 0 &&
+            !mbar_wait(&round_done[rho % R], ((rho / R) & 1) ^ 1, args.status,
+                       kStatusGemmLoadTimeout, abort_flag))
+          break;
         uint8_t* st = l_smem + s * Plan::kStage;
-        mbar_arrive_expect_tx(&full_l[s], Plan::kXBytes + BLOB);
+        const bool skip_x = (args.diag & 4) != 0;
+        mbar_arrive_expect_tx(&full_l[s], (skip_x ? 0 : Plan::kXBytes) + BLOB);
         bulk_g2s(st + Plan::kXBytes, args.wblob + ((size_t)rt * KB + kb) * BLOB, BLOB,
                  &full_l[s]);
-        tma_load_2d(st, &tmap_x, kb * 128, tt * MT, &full_l[s]);
-        tma_load_2d(st + MT * 128, &tmap_x, kb * 128 + 64, tt * MT, &full_l[s]);
+        if (!skip_x) {
+          tma_load_2d(st, &tmap_x, kb * 128, tt * MT, &full_l[s]);
+          tma_load_2d(st + MT * 128, &tmap_x, kb * 128 + 64, tt * MT, &full_l[s]);
+        }
         ++issued;
       }
       for (int it = max(0, issued - SL); it < issued; ++it)
@@ -554,8 +562,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
         const int s = i % SL;
         const int g = i % kGroups;
-        if (!mbar_wait(&full_a[g], (i / kGroups) & 1, args.status, kStatusGemmMmaTimeout,
-                       abort_flag) ||
+        const int rho = i / kGroups;
+        if (!mbar_wait(&full_a[g], rho & 1, args.status, kStatusGemmMmaTimeout, abort_flag) ||
             !mbar_wait(&full_l[s], (i / SL) & 1, args.status, kStatusGemmMmaTimeout,
                        abort_flag)) {
           ok = false;
@@ -571,12 +579,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
           const uint64_t db = umma_desc_sw128(x_addr + (kk >> 2) * (MT * 128) + (kk & 3) * 32);
           mma_bf16_ts(d_tm, a_tm + kk * 8, db, kIdesc, (first && kk == 0) ? 0u : 1u);
         }
-        mma_commit(&empty_a[g]);
-        mma_commit(&empty_l[s]);
         if (last) {
           mma_commit(&acc_full[buf]);
           ++seg;
         }
+        if (g == kGroups - 1 || i == n_units - 1) mma_commit(&round_done[rho % R]);
       }
     }
   } else if (warp < 2 + kDequantWarps) {
@@ -590,24 +597,26 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const uint32_t a_tm = tmem_base + grp * kACols + ((uint32_t)(q * 32) << 16);
     for (int it = grp; it < n_units; it += kGroups) {
       const int s = it % SL;
+      const int rho = it / kGroups;
       if (!mbar_wait(&full_l[s], (it / SL) & 1, args.status, kStatusGemmDequantTimeout,
                      abort_flag))
         break;
       const uint32_t wb = l_base + s * Plan::kStage;
-      uint4 p[4];
+      uint4 p[4] = {};
+      __nv_bfloat162 s2[4] = {};
+      if (!(args.diag & 8)) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) p[c] = lds128(wb + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
-      __nv_bfloat162 s2[4];
+        for (int c = 0; c < 4; ++c) p[c] = lds128(wb + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int si = GS == 128 ? r : r * (128 / GS) + (c * 32) / GS;
-        const uint16_t sraw = lds16(wb + BlobInfo<GS>::kPacked + si * 2);
-        s2[c] = __halves2bfloat162(__ushort_as_bfloat16(sraw), __ushort_as_bfloat16(sraw));
+        for (int c = 0; c < 4; ++c) {
+          const int si = GS == 128 ? r : r * (128 / GS) + (c * 32) / GS;
+          const uint16_t sraw = lds16(wb + BlobInfo<GS>::kPacked + si * 2);
+          s2[c] = __halves2bfloat162(__ushort_as_bfloat16(sraw), __ushort_as_bfloat16(sraw));
+        }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_l[s]);
-      if (!mbar_wait(&empty_a[grp], ((it / kGroups) & 1) ^ 1, args.status,
-                     kStatusGemmDequantTimeout, abort_flag))
+      // The previous round's MMAs must be done with this group's A buffer.
+      if (rho >= 1 && !mbar_wait(&round_done[(rho - 1) % R], ((rho - 1) / R) & 1, args.status,
+                                 kStatusGemmDequantTimeout, abort_flag))
         break;
       tc_fence_after();
 #pragma unroll
@@ -758,12 +767,9 @@ void dispatch_persistent(int MT, const CUtensorMap& tmap, const GemmArgs& a, int
 
 template <int GS, int EPI>
 void dispatch_mt(int MT, const CUtensorMap& tmap, const GemmArgs& a, dim3 grid, cudaStream_t s) {
-  switch (MT) {
-    case 16: launch_w4a16<16, GS, EPI>(tmap, a, grid, s); break;
-    case 32: launch_w4a16<32, GS, EPI>(tmap, a, grid, s); break;
-    case 64: launch_w4a16<64, GS, EPI>(tmap, a, grid, s); break;
-    default: launch_w4a16<128, GS, EPI>(tmap, a, grid, s); break;
-  }
+  // Token tiles up to 64 run the persistent kernel; this one serves 128.
+  (void)MT;
+  launch_w4a16<128, GS, EPI>(tmap, a, grid, s);
 }
 
 static int pick_mt(int M) {
@@ -819,6 +825,16 @@ static GemmPlanInfo plan_gemm(int M, int N, int K, int forced_splits) {
     return e != nullptr && std::atoi(e) != 0;
   }();
   p.persistent = p.MT <= 64 && forced_splits <= 0 && !no_persist;
+  if (!p.persistent && p.MT < 128) {
+    // The split-K (non-persistent) kernel is instantiated for 128-token tiles.
+    p.MT = 128;
+    p.token_tiles = (M + 127) / 128;
+    splits = forced_splits > 0 ? forced_splits
+                               : pick_splits(p.row_tiles * p.token_tiles, KB, num_sms());
+    splits = std::max(1, std::min(splits, KB));
+    p.kbps = (KB + splits - 1) / splits;
+    p.splits = (KB + p.kbps - 1) / p.kbps;
+  }
   p.units = p.row_tiles * p.token_tiles * KB;
   p.ctas = std::min(num_sms(), p.units);
   p.ub = p.units / p.ctas;
