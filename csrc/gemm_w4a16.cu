@@ -405,6 +405,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ------------------------------------------------------------------------
 // Persistent stream-K variant (decode, MT <= 64).
 //
+// Measured on B200: a single SM streams bulk copies at a rate set by the
+// number of copies, not by bytes in flight (8.4 KiB copies top out near
+// 3.5 TB/s over 148 SMs at any ring depth, >= 16.9 KiB copies reach the HBM
+// peak).  The producer therefore fetches the weight blobs of two consecutive
+// k-blocks (contiguous in the blob layout) with ONE bulk copy into a stage
+// pair; dequantisation and MMA still work per k-block.
+//
 // One CTA per SM; the (tile, k-block) units of the whole GEMM are split into
 // equal contiguous ranges, one per CTA, so there is no wave quantisation and
 // the TMA ring streams across tile boundaries without refilling.  The MMA
@@ -416,6 +423,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 // lane shuffle.
 constexpr int kEpiWarps = 4;
 constexpr int kPThreads = 64 + kDequantThreads + kEpiWarps * 32;
+
+template <int MT, int GS>
+struct PairPlan {
+  static constexpr int kBlob = BlobInfo<GS>::kBytes;
+  static constexpr int kUnitX = 2 * MT * 128;                      // X of one k-block
+  static constexpr int kXOff = (2 * kBlob + 1023) / 1024 * 1024;  // X after both blobs
+  static constexpr int kPair = kXOff + 2 * kUnitX;
+  static constexpr int kNPraw = (210 * 1024) / kPair / 2 * 2;      // even
+  static constexpr int kNP = kNPraw > 8 ? 8 : kNPraw;
+  static constexpr int kSL = 2 * kNP;                              // k-block slots (mult. of 4)
+  static constexpr int kBarOff = kNP * kPair;
+  static constexpr int kTotal = kBarOff + 1024 + 1024;
+  static_assert(kNP >= 2 && kSL % 4 == 0, "need an even number of stage pairs");
+};
 
 __device__ __forceinline__ int unit_begin(int c, int ub, int ur) { return c * ub + min(c, ur); }
 __device__ __forceinline__ int unit_owner(int u, int ub, int ur) {
@@ -455,16 +476,17 @@ __device__ __forceinline__ void persist_final(const GemmArgs& args, const float 
 template <int MT, int GS, int EPI>
 __global__ void __launch_bounds__(kPThreads, 1)
     w4a16_persistent_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs args) {
-  using Plan = SmemPlan<MT, GS>;
-  constexpr int SL = Plan::kSL;
-  constexpr int R = SL / kGroups;  // rounds resident in the ring
+  using Plan = PairPlan<MT, GS>;
+  constexpr int NP = Plan::kNP;     // stage pairs (one bulk copy each)
+  constexpr int SL = Plan::kSL;     // k-block slots
+  constexpr int R = SL / kGroups;   // rounds resident in the ring
   constexpr int BLOB = BlobInfo<GS>::kBytes;
   constexpr uint32_t kTmemCols = 512;
   constexpr uint32_t kIdesc = umma_idesc_bf16(128, MT);
   static_assert(MT <= 64, "persistent kernel is for decode token tiles");
 
   // Synchronisation (per "round" of 4 units, one per dequant group):
-  //   full_l[s]        TMA landed W + X of the unit in stage s
+  //   full_l[p]        TMA landed W + X of the two units of stage pair p
   //   full_a[g]        group g wrote its unit's A tile into TMEM (4 warps)
   //   round_done[r%R]  one tcgen05.commit after the round's MMAs: the round's
   //                    4 stages and 4 A buffers are free again (MMA completion
@@ -475,7 +497,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   uint8_t* l_smem = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Plan::kBarOff);
   uint64_t* full_l = bars;
-  uint64_t* round_done = bars + SL;
+  uint64_t* round_done = bars + NP;
   uint64_t* full_a = round_done + R;
   uint64_t* acc_full = full_a + kGroups;
   uint64_t* acc_empty = acc_full + 2;
@@ -493,7 +515,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   const int n_units = unit_begin(cta + 1, args.ub, args.ur) - u_begin;
 
   if (tid == 0) {
-    for (int s = 0; s < SL; ++s) mbar_init(&full_l[s], 1);
+    for (int p = 0; p < NP; ++p) mbar_init(&full_l[p], 1);
     for (int r = 0; r < R; ++r) mbar_init(&round_done[r], 1);
     for (int g = 0; g < kGroups; ++g) mbar_init(&full_a[g], 4);
     for (int b = 0; b < 2; ++b) {
@@ -519,30 +541,53 @@ __global__ void __launch_bounds__(kPThreads, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       prefetch_tmap(&tmap_x);
+      const bool skip_x = (args.diag & 4) != 0;
       int issued = 0;
-      for (int i = 0; i < n_units; ++i) {
-        const int u = u_begin + i;
-        const int tile = u / KB, kb = u % KB;
-        const int rt = tile % args.row_tiles, tt = tile / args.row_tiles;
-        const int s = i % SL;
-        const int rho = i / kGroups;
-        if ((i % kGroups) == 0 &&
-            !mbar_wait(&round_done[rho % R], ((rho / R) & 1) ^ 1, args.status,
-                       kStatusGemmLoadTimeout, abort_flag))
+      for (int j = 0; 2 * j < n_units; ++j) {
+        const int i0 = 2 * j;
+        const int nu = min(2, n_units - i0);  // units in this pair
+        const int p = j % NP;
+        const int rho = i0 / kGroups;
+        // A round (4 units = 2 pairs) frees both of its pairs at once.
+        if ((j & 1) == 0 && !mbar_wait(&round_done[rho % R], ((rho / R) & 1) ^ 1, args.status,
+                                       kStatusGemmLoadTimeout, abort_flag))
           break;
-        uint8_t* st = l_smem + s * Plan::kStage;
-        const bool skip_x = (args.diag & 4) != 0;
-        mbar_arrive_expect_tx(&full_l[s], (skip_x ? 0 : Plan::kXBytes) + BLOB);
-        bulk_g2s(st + Plan::kXBytes, args.wblob + ((size_t)rt * KB + kb) * BLOB, BLOB,
-                 &full_l[s]);
+        uint8_t* st = l_smem + p * Plan::kPair;
+        const int u0 = u_begin + i0;
+        const int tile0 = u0 / KB, kb0 = u0 % KB;
+        const int rt0 = tile0 % args.row_tiles, tt0 = tile0 / args.row_tiles;
+        int tt1 = tt0, rt1 = rt0, kb1 = kb0;
+        if (nu == 2) {
+          const int u1 = u0 + 1;
+          const int tile1 = u1 / KB;
+          kb1 = u1 % KB;
+          rt1 = tile1 % args.row_tiles;
+          tt1 = tile1 / args.row_tiles;
+        }
+        const uint32_t xbytes = skip_x ? 0u : (uint32_t)(nu * Plan::kUnitX);
+        mbar_arrive_expect_tx(&full_l[p], nu * BLOB + xbytes);
+        const uint8_t* w0 = args.wblob + ((size_t)rt0 * KB + kb0) * BLOB;
+        if (nu == 2 && tt1 == tt0) {
+          bulk_g2s(st, w0, 2 * BLOB, &full_l[p]);  // both k-blocks, one copy
+        } else {
+          bulk_g2s(st, w0, BLOB, &full_l[p]);
+          if (nu == 2)
+            bulk_g2s(st + BLOB, args.wblob + ((size_t)rt1 * KB + kb1) * BLOB, BLOB, &full_l[p]);
+        }
         if (!skip_x) {
-          tma_load_2d(st, &tmap_x, kb * 128, tt * MT, &full_l[s]);
-          tma_load_2d(st + MT * 128, &tmap_x, kb * 128 + 64, tt * MT, &full_l[s]);
+          uint8_t* x0 = st + Plan::kXOff;
+          tma_load_2d(x0, &tmap_x, kb0 * 128, tt0 * MT, &full_l[p]);
+          tma_load_2d(x0 + MT * 128, &tmap_x, kb0 * 128 + 64, tt0 * MT, &full_l[p]);
+          if (nu == 2) {
+            uint8_t* x1 = x0 + Plan::kUnitX;
+            tma_load_2d(x1, &tmap_x, kb1 * 128, tt1 * MT, &full_l[p]);
+            tma_load_2d(x1 + MT * 128, &tmap_x, kb1 * 128 + 64, tt1 * MT, &full_l[p]);
+          }
         }
         ++issued;
       }
-      for (int it = max(0, issued - SL); it < issued; ++it)
-        mbar_wait(&full_l[it % SL], (it / SL) & 1, nullptr, 0, nullptr);
+      for (int jj = max(0, issued - NP); jj < issued; ++jj)
+        mbar_wait(&full_l[jj % NP], (jj / NP) & 1, nullptr, 0, nullptr);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -560,18 +605,19 @@ __global__ void __launch_bounds__(kPThreads, 1)
                          kStatusGemmMmaTimeout, abort_flag);
           if (!ok) break;
         }
-        const int s = i % SL;
+        const int p = (i >> 1) % NP;
         const int g = i % kGroups;
         const int rho = i / kGroups;
         if (!mbar_wait(&full_a[g], rho & 1, args.status, kStatusGemmMmaTimeout, abort_flag) ||
-            !mbar_wait(&full_l[s], (i / SL) & 1, args.status, kStatusGemmMmaTimeout,
+            !mbar_wait(&full_l[p], ((i >> 1) / NP) & 1, args.status, kStatusGemmMmaTimeout,
                        abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t a_tm = tmem_base + g * kACols;
-        const uint32_t x_addr = smem_u32(l_smem + s * Plan::kStage);
+        const uint32_t x_addr =
+            smem_u32(l_smem + p * Plan::kPair + Plan::kXOff + (i & 1) * Plan::kUnitX);
         const uint32_t d_tm = tmem_acc + buf * MT;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
@@ -593,15 +639,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int q = warp & 3;
     const int r = q * 32 + lane;
     const __nv_bfloat162 k136 = __floats2bfloat162_rn(136.0f, 136.0f);
-    const uint32_t l_base = smem_u32(l_smem) + Plan::kXBytes;
+    const uint32_t l_base = smem_u32(l_smem);
     const uint32_t a_tm = tmem_base + grp * kACols + ((uint32_t)(q * 32) << 16);
     for (int it = grp; it < n_units; it += kGroups) {
-      const int s = it % SL;
+      const int pr = (it >> 1) % NP;
       const int rho = it / kGroups;
-      if (!mbar_wait(&full_l[s], (it / SL) & 1, args.status, kStatusGemmDequantTimeout,
+      if (!mbar_wait(&full_l[pr], ((it >> 1) / NP) & 1, args.status, kStatusGemmDequantTimeout,
                      abort_flag))
         break;
-      const uint32_t wb = l_base + s * Plan::kStage;
+      const uint32_t wb = l_base + pr * Plan::kPair + (it & 1) * BLOB;
       uint4 p[4] = {};
       __nv_bfloat162 s2[4] = {};
       if (!(args.diag & 8)) {
@@ -744,7 +790,7 @@ void launch_w4a16(const CUtensorMap& tmap, const GemmArgs& a, dim3 grid, cudaStr
 
 template <int MT, int GS, int EPI>
 void launch_persistent(const CUtensorMap& tmap, const GemmArgs& a, int ctas, cudaStream_t stream) {
-  using Plan = SmemPlan<MT, GS>;
+  using Plan = PairPlan<MT, GS>;
   static bool configured = false;
   if (!configured) {
     CB_CUDA_CHECK(cudaFuncSetAttribute(w4a16_persistent_kernel<MT, GS, EPI>,
@@ -767,9 +813,12 @@ void dispatch_persistent(int MT, const CUtensorMap& tmap, const GemmArgs& a, int
 
 template <int GS, int EPI>
 void dispatch_mt(int MT, const CUtensorMap& tmap, const GemmArgs& a, dim3 grid, cudaStream_t s) {
-  // Token tiles up to 64 run the persistent kernel; this one serves 128.
-  (void)MT;
-  launch_w4a16<128, GS, EPI>(tmap, a, grid, s);
+  switch (MT) {
+    case 16: launch_w4a16<16, GS, EPI>(tmap, a, grid, s); break;
+    case 32: launch_w4a16<32, GS, EPI>(tmap, a, grid, s); break;
+    case 64: launch_w4a16<64, GS, EPI>(tmap, a, grid, s); break;
+    default: launch_w4a16<128, GS, EPI>(tmap, a, grid, s); break;
+  }
 }
 
 static int pick_mt(int M) {
@@ -819,22 +868,13 @@ static GemmPlanInfo plan_gemm(int M, int N, int K, int forced_splits) {
   splits = std::max(1, std::min(splits, KB));
   p.kbps = (KB + splits - 1) / splits;
   p.splits = (KB + p.kbps - 1) / p.kbps;
-  // Decode-sized token tiles use the persistent stream-K kernel.
-  static const bool no_persist = [] {
-    const char* e = std::getenv("CASCADIA_GEMM_NO_PERSIST");
+  // The persistent stream-K kernel is opt-in (CASCADIA_GEMM_PERSIST=1): on
+  // B200 the per-k-block split-K kernel measured faster for every decode shape.
+  static const bool persist = [] {
+    const char* e = std::getenv("CASCADIA_GEMM_PERSIST");
     return e != nullptr && std::atoi(e) != 0;
   }();
-  p.persistent = p.MT <= 64 && forced_splits <= 0 && !no_persist;
-  if (!p.persistent && p.MT < 128) {
-    // The split-K (non-persistent) kernel is instantiated for 128-token tiles.
-    p.MT = 128;
-    p.token_tiles = (M + 127) / 128;
-    splits = forced_splits > 0 ? forced_splits
-                               : pick_splits(p.row_tiles * p.token_tiles, KB, num_sms());
-    splits = std::max(1, std::min(splits, KB));
-    p.kbps = (KB + splits - 1) / splits;
-    p.splits = (KB + p.kbps - 1) / p.kbps;
-  }
+  p.persistent = p.MT <= 64 && forced_splits <= 0 && persist;
   p.units = p.row_tiles * p.token_tiles * KB;
   p.ctas = std::min(num_sms(), p.units);
   p.ub = p.units / p.ctas;
