@@ -42,6 +42,8 @@ def parse():
     p.add_argument("--ttft-reps", type=int, default=5)
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--layers", type=int, default=0, help="debug only: override layer count")
+    p.add_argument("--tp-comm", default="fused", choices=["fused", "nccl"],
+                   help="row-parallel all-reduce: peer-memory fused kernel or NCCL")
     return p.parse_args()
 
 
@@ -140,6 +142,10 @@ def main():
     if args.layers:
         cfg.num_layers = args.layers
     tp = TPGroup(rank, world, group)
+    if world > 1 and args.tp_comm == "fused":
+        from cascadia_b200.parallel.tp import FusedTP
+
+        tp.fused = FusedTP(group, rank, world, dev, cfg.hidden_size, max(64, args.batch))
     t0 = time.time()
     model = LlamaModel(cfg, dev, tp=tp).init_random(seed=1234)
     torch.cuda.synchronize()
@@ -254,6 +260,7 @@ def main():
             "config": {"model": args.model + (f"-L{args.layers}" if args.layers else ""),
                        "global_batch": B, "seq_len": P, "decode_context": f"{P}..{P + args.warmup + 2 * args.steps}",
                        "parallelism": f"tp{world}", "kv_block": BLOCK_SIZE,
+                       "tp_comm": args.tp_comm if world > 1 else None,
                        "l2": "inputs larger than L2 (weights+KV >> 126 MB)",
                        "cuda_graph": graph.graph is not None},
             "ttft_p50_ms": round(ttft, 3),

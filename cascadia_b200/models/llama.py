@@ -72,10 +72,15 @@ class LayerWeights:
 
 
 class TPGroup:
-    """Tensor-parallel communicator used by the models (NCCL baseline path)."""
+    """Tensor-parallel communicator used by the models.
+
+    NCCL all-reduce is the baseline (and prefill) path; when ``fused`` is set
+    (parallel.tp.FusedTP), decode-sized batches use the peer-memory
+    all-reduce + RMSNorm kernel instead."""
 
     def __init__(self, rank: int = 0, size: int = 1, group=None):
         self.rank, self.size, self.group = rank, size, group
+        self.fused = None
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         if self.size > 1:
@@ -239,6 +244,9 @@ class LlamaModel:
         cfg = self.cfg
         T = hidden.shape[0]
         h = torch.empty_like(hidden)
+        fz = self.tp.fused
+        if fz is not None and self.device.type == "cuda" and T <= fz.max_tokens:
+            return self._forward_fused(batch, hidden, h, fz)
         pending: Optional[torch.Tensor] = None  # TP partial sum not yet added
         tp1 = self.tp.size == 1
         for i, lw in enumerate(self.layers):
@@ -261,6 +269,25 @@ class LlamaModel:
         if pending is not None:
             hidden.copy_((hidden.float() + pending.float()).to(torch.bfloat16)) \
                 if self.device.type != "cuda" else hidden.add_(pending)
+        return hidden
+
+    def _forward_fused(self, batch, hidden, h, fz):
+        """TP forward with the peer-memory all-reduce fused into RMSNorm: the
+        row-parallel GEMMs write partials into the symmetric buffer; each
+        all-reduce also applies the next norm (post-attention norm after
+        o_proj, the next layer's input norm after down_proj)."""
+        T = hidden.shape[0]
+        eps = self.cfg.rms_eps
+        self._norm(hidden, self.layers[0].in_norm, h)
+        for i, lw in enumerate(self.layers):
+            qkv = lw.qkv(h)
+            attn = self._attention(i, qkv, batch)
+            lw.o(attn, out=fz.partial_out(0, T))
+            fz.allreduce(0, T, hidden, lw.post_norm, h, eps)
+            act = lw.gate_up(h, ops.EPI_SILU)
+            lw.down(act, out=fz.partial_out(1, T))
+            nxt = self.layers[i + 1].in_norm if i + 1 < len(self.layers) else None
+            fz.allreduce(1, T, hidden, nxt, h if nxt is not None else h, eps)
         return hidden
 
     def _attention(self, li: int, qkv: torch.Tensor, batch: "Batch") -> torch.Tensor:

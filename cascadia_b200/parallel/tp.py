@@ -1,0 +1,61 @@
+"""Tensor-parallel communication for the dense model.
+
+Two paths, same semantics (sum of row-parallel partials over the TP group):
+
+* ``TPGroup`` (models.llama): NCCL all-reduce, the baseline / prefill path;
+* ``FusedTP``: our ``ar_rmsnorm`` kernel over NVLink peer memory.  The
+  row-parallel GEMM writes its partial straight into a symmetric buffer (the
+  same allocation mapped on every GPU of the group); one kernel then signals,
+  waits (bounded) for the peers, sums the partials with P2P loads, adds the
+  residual and applies the next RMSNorm.  Used for decode-sized token counts.
+
+Symmetric allocation and peer mapping come from
+``torch.distributed._symmetric_memory`` (plumbing only: no torch collective
+runs on this path).  The signal pad is our own zeroed int32 symmetric tensor.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+
+
+class FusedTP:
+    def __init__(self, group, rank: int, world: int, device, hidden: int, max_tokens: int = 256):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.rank, self.world = rank, world
+        self.dev = torch.device(device)
+        self.hidden = hidden
+        self.max_tokens = max_tokens
+        self.buf = symm_mem.empty((2, max_tokens, hidden), dtype=torch.bfloat16, device=self.dev)
+        self.buf.zero_()
+        gname = group.group_name if group is not None else dist.group.WORLD.group_name
+        hdl = symm_mem.rendezvous(self.buf, gname)
+        self.sig = symm_mem.empty((8,), dtype=torch.int32, device=self.dev)
+        self.sig.zero_()
+        shdl = symm_mem.rendezvous(self.sig, gname)
+        self.buf_ptrs = torch.tensor([int(p) for p in hdl.buffer_ptrs], dtype=torch.int64)
+        self.sig_ptrs = torch.tensor([int(p) for p in shdl.buffer_ptrs], dtype=torch.int64)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        self.done = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        self._handles = (hdl, shdl)
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=group)  # every pad is zero before anyone signals
+
+    def partial_out(self, slot: int, m: int) -> torch.Tensor:
+        return self.buf[slot, :m]
+
+    def allreduce(self, slot: int, m: int, residual: Optional[torch.Tensor],
+                  weight: Optional[torch.Tensor], out: torch.Tensor, eps: float):
+        """out = rmsnorm(residual + sum_ranks(partial[slot])) * weight; the
+        residual stream is updated in place.  weight=None: out = the sum."""
+        ops.ext().ar_rmsnorm(self.buf_ptrs, slot * self.max_tokens * self.hidden * 2,
+                             self.sig_ptrs, self.epoch, self.done,
+                             ops.status_buffer(self.dev), self.rank, self.world, m, self.hidden,
+                             residual, weight, out, eps)
+        ops.LAUNCHES.add(1)
+        return out

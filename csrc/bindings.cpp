@@ -33,6 +33,11 @@ void sample(torch::Tensor logits, torch::Tensor params, c10::optional<torch::Ten
             c10::optional<torch::Tensor> hist_len, torch::Tensor work, torch::Tensor seeds,
             torch::Tensor offsets, torch::Tensor out);
 void spec_verify(torch::Tensor target, torch::Tensor draft, torch::Tensor out);
+// comm.cu
+void ar_rmsnorm(torch::Tensor buf_ptrs, int64_t buf_offset_bytes, torch::Tensor sig_ptrs,
+                torch::Tensor epoch, torch::Tensor done, torch::Tensor status, int64_t rank,
+                int64_t world, int64_t M, int64_t H, c10::optional<torch::Tensor> residual,
+                c10::optional<torch::Tensor> w, torch::Tensor out, double eps);
 }  // namespace cb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -49,4 +54,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax", &cb::argmax);
   m.def("sample", &cb::sample);
   m.def("spec_verify", &cb::spec_verify);
+  m.def("ar_rmsnorm", &cb::ar_rmsnorm);
 }

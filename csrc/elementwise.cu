@@ -140,6 +140,21 @@ void rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tens
 // qkv: [T, (Hq + 2*Hkv) * D] (q heads, then k heads, then v heads).
 // cos_sin: [max_pos, rot] fp32, first rot/2 columns cos, last rot/2 sin.
 // Non-interleaved (rotate-half, Llama/Qwen) or interleaved pairs (GLM).
+// Vectorised: one thread rotates 8 pairs (two 16-byte loads / stores).
+__device__ __forceinline__ void load8(const bf16* p, float (&v)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const bf16* e = reinterpret_cast<const bf16*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(e[i]);
+}
+__device__ __forceinline__ void store8(bf16* p, const float (&v)[8]) {
+  uint4 u;
+  bf16* e = reinterpret_cast<bf16*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) e[i] = __float2bfloat16(v[i]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
 __global__ void rope_kv_kernel(bf16* __restrict__ qkv, int ldq, const int* __restrict__ positions,
                                const float* __restrict__ cos_sin, const int* __restrict__ slots,
                                bf16* __restrict__ k_cache, bf16* __restrict__ v_cache, int layer,
@@ -150,37 +165,76 @@ __global__ void rope_kv_kernel(bf16* __restrict__ qkv, int ldq, const int* __res
   bf16* row = qkv + (size_t)t * ldq;
   const float* cs = cos_sin + (size_t)pos * rot;
   const int half = rot / 2;
-  const int nrot = (Hq + Hkv) * half;
+  const int pieces = half / 8;  // 8 pairs per thread
+  const int nrot = (Hq + Hkv) * pieces;
+  const size_t cache_row =
+      slot >= 0 ? ((((size_t)layer * NB + slot / 16) * Hkv) * 16 + (slot % 16)) * (size_t)D : 0;
   for (int idx = threadIdx.x; idx < nrot; idx += blockDim.x) {
-    const int hh = idx / half;
-    const int i = idx % half;
+    const int hh = idx / pieces;
+    const int i0 = (idx % pieces) * 8;
     bf16* hp = row + (size_t)hh * D;
-    const int i0 = interleaved ? 2 * i : i;
-    const int i1 = interleaved ? 2 * i + 1 : i + half;
-    const float x0 = __bfloat162float(hp[i0]);
-    const float x1 = __bfloat162float(hp[i1]);
-    const float c = cs[i], s = cs[half + i];
-    const bf16 y0 = __float2bfloat16(x0 * c - x1 * s);
-    const bf16 y1 = __float2bfloat16(x1 * c + x0 * s);
+    float x0[8], x1[8], c[8], sn[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      c[k] = cs[i0 + k];
+      sn[k] = cs[half + i0 + k];
+    }
+    if (!interleaved) {
+      load8(hp + i0, x0);
+      load8(hp + half + i0, x1);
+    } else {
+      float a[8], b[8];
+      load8(hp + 2 * i0, a);
+      load8(hp + 2 * i0 + 8, b);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        x0[k] = a[2 * k];
+        x1[k] = a[2 * k + 1];
+        x0[4 + k] = b[2 * k];
+        x1[4 + k] = b[2 * k + 1];
+      }
+    }
+    float y0[8], y1[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      y0[k] = x0[k] * c[k] - x1[k] * sn[k];
+      y1[k] = x1[k] * c[k] + x0[k] * sn[k];
+    }
+    bf16* dst;
     if (hh < Hq) {
-      hp[i0] = y0;
-      hp[i1] = y1;
-    } else if (slot >= 0) {
-      const int kh = hh - Hq;
-      const size_t base =
-          ((((size_t)layer * NB + slot / 16) * Hkv + kh) * 16 + (slot % 16)) * (size_t)D;
-      k_cache[base + i0] = y0;
-      k_cache[base + i1] = y1;
+      dst = hp;
+    } else {
+      if (slot < 0) continue;
+      dst = k_cache + cache_row + (size_t)(hh - Hq) * 16 * D;
+    }
+    if (!interleaved) {
+      store8(dst + i0, y0);
+      store8(dst + half + i0, y1);
+    } else {
+      float a[8], b[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        a[2 * k] = y0[k];
+        a[2 * k + 1] = y1[k];
+        b[2 * k] = y0[4 + k];
+        b[2 * k + 1] = y1[4 + k];
+      }
+      store8(dst + 2 * i0, a);
+      store8(dst + 2 * i0 + 8, b);
     }
   }
   if (slot < 0) return;
-  // Non-rotated part of K (partial rotary) and all of V.
-  for (int idx = threadIdx.x; idx < Hkv * D; idx += blockDim.x) {
-    const int kh = idx / D;
-    const int d = idx % D;
-    const size_t base = ((((size_t)layer * NB + slot / 16) * Hkv + kh) * 16 + (slot % 16)) * (size_t)D;
-    v_cache[base + d] = row[(size_t)(Hq + Hkv + kh) * D + d];
-    if (d >= rot) k_cache[base + d] = row[(size_t)(Hq + kh) * D + d];
+  // Non-rotated part of K (partial rotary) and all of V, 8 values per thread.
+  const int vec_per_head = D / 8;
+  for (int idx = threadIdx.x; idx < Hkv * vec_per_head; idx += blockDim.x) {
+    const int kh = idx / vec_per_head;
+    const int d = (idx % vec_per_head) * 8;
+    const size_t base = cache_row + (size_t)kh * 16 * D + d;
+    *reinterpret_cast<uint4*>(v_cache + base) =
+        *reinterpret_cast<const uint4*>(row + (size_t)(Hq + Hkv + kh) * D + d);
+    if (d >= rot)
+      *reinterpret_cast<uint4*>(k_cache + base) =
+          *reinterpret_cast<const uint4*>(row + (size_t)(Hq + kh) * D + d);
   }
 }
 
@@ -190,6 +244,8 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos
   const int T = (int)qkv.size(0);
   if (T == 0) return;
   TORCH_CHECK(qkv.stride(1) == 1, "qkv inner stride must be 1");
+  TORCH_CHECK(rot % 16 == 0 && D % 8 == 0, "rotary dim must be a multiple of 16");
+  TORCH_CHECK((qkv.stride(0) * 2) % 16 == 0, "qkv rows must be 16-byte aligned");
   const c10::cuda::CUDAGuard guard(qkv.device());
   rope_kv_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<bf16*>(qkv.data_ptr()), (int)qkv.stride(0), positions.data_ptr<int>(),
@@ -210,13 +266,34 @@ __global__ void argmax_kernel(const T* __restrict__ logits, int ld, int V, int* 
   const T* x = logits + (size_t)row * ld;
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    float v;
-    if constexpr (std::is_same<T, float>::value) v = x[i];
-    else v = __bfloat162float(x[i]);
-    if (v > best || (v == best && i < bi)) {
-      best = v;
-      bi = i;
+  constexpr int VEC = 16 / sizeof(T);
+  const bool vec_ok = (V % VEC == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  if (vec_ok) {
+    // 16-byte loads; indices visited in increasing order per thread, so the
+    // lowest-index tie rule is preserved by the strict comparisons.
+    for (int i = threadIdx.x * VEC; i < V; i += blockDim.x * VEC) {
+      const uint4 u = *reinterpret_cast<const uint4*>(x + i);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) {
+        float v;
+        if constexpr (std::is_same<T, float>::value) v = e[k];
+        else v = __bfloat162float(e[k]);
+        if (v > best) {
+          best = v;
+          bi = i + k;
+        }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      float v;
+      if constexpr (std::is_same<T, float>::value) v = x[i];
+      else v = __bfloat162float(x[i]);
+      if (v > best || (v == best && i < bi)) {
+        best = v;
+        bi = i;
+      }
     }
   }
 #pragma unroll

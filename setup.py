@@ -23,6 +23,7 @@ SOURCES = [
     "gemm_w4a16.cu",
     "attention.cu",
     "elementwise.cu",
+    "comm.cu",
 ]
 
 NVCC_FLAGS = [
