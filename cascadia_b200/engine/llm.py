@@ -335,12 +335,21 @@ class LLMBuilder(Builder):
     def connect(self, peers: PeerLayout) -> None:
         pass
 
+    def model_class(self, cfg):
+        """Dense Llama-family model, or the sparse-MoE model for MoE configs."""
+        if cfg.is_moe:
+            from ..models.moe import MoEModel
+
+            return MoEModel
+        from ..models.llama import LlamaModel
+
+        return LlamaModel
+
     def load(self, shard: ShardSpec) -> Iterable[LoadProgress]:
         import os
 
         from ..api.templates import load_tokenizer
         from ..models.config import get_config
-        from ..models.llama import LlamaModel
 
         yield LoadProgress.msg(f"loading {self.model_name}")
         if os.path.isdir(self.model_name):
@@ -353,11 +362,12 @@ class LLMBuilder(Builder):
                 tok_dir = os.path.join(self.model_name, "tokenizer")
         else:
             cfg = get_config(self.model_name)
-            self.model = LlamaModel(cfg, self.device, tp=self.tp,
-                                    layer_start=shard.layer_start,
-                                    layer_end=shard.layer_end,
-                                    has_embed=shard.is_first_stage,
-                                    has_head=shard.is_last_stage).init_random(seed=self.seed)
+            self.model = self.model_class(cfg)(cfg, self.device, tp=self.tp,
+                                               layer_start=shard.layer_start,
+                                               layer_end=shard.layer_end,
+                                               has_embed=shard.is_first_stage,
+                                               has_head=shard.is_last_stage).init_random(
+                                                   seed=self.seed)
             tok_dir = self.tokenizer_path
         cfg = self.model.cfg
         self.tokenizer = load_tokenizer(tok_dir, cfg.vocab_size, cfg.eos_token_ids[0])

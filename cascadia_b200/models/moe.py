@@ -1,0 +1,236 @@
+"""Sparse-MoE decoder (Qwen3-MoE shape; Kimi-K2-style sigmoid routing and
+shared experts are supported by the same layer).
+
+Per layer: RMSNorm -> attention (bf16 projections through cuBLAS, or INT4,
+with optional per-head q/k RMSNorm) -> residual -> RMSNorm -> MoE FFN:
+
+    ids, w = topk_gate(h)                      (fused router + top-k kernel)
+    perm   = counting sort of (token, slot) by expert; gather rows
+    act    = grouped W4A16 GEMM gate_up (+SiLU epilogue), all experts, 1 launch
+    y      = grouped W4A16 GEMM down
+    out    = residual + sum_j w[t, j] * y[pos(t, j)]  (+ shared expert)
+
+Routing semantics: softmax + top-k + renormalise (Qwen3, norm_topk_prob), or
+sigmoid + bias-for-choice + top-k + renormalise x routed_scaling_factor
+(Kimi-K2 / DeepSeek-V3; reference crates/cascadia-int4-gemm/src/shell.rs:261-298).
+Expert weights are INT4 (group 128 for Qwen3, 32 for Kimi: the reference's F1
+expert format, crates/cascadia-int4-gemm/src/kernel.rs:46-70).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional
+
+import torch
+
+from .. import ops
+from ..ops import reference as ref
+from ..quant import Int4Weight
+from .config import ModelConfig, rope_table
+from .llama import Batch, LlamaModel, QLinear, TPGroup, _layer_generator, random_int4
+
+
+class BF16Linear:
+    """Plain bf16 projection (the MoE config's attention is bf16); on CUDA
+    this is a cuBLAS GEMM through torch.matmul."""
+
+    def __init__(self, w: torch.Tensor, device):
+        self.w = w.to(torch.bfloat16).to(device)
+        self.n, self.k = self.w.shape
+
+    def __call__(self, x, epilogue=ops.EPI_STORE, residual=None, out=None):
+        if self.w.device.type == "cuda":
+            y = torch.matmul(x, self.w.t())
+        else:
+            y = (x.float() @ self.w.float().t()).to(torch.bfloat16)
+        if epilogue == ops.EPI_RESID:
+            y = (y.float() + residual.float()).to(torch.bfloat16)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+
+
+class ExpertBank:
+    """All routed experts of one layer: blobs back to back (GPU) or dequantised
+    fp32 weights (CPU oracle)."""
+
+    def __init__(self, gate_up: List[Int4Weight], down: List[Int4Weight], device):
+        self.E = len(gate_up)
+        self.inter = gate_up[0].n // 2
+        self.hidden = gate_up[0].k
+        self.gs = gate_up[0].group_size
+        dev = torch.device(device)
+        if dev.type == "cuda":
+            self.gu_blob = torch.cat([w.to(dev).blob(interleave_gate_up=True) for w in gate_up])
+            self.dn_blob = torch.cat([w.to(dev).blob() for w in down])
+            self.gu_ref = self.dn_ref = None
+        else:
+            self.gu_blob = self.dn_blob = None
+            self.gu_ref = [w.dequant_bf16().float() for w in gate_up]
+            self.dn_ref = [w.dequant_bf16().float() for w in down]
+
+
+@dataclass
+class MoELayer:
+    in_norm: torch.Tensor
+    post_norm: torch.Tensor
+    qkv: object
+    o: object
+    q_norm: Optional[torch.Tensor]
+    k_norm: Optional[torch.Tensor]
+    dense: Optional[tuple]            # (gate_up QLinear, down QLinear) for dense layers
+    router: Optional[torch.Tensor]    # [E, H] bf16
+    router_bias: Optional[torch.Tensor]
+    experts: Optional[ExpertBank]
+    shared: Optional[tuple]           # (gate_up QLinear, down QLinear)
+
+
+class MoEModel(LlamaModel):
+    def __init__(self, cfg: ModelConfig, device, tp: Optional[TPGroup] = None,
+                 layer_start: int = 0, layer_end: Optional[int] = None,
+                 has_embed: bool = True, has_head: bool = True, bf16_attention: bool = True):
+        super().__init__(cfg, device, tp, layer_start, layer_end, has_embed, has_head)
+        assert self.tp.size == 1, "MoE model: expert parallelism replaces TP (see parallel.ep)"
+        self.bf16_attention = bf16_attention
+        self.layers: List[MoELayer] = []
+
+    def init_random(self, seed: int = 0, std: float = 0.02, gen_device=None):
+        cfg = self.cfg
+        dev = torch.device(gen_device) if gen_device is not None else self.device
+        gs = cfg.group_size
+        h, d = cfg.hidden_size, cfg.head_dim
+        self.cos_sin = rope_table(cfg, min(cfg.max_position, 1 << 16), device=self.device)
+        if self.has_embed or (self.has_head and cfg.tie_word_embeddings):
+            g = _layer_generator(seed, 100000, dev)
+            self.embed = (torch.randn(cfg.vocab_size, h, generator=g, device=dev) * std).to(
+                torch.bfloat16).to(self.device)
+        ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=self.device)  # noqa: E731
+        for li in range(self.layer_start, self.layer_end):
+            g = _layer_generator(seed, li, dev)
+            qkv_rows = (cfg.num_heads + 2 * cfg.num_kv_heads) * d
+            if self.bf16_attention:
+                qkv = BF16Linear(torch.randn(qkv_rows, h, generator=g, device=dev) * std,
+                                 self.device)
+                o = BF16Linear(torch.randn(h, cfg.num_heads * d, generator=g, device=dev) * std,
+                               self.device)
+            else:
+                qkv = QLinear(random_int4(qkv_rows, h, g, dev, std, gs), self.device)
+                o = QLinear(random_int4(h, cfg.num_heads * d, g, dev, std, gs), self.device)
+            dense = router = bias = bank = shared = None
+            if li < cfg.first_k_dense_replace:
+                I = cfg.intermediate_size
+                gu = Int4Weight.cat_rows([random_int4(I, h, g, dev, std, gs),
+                                          random_int4(I, h, g, dev, std, gs)])
+                dense = (QLinear(gu, self.device, interleave_gate_up=True),
+                         QLinear(random_int4(h, I, g, dev, std, gs), self.device))
+            else:
+                I = cfg.moe_intermediate_size
+                router = (torch.randn(cfg.num_experts, h, generator=g, device=dev) * std).to(
+                    torch.bfloat16).to(self.device)
+                if cfg.router == "sigmoid":
+                    bias = (torch.randn(cfg.num_experts, generator=g, device=dev) * 0.1).float().to(
+                        self.device)
+                gus, dns = [], []
+                for _ in range(cfg.num_experts):
+                    gus.append(Int4Weight.cat_rows([random_int4(I, h, g, dev, std, gs),
+                                                    random_int4(I, h, g, dev, std, gs)]))
+                    dns.append(random_int4(h, I, g, dev, std, gs))
+                bank = ExpertBank(gus, dns, self.device)
+                del gus, dns
+                if cfg.num_shared_experts:
+                    Is = I * cfg.num_shared_experts
+                    gu = Int4Weight.cat_rows([random_int4(Is, h, g, dev, std, gs),
+                                              random_int4(Is, h, g, dev, std, gs)])
+                    shared = (QLinear(gu, self.device, interleave_gate_up=True),
+                              QLinear(random_int4(h, Is, g, dev, std, gs), self.device))
+            self.layers.append(MoELayer(
+                in_norm=ones(h), post_norm=ones(h), qkv=qkv, o=o,
+                q_norm=ones(d) if cfg.qk_norm else None, k_norm=ones(d) if cfg.qk_norm else None,
+                dense=dense, router=router, router_bias=bias, experts=bank, shared=shared))
+        if self.has_head:
+            self.final_norm = ones(h)
+            g = _layer_generator(seed, 100001, dev)
+            self.lm_head = QLinear(random_int4(cfg.vocab_size, h, g, dev, std, gs), self.device)
+        return self
+
+    # ------------------------------------------------------------ forward
+    def forward(self, batch: Batch, hidden: torch.Tensor) -> torch.Tensor:
+        h = torch.empty_like(hidden)
+        for i, lw in enumerate(self.layers):
+            self._norm(hidden, lw.in_norm, h)
+            qkv = lw.qkv(h)
+            if lw.q_norm is not None:
+                self._qk_norm(qkv, lw)
+            attn = self._attention(i, qkv, batch)
+            lw.o(attn, ops.EPI_RESID, residual=hidden, out=hidden)
+            self._norm(hidden, lw.post_norm, h)
+            if lw.dense is not None:
+                act = lw.dense[0](h, ops.EPI_SILU)
+                lw.dense[1](act, ops.EPI_RESID, residual=hidden, out=hidden)
+            else:
+                self._moe(lw, h, hidden)
+        return hidden
+
+    def _qk_norm(self, qkv: torch.Tensor, lw: MoELayer):
+        """Per-head RMSNorm of q and k (Qwen3) applied in place before RoPE."""
+        T = qkv.shape[0]
+        hq, hkv, d = self.hq, self.hkv, self.d
+        if self.device.type == "cuda":
+            ops.head_rmsnorm(qkv, lw.q_norm, lw.k_norm, hq, hkv, d, self.cfg.rms_eps)
+            return
+        for lo, nh, w in ((0, hq, lw.q_norm), (hq * d, hkv, lw.k_norm)):
+            part = qkv[:, lo:lo + nh * d]
+            x = part.float().view(T, nh, d)
+            part.copy_(ref.rmsnorm(x, w, self.cfg.rms_eps).to(torch.bfloat16).view(T, nh * d))
+
+    def _moe(self, lw: MoELayer, h: torch.Tensor, hidden: torch.Tensor):
+        cfg = self.cfg
+        k = cfg.num_experts_per_tok
+        scoring = 0 if cfg.router == "softmax" else 1
+        bank = lw.experts
+        shared_out = None
+        if lw.shared is not None:
+            shared_out = lw.shared[1](lw.shared[0](h, ops.EPI_SILU))
+        if self.device.type == "cuda":
+            ids, w = ops.moe_topk_gate(h, lw.router, k, scoring, cfg.norm_topk_prob,
+                                       cfg.routed_scaling_factor, lw.router_bias)
+            offsets, perm, inv, xp = ops.moe_permute(ids, bank.E, h)
+            T = h.shape[0]
+            act = ops.w4a16_gemm_grouped(xp, bank.gu_blob, 2 * bank.inter, bank.gs, ops.EPI_SILU,
+                                         offsets, bank.E, T)
+            y = ops.w4a16_gemm_grouped(act, bank.dn_blob, bank.hidden, bank.gs, ops.EPI_STORE,
+                                       offsets, bank.E, T)
+            add = hidden if shared_out is None else (hidden.float() + shared_out.float()).to(
+                torch.bfloat16)
+            ops.moe_combine(y, inv, w, add=add, out=hidden)
+            return
+        # CPU oracle.
+        ids, w = ref_topk_gate(h, lw.router, lw.router_bias, k, scoring, cfg.norm_topk_prob,
+                               cfg.routed_scaling_factor)
+        out = torch.zeros(h.shape[0], cfg.hidden_size)
+        for t in range(h.shape[0]):
+            for j in range(k):
+                e = int(ids[t, j])
+                gu = h[t:t + 1].float() @ bank.gu_ref[e].t()
+                a = ref.silu_mul(gu[:, :bank.inter], gu[:, bank.inter:]).to(torch.bfloat16)
+                y = (a.float() @ bank.dn_ref[e].t()).to(torch.bfloat16)
+                out[t] += float(w[t, j]) * y[0].float()
+        if shared_out is not None:
+            out += shared_out.float()
+        hidden.copy_((hidden.float() + out).to(torch.bfloat16))
+
+
+def ref_topk_gate(h, wg, bias, k, scoring, norm_topk, routed_scale):
+    logits = h.float() @ wg.float().t()
+    if scoring == 0:
+        scores = torch.softmax(logits, dim=-1)
+        sel = scores
+    else:
+        scores = torch.sigmoid(logits)
+        sel = scores + (bias.float() if bias is not None else 0.0)
+    ids = torch.topk(sel, k, dim=-1).indices
+    w = torch.gather(scores, 1, ids)
+    if norm_topk:
+        w = w / w.sum(-1, keepdim=True)
+    return ids.to(torch.int32), w * routed_scale

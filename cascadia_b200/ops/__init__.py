@@ -216,6 +216,13 @@ def rmsnorm(x, w, out, eps: float, residual=None):
     return out
 
 
+def head_rmsnorm(qkv, q_w, k_w, hq, hkv, d, eps):
+    """In-place per-head RMSNorm of the q and k heads of a fused qkv row."""
+    ext().head_rmsnorm(qkv, q_w, k_w, hq, hkv, d, eps)
+    LAUNCHES.add(1)
+    return qkv
+
+
 def rope_kv_write(qkv, positions, cos_sin, slots, k_cache, v_cache, layer, hq, hkv, d, rot,
                   interleaved=False):
     ext().rope_kv_write(qkv, positions, cos_sin, slots, k_cache, v_cache, layer, hq, hkv, d, rot,
@@ -237,5 +244,53 @@ def sample(logits, params, history, hist_len, work, seeds, offsets, out):
 
 def spec_verify(target, draft, out):
     ext().spec_verify(target, draft, out)
+    LAUNCHES.add(1)
+    return out
+
+
+# ----------------------------------------------------------------- MoE
+def moe_topk_gate(x, wg, k: int, scoring: int = 0, norm_topk: bool = True,
+                  routed_scale: float = 1.0, bias=None, logits_out=None):
+    """Router + top-k: returns (ids int32 [T, k], weights fp32 [T, k])."""
+    T = x.shape[0]
+    ids = torch.empty(T, k, dtype=torch.int32, device=x.device)
+    w = torch.empty(T, k, dtype=torch.float32, device=x.device)
+    ext().moe_topk_gate(x, wg, bias, k, scoring, norm_topk, routed_scale, ids, w, logits_out)
+    LAUNCHES.add(1)
+    return ids, w
+
+
+def moe_permute(ids, num_experts: int, x=None):
+    """Counting sort of (token, slot) pairs by expert; optionally gathers x."""
+    n = ids.numel()
+    dev = ids.device
+    offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+    perm = torch.empty(max(1, n), dtype=torch.int32, device=dev)
+    inv = torch.empty(max(1, n), dtype=torch.int32, device=dev)
+    xp = None
+    if x is not None:
+        xp = torch.empty(max(1, n), x.shape[1], dtype=x.dtype, device=dev)
+    ext().moe_permute(ids, num_experts, offsets, perm, inv, x, xp)
+    LAUNCHES.add(2 if x is not None else 1)
+    return offsets, perm, inv, xp
+
+
+def w4a16_gemm_grouped(x, blob, n: int, group_size: int, epilogue: int, offsets,
+                       num_groups: int, max_rows: int, out=None):
+    m = x.shape[0]
+    n_out = n // 2 if epilogue == EPI_SILU else n
+    if out is None:
+        out = torch.empty(m, n_out, dtype=torch.bfloat16, device=x.device)
+    ext().w4a16_gemm_grouped(x, blob, out, n, group_size, epilogue, offsets, num_groups,
+                             max_rows, status_buffer(x.device))
+    LAUNCHES.add(1)
+    return out
+
+
+def moe_combine(y, inv, w, add=None, out=None):
+    T = w.shape[0]
+    if out is None:
+        out = torch.empty(T, y.shape[1], dtype=torch.bfloat16, device=y.device)
+    ext().moe_combine(y, inv, w, add, out)
     LAUNCHES.add(1)
     return out

@@ -12,6 +12,19 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
 int64_t w4a16_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t forced_splits);
 int64_t w4a16_counter_count(int64_t M, int64_t N);
 std::vector<int64_t> w4a16_plan(int64_t M, int64_t N, int64_t K, int64_t forced_splits);
+void w4a16_gemm_grouped(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t N,
+                        int64_t group_size, int64_t epilogue, torch::Tensor group_offsets,
+                        int64_t num_groups, int64_t max_rows_per_group, torch::Tensor status);
+// moe.cu
+void moe_topk_gate(torch::Tensor x, torch::Tensor wg, c10::optional<torch::Tensor> bias,
+                   int64_t k, int64_t scoring, bool norm_topk, double routed_scale,
+                   torch::Tensor topk_ids, torch::Tensor topk_w,
+                   c10::optional<torch::Tensor> logits_out);
+void moe_permute(torch::Tensor topk_ids, int64_t E, torch::Tensor offsets, torch::Tensor perm,
+                 torch::Tensor inv, c10::optional<torch::Tensor> x,
+                 c10::optional<torch::Tensor> xp);
+void moe_combine(torch::Tensor y, torch::Tensor inv, torch::Tensor w,
+                 c10::optional<torch::Tensor> add, torch::Tensor out);
 // attention.cu
 void attn_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                  torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
@@ -33,6 +46,8 @@ void sample(torch::Tensor logits, torch::Tensor params, c10::optional<torch::Ten
             c10::optional<torch::Tensor> hist_len, torch::Tensor work, torch::Tensor seeds,
             torch::Tensor offsets, torch::Tensor out);
 void spec_verify(torch::Tensor target, torch::Tensor draft, torch::Tensor out);
+void head_rmsnorm(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, int64_t Hq,
+                  int64_t Hkv, int64_t D, double eps);
 // comm.cu
 void ar_rmsnorm(torch::Tensor buf_ptrs, int64_t buf_offset_bytes, torch::Tensor sig_ptrs,
                 torch::Tensor epoch, torch::Tensor done, torch::Tensor status, int64_t rank,
@@ -55,4 +70,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &cb::sample);
   m.def("spec_verify", &cb::spec_verify);
   m.def("ar_rmsnorm", &cb::ar_rmsnorm);
+  m.def("w4a16_gemm_grouped", &cb::w4a16_gemm_grouped);
+  m.def("moe_topk_gate", &cb::moe_topk_gate);
+  m.def("moe_permute", &cb::moe_permute);
+  m.def("moe_combine", &cb::moe_combine);
+  m.def("head_rmsnorm", &cb::head_rmsnorm);
 }

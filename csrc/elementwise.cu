@@ -255,6 +255,53 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos
   CB_CUDA_CHECK(cudaGetLastError());
 }
 
+// ------------------------------------------------------------------ q/k norm
+// Per-head RMSNorm of the q and k heads of a fused qkv row, in place (Qwen3's
+// q_norm / k_norm, applied before RoPE).  One warp per head; D <= 256.
+__global__ void head_rmsnorm_kernel(bf16* __restrict__ qkv, int ldq, const bf16* __restrict__ qw,
+                                    const bf16* __restrict__ kw, int Hq, int Hkv, int D,
+                                    float eps) {
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nw = blockDim.x / 32;
+  for (int hh = warp; hh < Hq + Hkv; hh += nw) {
+    bf16* hp = qkv + (size_t)t * ldq + (size_t)hh * D;
+    const bf16* w = hh < Hq ? qw : kw;
+    float v[8];
+    const int d0 = lane * 8;
+    const bool act = d0 < D;
+    float ss = 0.f;
+    if (act) {
+      load8(hp + d0, v);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ss += v[k] * v[k];
+    }
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / (float)D + eps);
+    if (act) {
+      float wv[8];
+      load8(w + d0, wv);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = v[k] * inv * wv[k];
+      store8(hp + d0, v);
+    }
+  }
+}
+
+void head_rmsnorm(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, int64_t Hq,
+                  int64_t Hkv, int64_t D, double eps) {
+  const int T = (int)qkv.size(0);
+  if (T == 0) return;
+  TORCH_CHECK(qkv.stride(1) == 1 && (qkv.stride(0) * 2) % 16 == 0, "qkv rows must be aligned");
+  TORCH_CHECK(D % 8 == 0 && D <= 256, "head_rmsnorm: D must be a multiple of 8, <= 256");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  head_rmsnorm_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<bf16*>(qkv.data_ptr()), (int)qkv.stride(0),
+      reinterpret_cast<const bf16*>(q_w.data_ptr()), reinterpret_cast<const bf16*>(k_w.data_ptr()),
+      (int)Hq, (int)Hkv, (int)D, (float)eps);
+  CB_CUDA_CHECK(cudaGetLastError());
+}
+
 // ------------------------------------------------------------------ argmax
 // Row-wise argmax over [M, V] logits; ties resolve to the lowest index (the
 // reference's strict `>` scan).  Optionally returns the max value too, which

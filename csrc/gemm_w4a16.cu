@@ -48,7 +48,9 @@ enum Epilogue : int { kEpiStore = 0, kEpiSilu = 1, kEpiResid = 2 };
 constexpr int kGroups = 4;                 // dequant groups (A buffers in TMEM)
 constexpr int kDequantWarps = 4 * kGroups; // each group: 4 warps = 128 rows
 constexpr int kDequantThreads = kDequantWarps * 32;
-constexpr int kThreads = 64 + kDequantThreads;  // + producer warp + MMA warp
+constexpr int kMaxIssuers = 4;                             // MMA issuing warps
+constexpr int kThreads = 64 + kDequantThreads + 32 * (kMaxIssuers - 1);
+constexpr int kMmaExtraWarp = 2 + kDequantWarps;           // issuers 1.. live here
 constexpr uint32_t kACols = 64;            // TMEM columns of one 128x128 bf16 A tile
 constexpr uint32_t kAccCol = kGroups * kACols;  // accumulator starts after the A buffers
 
@@ -74,6 +76,9 @@ struct SmemPlan {
   // Independent TMEM accumulators the MMAs rotate over (dependent MMAs into
   // one accumulator serialise on its read-modify-write latency).
   static constexpr int kNAcc = MT <= 32 ? 8 : MT <= 64 ? 4 : 2;
+  // MMA issuing warps (one accumulator each): one per dequant group when the
+  // accumulators fit next to the A buffers in TMEM.
+  static constexpr int kIssuers = MT <= 64 ? 4 : 2;
   static constexpr int kLOff = 0;
   static constexpr int kBarOff = kSL * kStage;
   static constexpr int kTileBytes = 128 * (MT + 1) * 4;
@@ -100,6 +105,12 @@ struct GemmArgs {
   int diag;
   // Persistent (stream-K) kernel only.
   int row_tiles, units, ub, ur, max_contrib;
+  // Grouped mode (MoE experts): blockIdx.z = expert * group_tiles + tile; the
+  // expert's token rows are [group_offsets[e], group_offsets[e + 1]) of X and
+  // Y, its weights start at wblob + e * group_blob_stride.
+  const int* group_offsets;
+  long long group_blob_stride;
+  int group_tiles;
 };
 
 template <int MT, int GS, int EPI>
@@ -137,6 +148,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kb0 = split * args.kb_per_split;
   const int kb1 = min(KB, kb0 + args.kb_per_split);
   const int nkb = kb1 - kb0;
+  // Token rows of this CTA: [m0, m_lim).  Grouped mode reads the expert's
+  // range from device memory; an empty tile leaves before touching anything.
+  int m0 = tt * MT, m_lim = args.M;
+  const uint8_t* wbase = args.wblob;
+  if (args.group_offsets != nullptr) {
+    const int e = blockIdx.z / args.group_tiles;
+    const int lt = blockIdx.z % args.group_tiles;
+    m0 = args.group_offsets[e] + lt * MT;
+    m_lim = args.group_offsets[e + 1];
+    wbase = args.wblob + (size_t)e * (size_t)args.group_blob_stride;
+    if (m0 >= m_lim) return;
+  }
 
   if (tid == 0) {
     for (int s = 0; s < SL; ++s) {
@@ -147,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full_a[g], 4);
       mbar_init(&empty_a[g], 1);
     }
-    mbar_init(acc_full, 1);
+    mbar_init(acc_full, SmemPlan<MT, GS>::kIssuers);  // every MMA issuer commits
     *abort_flag = 0;
     *is_last_flag = 0;
     fence_mbar_init();
@@ -166,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       prefetch_tmap(&tmap_x);
-      const uint8_t* wsrc = args.wblob + ((size_t)rt * KB + kb0) * BLOB;
+      const uint8_t* wsrc = wbase + ((size_t)rt * KB + kb0) * BLOB;
       int issued = 0;
       for (int it = 0; it < nkb; ++it) {
         const int s = it % SL;
@@ -176,8 +199,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&full_l[s], Plan::kXBytes + BLOB);
         bulk_g2s(st + Plan::kXBytes, wsrc + (size_t)it * BLOB, BLOB, &full_l[s]);
         const int k = (kb0 + it) * 128;
-        tma_load_2d(st, &tmap_x, k, tt * MT, &full_l[s]);
-        tma_load_2d(st + MT * 128, &tmap_x, k + 64, tt * MT, &full_l[s]);
+        tma_load_2d(st, &tmap_x, k, m0, &full_l[s]);
+        tma_load_2d(st + MT * 128, &tmap_x, k + 64, m0, &full_l[s]);
         ++issued;
       }
       // Drain: never leave the CTA while our copies still write into smem.
@@ -185,10 +208,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&full_l[it % SL], (it / SL) & 1, nullptr, 0, nullptr);
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      for (int it = 0; it < nkb; ++it) {
+  } else if (warp == 1 || warp >= kMmaExtraWarp) {
+    // ------------------------------------------------------------ MMA issuers
+    // Several issuing warps take k-blocks round-robin, each into its own
+    // accumulator: the issue latency of one thread (measured ~64 cycles per
+    // tcgen05.mma) does not bound the k-block rate.
+    constexpr int NI = Plan::kIssuers;
+    const int who = warp == 1 ? 0 : warp - kMmaExtraWarp + 1;
+    if (lane == 0 && who < NI) {
+      for (int it = who; it < nkb; it += NI) {
         const int s = it % SL;
         const uint32_t phl = (it / SL) & 1;
         const int g = it % kGroups;
@@ -198,13 +226,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t a_tm = tmem_base + g * kACols;
         const uint32_t x_addr = smem_u32(l_smem + s * Plan::kStage);
+        const uint32_t d_tm = tmem_acc + who * MT;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           if (args.diag & 2) break;
           const uint64_t db = umma_desc_sw128(x_addr + (kk >> 2) * (MT * 128) + (kk & 3) * 32);
-          const int j = it * 8 + kk;                 // global MMA index
-          const int acc = j % Plan::kNAcc;
-          mma_bf16_ts(tmem_acc + acc * MT, a_tm + kk * 8, db, kIdesc, j >= Plan::kNAcc ? 1u : 0u);
+          mma_bf16_ts(d_tm, a_tm + kk * 8, db, kIdesc, (it < NI && kk == 0) ? 0u : 1u);
         }
         mma_commit(&empty_a[g]);
         mma_commit(&empty_l[s]);
@@ -285,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int cg = grp;                   // which quarter of the MT columns
     const int row = r;                    // weight row inside the tile
     const int n0 = rt * 128;
-    const int m_base = tt * MT;
+    const int m_base = m0;
     const int Mpad = gridDim.z * MT;
     constexpr int CQ = MT / 4;            // columns per warp
     tc_fence_after();
@@ -300,8 +327,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = 0.f;
-        // Only accumulators that received at least one MMA hold data.
-        const int nacc = min(Plan::kNAcc, nkb * 8);
+        // One accumulator per MMA issuer that received a k-block.
+        const int nacc = min(Plan::kIssuers, nkb);
 #pragma unroll 1
         for (int ai = 0; ai < nacc; ++ai) {
           const uint32_t ad = lane_addr + ai * MT + c0;
@@ -370,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int j = idx & 63;
             const int m = idx >> 6;
             const int gm = m_base + m;
-            if (gm < args.M) {
+            if (gm < m_lim) {
               const float g = tile[(2 * j) * (MT + 1) + m];
               const float u = tile[(2 * j + 1) * (MT + 1) + m];
               const float y = g / (1.f + __expf(-g)) * u;
@@ -382,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int rr = idx & 127;
             const int m = idx >> 7;
             const int gm = m_base + m;
-            if (gm < args.M) {
+            if (gm < m_lim) {
               float y = tile[rr * (MT + 1) + m];
               if constexpr (EPI == kEpiResid)
                 y += __bfloat162float(args.residual[(size_t)gm * args.ldr + n0 + rr]);
@@ -926,7 +953,7 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
     TORCH_CHECK(ws.numel() >= (int64_t)p.splits * p.token_tiles * p.MT * N, "workspace too small");
     TORCH_CHECK(counters.numel() >= (int64_t)p.token_tiles * p.row_tiles, "counters too small");
   }
-  GemmArgs a;
+  GemmArgs a{};
   a.wblob = wblob.data_ptr<uint8_t>();
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   a.residual = residual.has_value()
@@ -979,6 +1006,52 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
     if (epilogue == kEpiStore) dispatch_mt<32, kEpiStore>(p.MT, tmap, a, grid, stream);
     else if (epilogue == kEpiSilu) dispatch_mt<32, kEpiSilu>(p.MT, tmap, a, grid, stream);
     else dispatch_mt<32, kEpiResid>(p.MT, tmap, a, grid, stream);
+  }
+}
+
+// Grouped (MoE) GEMM: x holds the tokens of all experts in expert order,
+// group_offsets [E + 1] (device) gives each expert's row range, wblob holds E
+// weight blobs of identical shape back to back.  max_rows_per_group bounds
+// the tiles launched per expert (CTAs of empty tiles exit at once).
+void w4a16_gemm_grouped(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t N,
+                        int64_t group_size, int64_t epilogue, torch::Tensor group_offsets,
+                        int64_t num_groups, int64_t max_rows_per_group, torch::Tensor status) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(1) == 1, "x");
+  TORCH_CHECK(epilogue != kEpiResid, "grouped GEMM supports store and SiLU epilogues");
+  const int M = (int)x.size(0);
+  const int K = (int)x.size(1);
+  TORCH_CHECK(K % 128 == 0 && N % 128 == 0, "K and N must be multiples of 128");
+  const int64_t per =
+      (int64_t)(N / 128) * (K / 128) * (8192 + 128 * (128 / group_size) * 2);
+  TORCH_CHECK(wblob.numel() == per * num_groups, "weight blob has wrong size");
+  if (M == 0 || num_groups == 0) return;
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int MT = pick_mt((int)std::max<int64_t>(1, max_rows_per_group));
+  const int tiles = (int)((max_rows_per_group + MT - 1) / MT);
+  GemmArgs a{};
+  a.wblob = wblob.data_ptr<uint8_t>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.status = status.data_ptr<int>();
+  a.M = M;
+  a.N = (int)N;
+  a.K = K;
+  a.ldo = (int)out.stride(0);
+  a.kb_per_split = K / 128;
+  a.splits = 1;
+  a.group_offsets = group_offsets.data_ptr<int>();
+  a.group_blob_stride = per;
+  a.group_tiles = tiles;
+  CUtensorMap tmap = make_tmap_2d_bf16(x.data_ptr(), (uint64_t)K, (uint64_t)M,
+                                       (uint64_t)x.stride(0) * 2, 64, (uint32_t)MT,
+                                       CU_TENSOR_MAP_SWIZZLE_128B);
+  dim3 grid((unsigned)(N / 128), 1, (unsigned)(num_groups * tiles));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (group_size == 128) {
+    if (epilogue == kEpiStore) dispatch_mt<128, kEpiStore>(MT, tmap, a, grid, stream);
+    else dispatch_mt<128, kEpiSilu>(MT, tmap, a, grid, stream);
+  } else {
+    if (epilogue == kEpiStore) dispatch_mt<32, kEpiStore>(MT, tmap, a, grid, stream);
+    else dispatch_mt<32, kEpiSilu>(MT, tmap, a, grid, stream);
   }
 }
 

@@ -24,6 +24,7 @@ SOURCES = [
     "attention.cu",
     "elementwise.cu",
     "comm.cu",
+    "moe.cu",
 ]
 
 NVCC_FLAGS = [
