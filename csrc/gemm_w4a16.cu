@@ -1062,3 +1062,204 @@ std::vector<int64_t> w4a16_plan(int64_t M, int64_t N, int64_t K, int64_t forced_
 }
 
 }  // namespace cb
+
+// ------------------------------------------------------------------ no-alloc entry point
+// The C entry point declared in gemm_w4a16_noalloc.h: the same kernels as
+// w4a16_gemm, with the split-K scratch (fp32 partials, per-tile counters and
+// a status word) in a fixed file-scope device array instead of caller tensors.
+#include "gemm_w4a16_noalloc.h"
+
+#include <cstring>
+
+namespace {
+
+constexpr size_t kNaWsBytes = size_t(CB_NOALLOC_MAX_WS_FLOATS) * 4;
+constexpr size_t kNaCounterBytes = size_t(CB_NOALLOC_MAX_COUNTERS) * 4;
+constexpr size_t kNaStatusOff = kNaWsBytes + kNaCounterBytes;
+static_assert(kNaStatusOff + 256 == CB_NOALLOC_SCRATCH_BYTES, "scratch layout");
+
+}  // namespace
+
+// In host code this name is only a stand-in: the device address comes from
+// cudaGetSymbolAddress, once per device.
+static __device__ __align__(256) unsigned char cb_noalloc_scratch[CB_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kNaMaxDevices = 64;
+std::mutex g_na_mu;
+unsigned char* g_na_base[kNaMaxDevices] = {};
+
+void na_error(char* err, int err_len, const std::string& msg) {
+  if (err == nullptr || err_len <= 0) return;
+  const size_t n = std::min(msg.size(), (size_t)err_len - 1);
+  std::memcpy(err, msg.data(), n);
+  err[n] = '\0';
+}
+
+template <int GS, int EPI>
+cudaError_t na_set_attrs() {
+  cudaError_t e = cudaSuccess;
+  auto set = [&](const void* f, int bytes) {
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  };
+  set((const void*)cb::w4a16_gemm_kernel<16, GS, EPI>, cb::SmemPlan<16, GS>::kTotal);
+  set((const void*)cb::w4a16_gemm_kernel<32, GS, EPI>, cb::SmemPlan<32, GS>::kTotal);
+  set((const void*)cb::w4a16_gemm_kernel<64, GS, EPI>, cb::SmemPlan<64, GS>::kTotal);
+  set((const void*)cb::w4a16_gemm_kernel<128, GS, EPI>, cb::SmemPlan<128, GS>::kTotal);
+  set((const void*)cb::w4a16_persistent_kernel<16, GS, EPI>, cb::PairPlan<16, GS>::kTotal);
+  set((const void*)cb::w4a16_persistent_kernel<32, GS, EPI>, cb::PairPlan<32, GS>::kTotal);
+  set((const void*)cb::w4a16_persistent_kernel<64, GS, EPI>, cb::PairPlan<64, GS>::kTotal);
+  return e;
+}
+
+// Set-up for the current device (once): scratch address, kernel attributes
+// (they are per device) and the tensor-map encoder.
+cudaError_t na_setup(int dev, unsigned char** base, std::string* why) {
+  std::lock_guard<std::mutex> lk(g_na_mu);
+  if (g_na_base[dev] != nullptr) {
+    *base = g_na_base[dev];
+    return cudaSuccess;
+  }
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, cb_noalloc_scratch);
+  if (e != cudaSuccess) {
+    *why = "cudaGetSymbolAddress";
+    return e;
+  }
+  const cudaError_t attrs[] = {
+      na_set_attrs<128, cb::kEpiStore>(), na_set_attrs<128, cb::kEpiSilu>(),
+      na_set_attrs<128, cb::kEpiResid>(), na_set_attrs<32, cb::kEpiStore>(),
+      na_set_attrs<32, cb::kEpiSilu>(),  na_set_attrs<32, cb::kEpiResid>()};
+  for (cudaError_t a : attrs)
+    if (a != cudaSuccess) {
+      *why = "cudaFuncSetAttribute";
+      return a;
+    }
+  try {
+    (void)cb::encode_tiled_fn();
+  } catch (const std::exception& ex) {
+    *why = ex.what();
+    return cudaErrorUnknown;
+  }
+  g_na_base[dev] = static_cast<unsigned char*>(p);
+  *base = g_na_base[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int cb_w4a16_gemm_noalloc(
+    const void* x, long long ldx, const void* wblob, void* out, long long ldo,
+    const void* residual, long long ldr, int M, int N, int K, int group_size, int epilogue,
+    int* status, void* stream, char* err, int err_len) {
+  using namespace cb;
+  if (x == nullptr || wblob == nullptr || out == nullptr || M < 0 || N <= 0 || K <= 0 ||
+      N % 128 != 0 || K % 128 != 0 || (group_size != 128 && group_size != 32) ||
+      epilogue < kEpiStore || epilogue > kEpiResid || ldx < K ||
+      ldo < (epilogue == kEpiSilu ? N / 2 : N) || (ldx * 2) % 16 != 0 ||
+      (reinterpret_cast<uintptr_t>(x) & 15) != 0 ||
+      (epilogue == kEpiResid && (residual == nullptr || ldr < N))) {
+    na_error(err, err_len,
+             "cb_w4a16_gemm_noalloc: invalid argument (K, N multiples of 128; group size 128 or "
+             "32; x 16-byte aligned with 16-byte row pitch; residual needed for epilogue 2)");
+    return CB_NOALLOC_EINVAL;
+  }
+  if (M == 0) return CB_NOALLOC_OK;
+  // The plan (tile size, k-splits) and its scratch need, exactly as w4a16_gemm.
+  const GemmPlanInfo p = plan_gemm(M, N, K, 0);
+  const bool split = p.splits > 1 || p.persistent;
+  const long long ws_floats =
+      p.persistent ? (long long)p.row_tiles * p.token_tiles * p.max_contrib * p.MT * 128
+                   : (p.splits > 1 ? (long long)p.splits * p.token_tiles * p.MT * N : 0);
+  const long long counters = split ? (long long)p.token_tiles * p.row_tiles : 0;
+  if (ws_floats > (long long)CB_NOALLOC_MAX_WS_FLOATS ||
+      counters > (long long)CB_NOALLOC_MAX_COUNTERS) {
+    na_error(err, err_len,
+             "cb_w4a16_gemm_noalloc: M=" + std::to_string(M) + " N=" + std::to_string(N) +
+                 " K=" + std::to_string(K) + " needs " + std::to_string(ws_floats) +
+                 " scratch floats and " + std::to_string(counters) +
+                 " counters; the fixed maximum is " + std::to_string(CB_NOALLOC_MAX_WS_FLOATS) +
+                 " floats and " + std::to_string(CB_NOALLOC_MAX_COUNTERS) + " counters");
+    return CB_NOALLOC_ETOOBIG;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess && (dev < 0 || dev >= kNaMaxDevices)) e = cudaErrorInvalidDevice;
+  if (e != cudaSuccess) {
+    na_error(err, err_len, std::string("cb_w4a16_gemm_noalloc: cudaGetDevice: ") +
+                               cudaGetErrorString(e));
+    return CB_NOALLOC_ECUDA;
+  }
+  unsigned char* base = nullptr;
+  std::string why;
+  e = na_setup(dev, &base, &why);
+  if (e != cudaSuccess) {
+    na_error(err, err_len, "cb_w4a16_gemm_noalloc: set-up failed in " + why + ": " +
+                               cudaGetErrorString(e));
+    return CB_NOALLOC_ECUDA;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* ws = reinterpret_cast<float*>(base);
+  int* ctr = reinterpret_cast<int*>(base + kNaWsBytes);
+  int* st = status != nullptr ? status : reinterpret_cast<int*>(base + kNaStatusOff);
+  // What must start at zero: the tile counters this plan uses and (when the
+  // scratch word is used) the status.  The partials are written before read.
+  if (counters > 0) e = cudaMemsetAsync(ctr, 0, (size_t)counters * 4, s);
+  if (e == cudaSuccess && status == nullptr) e = cudaMemsetAsync(st, 0, 4, s);
+  if (e != cudaSuccess) {
+    na_error(err, err_len, std::string("cb_w4a16_gemm_noalloc: cudaMemsetAsync: ") +
+                               cudaGetErrorString(e));
+    return CB_NOALLOC_ECUDA;
+  }
+  GemmArgs a{};
+  a.wblob = static_cast<const uint8_t*>(wblob);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.residual = epilogue == kEpiResid ? static_cast<const __nv_bfloat16*>(residual) : nullptr;
+  a.ldr = epilogue == kEpiResid ? (int)ldr : 0;
+  a.ws = split ? ws : nullptr;
+  a.counters = split ? ctr : nullptr;
+  a.row_tiles = p.row_tiles;
+  a.units = p.units;
+  a.ub = p.ub;
+  a.ur = p.ur;
+  a.max_contrib = p.max_contrib;
+  a.status = st;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.ldo = (int)ldo;
+  a.kb_per_split = p.kbps;
+  a.splits = p.splits;
+  try {
+    CUtensorMap tmap = make_tmap_2d_bf16(const_cast<void*>(x), (uint64_t)K, (uint64_t)M,
+                                         (uint64_t)ldx * 2, 64, (uint32_t)p.MT,
+                                         CU_TENSOR_MAP_SWIZZLE_128B);
+    if (p.persistent) {
+      if (group_size == 128) {
+        if (epilogue == kEpiStore) dispatch_persistent<128, kEpiStore>(p.MT, tmap, a, p.ctas, s);
+        else if (epilogue == kEpiSilu) dispatch_persistent<128, kEpiSilu>(p.MT, tmap, a, p.ctas, s);
+        else dispatch_persistent<128, kEpiResid>(p.MT, tmap, a, p.ctas, s);
+      } else {
+        if (epilogue == kEpiStore) dispatch_persistent<32, kEpiStore>(p.MT, tmap, a, p.ctas, s);
+        else if (epilogue == kEpiSilu) dispatch_persistent<32, kEpiSilu>(p.MT, tmap, a, p.ctas, s);
+        else dispatch_persistent<32, kEpiResid>(p.MT, tmap, a, p.ctas, s);
+      }
+    } else {
+      const dim3 grid(p.row_tiles, p.splits, p.token_tiles);
+      if (group_size == 128) {
+        if (epilogue == kEpiStore) dispatch_mt<128, kEpiStore>(p.MT, tmap, a, grid, s);
+        else if (epilogue == kEpiSilu) dispatch_mt<128, kEpiSilu>(p.MT, tmap, a, grid, s);
+        else dispatch_mt<128, kEpiResid>(p.MT, tmap, a, grid, s);
+      } else {
+        if (epilogue == kEpiStore) dispatch_mt<32, kEpiStore>(p.MT, tmap, a, grid, s);
+        else if (epilogue == kEpiSilu) dispatch_mt<32, kEpiSilu>(p.MT, tmap, a, grid, s);
+        else dispatch_mt<32, kEpiResid>(p.MT, tmap, a, grid, s);
+      }
+    }
+  } catch (const std::exception& ex) {
+    na_error(err, err_len, std::string("cb_w4a16_gemm_noalloc: ") + ex.what());
+    return CB_NOALLOC_ECUDA;
+  }
+  return CB_NOALLOC_OK;
+}
