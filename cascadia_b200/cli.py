@@ -54,6 +54,10 @@ def _common(p: argparse.ArgumentParser):
     p.add_argument("--tokenizer", default=None)
     p.add_argument("--log-level", default="info")
     p.add_argument("--max-concurrent", type=int, default=16)
+    p.add_argument("--spec", default=None, choices=["ngram", "draft"],
+                   help="speculative decoding of greedy requests")
+    p.add_argument("--spec-k", type=int, default=4, help="draft tokens per round")
+    p.add_argument("--draft-model", default=None, help="draft model preset (--spec draft)")
 
 
 def _serve(runner, api: str, model_name: str, max_concurrent: int):
@@ -84,7 +88,8 @@ def _builder(args, tp=None):
                       max_model_len=args.max_model_len,
                       prefix_cache_blocks=args.kv_prefix_cache_size,
                       use_graph=not args.no_cuda_graph, seed=args.seed, tp=tp,
-                      tokenizer_path=args.tokenizer)
+                      tokenizer_path=args.tokenizer, spec=args.spec, spec_k=args.spec_k,
+                      draft_model=args.draft_model)
 
 
 def cmd_run(args):

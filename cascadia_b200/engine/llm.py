@@ -51,7 +51,8 @@ class LLMEngine(Engine):
     def __init__(self, model, tokenizer=None, max_running: int = 64,
                  max_prefill_tokens: int = 8192, max_model_len: int = 8192,
                  use_graph: bool = True, prefix_cache_blocks: int = 0, model_id: str = "llm",
-                 max_queue: int = 1024):
+                 max_queue: int = 1024, spec: Optional[str] = None, draft_model=None,
+                 spec_k: int = 4):
         self.model = model
         self.dev = model.device
         self.cfg = model.cfg
@@ -74,6 +75,24 @@ class LLMEngine(Engine):
         # Set for the first stage of a pipeline (parallel.pp.PipelineHead):
         # the model forward then relays through the downstream stages.
         self.pipeline = None
+        # Speculative decoding of greedy sequences: "ngram" (prompt lookup)
+        # or "draft" (a small model with its own KV, ``draft_model``).
+        if spec not in (None, "ngram", "draft"):
+            raise InvalidConfig(f"unknown speculative mode {spec!r}")
+        if spec == "draft" and draft_model is None:
+            raise InvalidConfig("speculative mode 'draft' needs a draft model")
+        self.spec = spec
+        self.spec_k = spec_k
+        self.drafter = None
+        if spec == "draft":
+            from ..runtime.spec import ModelDrafter
+
+            self.drafter = ModelDrafter(draft_model, use_graph)
+        self.spec_stats = None
+        if spec is not None:
+            from ..runtime.spec import SpecStats
+
+            self.spec_stats = SpecStats()
 
     # ------------------------------------------------------------ Engine API
     def warmup(self) -> None:
@@ -113,6 +132,8 @@ class LLMEngine(Engine):
     def cancel(self, task_id: str) -> None:
         self.sched.remove(task_id)
         self.decoders.pop(task_id, None)
+        if self.drafter is not None:
+            self.drafter.release(task_id)
 
     def close(self) -> None:
         for sid in list(self.sched.by_id):
@@ -187,6 +208,14 @@ class LLMEngine(Engine):
     def _decode(self, seqs: List[Sequence], out):
         m = self.model
         kv = m.kv
+        if self.spec is not None and self.pipeline is None:
+            greedy = [s for s in seqs if s.task.temperature <= 0 and not self._has_penalty(s)]
+            if greedy:
+                self._spec_decode(greedy, out)
+                seqs = [s for s in seqs if not (s.task.temperature <= 0
+                                                and not self._has_penalty(s))]
+                if not seqs:
+                    return
         if self.dev.type != "cuda" or self.pipeline is not None:
             starts = [s.total_len - 1 for s in seqs]
             batch = build_batch(m, [s.seq_id for s in seqs], [1] * len(seqs), starts, True)
@@ -227,6 +256,52 @@ class LLMEngine(Engine):
             toks = self._pick(seqs, g.logits[:n])
         for s, t in zip(seqs, toks):
             self._emit(s, int(t), out)
+
+    def _spec_decode(self, seqs: List[Sequence], out):
+        """One speculative round for greedy sequences: draft, verify in one
+        multi-token target forward, emit the accepted tokens + correction,
+        rewind the KV to the accepted prefix."""
+        from ..runtime.spec import NGramDraft, verify_batch
+
+        m = self.model
+        k = self.spec_k
+        budget = [max(0, min(s.task.max_tokens - len(s.output_ids),
+                             self.max_model_len - s.total_len - 1) - 1) for s in seqs]
+        ids = [s.seq_id for s in seqs]
+        if self.drafter is not None:
+            maxlen = max(s.total_len for s in seqs) + k + 1
+            width = 1 << max(4, math.ceil(math.log2(-(-maxlen // BLOCK_SIZE))))
+            drafts = self.drafter.propose(ids, [s.prompt_ids + s.output_ids for s in seqs], k,
+                                          width)
+        else:
+            drafts = []
+            for s in seqs:
+                if getattr(s, "ngram", None) is None:
+                    s.ngram = NGramDraft(k)
+                    s.ngram.extend(s.prompt_ids + s.output_ids)
+                drafts.append(s.ngram.propose(k))
+        drafts = [d[:b] for d, b in zip(drafts, budget)]
+        kv_lens = [s.total_len - 1 for s in seqs]
+        results = verify_batch(m, ids, [s.output_ids[-1] for s in seqs], drafts, kv_lens)
+        st = self.spec_stats
+        st.rounds += 1
+        for s, d, acc, kl in zip(seqs, drafts, results, kv_lens):
+            a = len(acc) - 1
+            st.drafted += len(d)
+            st.accepted += a
+            st.emitted += len(acc)
+            if not s.finished:
+                m.kv.truncate(s.seq_id, kl + 1 + a)
+                if self.drafter is not None:
+                    self.drafter.accept(s.seq_id, a, k)
+            for t in acc:
+                self._emit(s, int(t), out)
+                if getattr(s, "ngram", None) is not None:
+                    s.ngram.append(int(t))
+                if s.finished:
+                    if self.drafter is not None:
+                        self.drafter.release(s.seq_id)
+                    break
 
     # ------------------------------------------------------------ sampling
     def _pick(self, seqs: List[Sequence], logits: torch.Tensor) -> List[int]:
@@ -317,7 +392,13 @@ class LLMBuilder(Builder):
     def __init__(self, model: str, device: str = "cuda", kv_blocks: int = 0,
                  kv_fraction: float = 0.5, max_running: int = 64, max_model_len: int = 8192,
                  prefix_cache_blocks: int = 0, use_graph: bool = True, seed: int = 0,
-                 tp=None, tokenizer_path: Optional[str] = None):
+                 tp=None, tokenizer_path: Optional[str] = None, spec: Optional[str] = None,
+                 spec_k: int = 4, draft_model: Optional[str] = None, draft_kv_blocks: int = 0):
+        self.spec = spec
+        self.spec_k = spec_k
+        self.draft_name = draft_model
+        self.draft_kv_blocks = draft_kv_blocks
+        self.draft = None
         self.model_name = model
         self.device = device
         self.kv_blocks = kv_blocks
@@ -381,6 +462,17 @@ class LLMBuilder(Builder):
                 blocks = max(64, (self.max_running * self.max_model_len) // BLOCK_SIZE // 4)
         self.model.allocate_kv(blocks)
         yield LoadProgress.msg(f"kv cache: {blocks} blocks")
+        if self.spec == "draft":
+            if not self.draft_name:
+                raise InvalidConfig("--spec draft needs --draft-model")
+            from ..models.llama import LlamaModel
+
+            dcfg = get_config(self.draft_name)
+            if dcfg.vocab_size != cfg.vocab_size:
+                raise InvalidConfig("draft and target vocabularies differ")
+            self.draft = LlamaModel(dcfg, self.device).init_random(seed=self.seed + 1)
+            self.draft.allocate_kv(self.draft_kv_blocks or blocks)
+            yield LoadProgress.msg(f"draft model {self.draft_name} loaded")
         yield LoadProgress.done()
 
     def build(self) -> Engine:
@@ -389,4 +481,5 @@ class LLMBuilder(Builder):
         return LLMEngine(self.model, self.tokenizer, max_running=self.max_running,
                          max_model_len=self.max_model_len, use_graph=self.use_graph,
                          prefix_cache_blocks=self.prefix_cache_blocks,
-                         model_id=self.model_name)
+                         model_id=self.model_name, spec=self.spec, draft_model=self.draft,
+                         spec_k=self.spec_k)

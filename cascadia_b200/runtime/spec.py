@@ -1,0 +1,300 @@
+"""Greedy speculative decoding over the paged-KV engine.
+
+One round for every running sequence at once (batched):
+
+1. draft up to ``k`` tokens per sequence, either with a small draft model
+   (its own paged KV; the reference pairs Llama-3.1-8B with Llama-3.2-1B,
+   crates/cascadia-engine-openvino/src/dist_spec.rs:958-1128) or with the
+   n-gram prompt-lookup table (crates/cascadia-engine-sparse-moe/src/ngram_draft.rs);
+2. verify: ONE target forward over ``[pending, d1 .. dk]`` per sequence
+   (a ragged multi-token batch through the prefill attention kernel), LM head
+   on every row, argmax per row, and the device verify kernel
+   (``ops.spec_verify``: longest accepted prefix + correction token);
+3. rewind: the target's KV length is reset to the accepted prefix (paged
+   blocks past it go back to the pool), the draft's likewise.  No data moves.
+
+Every round emits ``accepted + 1`` tokens per sequence, so the output equals
+plain greedy decoding of the target (the acceptance rule only keeps draft
+tokens the target itself would have produced).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..models.llama import build_batch
+from .kv_cache import BLOCK_SIZE
+
+MIN_NGRAM = 2
+MAX_NGRAM = 4
+DEFAULT_NGRAM_K = 8
+
+
+class NGramDraft:
+    """Prompt-lookup draft: maps each trailing 2..4-gram of the token history
+    to the token that most recently followed it; proposes by repeatedly
+    extending with the longest matching n-gram (behaviour of
+    crates/cascadia-engine-sparse-moe/src/ngram_draft.rs:42-190)."""
+
+    def __init__(self, k: int = DEFAULT_NGRAM_K):
+        self.k = max(1, min(64, k))
+        self.history: List[int] = []
+        self.table: Dict[Tuple[int, ...], int] = {}
+
+    def append(self, t: int):
+        h = self.history
+        for n in range(MIN_NGRAM, MAX_NGRAM + 1):
+            if len(h) >= n:
+                self.table[tuple(h[-n:])] = t
+        h.append(t)
+
+    def extend(self, tokens: Sequence[int]):
+        for t in tokens:
+            self.append(int(t))
+
+    def rewind(self, n: int):
+        """Drop the last n history tokens (their table entries stay)."""
+        n = min(n, len(self.history))
+        if n:
+            del self.history[-n:]
+
+    def _next(self, buf: List[int]) -> Optional[int]:
+        for n in range(MAX_NGRAM, MIN_NGRAM - 1, -1):
+            if len(buf) >= n:
+                t = self.table.get(tuple(buf[-n:]))
+                if t is not None:
+                    return t
+        return None
+
+    def propose(self, k: Optional[int] = None) -> List[int]:
+        k = self.k if k is None else k
+        buf = list(self.history[-MAX_NGRAM:])
+        out: List[int] = []
+        for _ in range(k):
+            t = self._next(buf)
+            if t is None:
+                break
+            out.append(t)
+            buf.append(t)
+        return out
+
+
+def count_accepted(drafts: Sequence[int], target: Sequence[int]) -> int:
+    """Length of the longest prefix where the draft equals the target's pick."""
+    a = 0
+    for d, t in zip(drafts, target):
+        if d != t:
+            break
+        a += 1
+    return a
+
+
+@dataclass
+class RoundReconcile:
+    history_pop: int
+    kv_rewind: int
+    new_tokens: int
+
+
+def reconcile_after_round(k_drafts: int, accepted: int, bonus_forward_ran: bool,
+                          pending_in_history: bool) -> RoundReconcile:
+    """KV / history bookkeeping of one round for a sequential (one token per
+    forward) spec loop: ``k_drafts`` drafts were pushed and forwarded (plus an
+    optional extra forward when all were accepted).  With the pending-token
+    convention the history runs one token ahead of the KV, so one slot less
+    is rewound.  (Same arithmetic as
+    crates/cascadia-engine-sparse-moe/src/spec_decode.rs:128-178; the batched
+    verify below needs only ``kv_len = kv_len + 1 + accepted``.)"""
+    assert 0 <= accepted <= k_drafts
+    writes = k_drafts + (1 if bonus_forward_ran else 0)
+    rewind = writes - accepted
+    if pending_in_history:
+        assert rewind >= 1
+        rewind -= 1
+    return RoundReconcile(history_pop=k_drafts - accepted, kv_rewind=rewind,
+                          new_tokens=accepted + 1)
+
+
+@dataclass
+class SpecState:
+    """One sequence under speculative decoding."""
+    sid: str
+    tokens: List[int]                 # prompt + generated; the last is pending
+    kv_len: int                       # target tokens with KV written
+    ngram: Optional[NGramDraft] = None
+    generated: int = 0
+    done: bool = False
+
+
+@dataclass
+class SpecStats:
+    rounds: int = 0
+    drafted: int = 0
+    accepted: int = 0
+    emitted: int = 0
+
+    @property
+    def accept_rate(self) -> float:
+        return self.accepted / self.drafted if self.drafted else 0.0
+
+
+def verify_batch(m, seq_ids: List[str], pending: List[int], drafts: List[List[int]],
+                 kv_lens: List[int]) -> List[List[int]]:
+    """One target forward over ``[pending, *drafts]`` per sequence (positions
+    from ``kv_lens``), argmax of every row, device verify.  Returns, per
+    sequence, the accepted drafts followed by the correction token.  The
+    caller rewinds the KV to ``kv_len + len(result)``."""
+    rows = [[p] + d for p, d in zip(pending, drafts)]
+    batch = build_batch(m, seq_ids, [len(r) for r in rows], kv_lens, False)
+    flat = torch.tensor([t for r in rows for t in r], dtype=torch.int32).to(m.device)
+    hidden = m.embed_tokens(flat)
+    m.forward(batch, hidden)
+    picks = m.greedy(m.head(hidden)).to(torch.int32)  # argmax of every row
+    kmax = max(len(d) for d in drafts)
+    B = len(rows)
+    if kmax == 0:
+        return [[int(t)] for t in picks.cpu()]
+    # Pad to [B, kmax+1] / [B, kmax] for the device verify kernel; padded
+    # draft slots hold -1 and never match.
+    offs = np.cumsum([0] + [len(r) for r in rows])
+    tgt_idx = np.empty((B, kmax + 1), dtype=np.int64)
+    dr = np.full((B, kmax), -1, dtype=np.int32)
+    for i in range(B):
+        n = len(rows[i])
+        tgt_idx[i, :n] = np.arange(offs[i], offs[i] + n)
+        tgt_idx[i, n:] = offs[i] + n - 1
+        dr[i, :n - 1] = drafts[i]
+    tgt = picks.index_select(0, torch.from_numpy(tgt_idx.ravel()).to(picks.device))
+    tgt = tgt.view(B, kmax + 1).contiguous()
+    if m.device.type == "cuda":
+        out = torch.empty(B, kmax + 2, dtype=torch.int32, device=m.device)
+        ops.spec_verify(tgt, torch.from_numpy(dr).to(m.device), out)
+        out = out.cpu()
+        return [out[i, :int(out[i, -1])].tolist() for i in range(B)]
+    from ..ops import reference as ref
+
+    t = tgt.cpu()
+    return [ref.spec_verify(t[i].tolist(), drafts[i]) for i in range(B)]
+
+
+class ModelDrafter:
+    """Greedy drafts from a small model with its own paged KV.  Per sequence
+    it remembers how many history tokens its KV holds; a round first feeds
+    the unseen history tail (ragged prefill, giving d1), then k-1 decode
+    steps (CUDA graphs on GPU)."""
+
+    def __init__(self, draft, use_graph: bool = True):
+        from .generator import BatchGenerator
+
+        self.model = draft
+        self.gen = BatchGenerator(draft, use_graph=use_graph)
+        self.kv_len: Dict[str, int] = {}
+
+    def propose(self, seq_ids: List[str], histories: List[List[int]], k: int,
+                width: int) -> List[List[int]]:
+        d = self.model
+        for sid in seq_ids:
+            if sid not in d.kv.seqs:
+                d.kv.add_sequence(sid)
+                self.kv_len[sid] = 0
+        starts = [self.kv_len[sid] for sid in seq_ids]
+        first = self.gen.prefill(seq_ids, [h[st:] for h, st in zip(histories, starts)], starts)
+        for sid, h in zip(seq_ids, histories):
+            self.kv_len[sid] = len(h)
+        drafts = [[int(t)] for t in first.cpu()]
+        last = [x[0] for x in drafts]
+        for _ in range(k - 1):
+            nxt = self.gen.decode(seq_ids, last, width)
+            if d.device.type == "cuda":
+                torch.cuda.current_stream(d.device).synchronize()
+            last = [int(t) for t in nxt]
+            for x, t in zip(drafts, last):
+                x.append(t)
+        return drafts
+
+    def accept(self, sid: str, accepted: int, k: int):
+        """After verify: the draft forwarded d1 .. d_{k-1}; keep the accepted
+        ones."""
+        self.kv_len[sid] += min(accepted, k - 1)
+        self.model.kv.truncate(sid, self.kv_len[sid])
+
+    def release(self, sid: str):
+        self.kv_len.pop(sid, None)
+        if sid in self.model.kv.seqs:
+            self.model.kv.free_sequence(sid)
+
+
+class SpecDecoder:
+    """Batched greedy speculative decoding of `target` with either a draft
+    model (``draft``: a model with its own KV cache) or n-gram drafts."""
+
+    def __init__(self, target, draft=None, k: int = 4, ngram_k: int = DEFAULT_NGRAM_K,
+                 use_graph: bool = True):
+        from .generator import BatchGenerator
+
+        self.target = target
+        self.k = k if draft is not None else ngram_k
+        self.tgen = BatchGenerator(target, use_graph=use_graph)
+        self.drafter = ModelDrafter(draft, use_graph) if draft is not None else None
+        self.stats = SpecStats()
+
+    def generate(self, prompts: Sequence[Sequence[int]], max_new_tokens: int,
+                 eos: Sequence[int] = (), prefix: str = "spec") -> List[List[int]]:
+        m = self.target
+        ids = [f"{prefix}{i}" for i in range(len(prompts))]
+        longest = max(len(p) for p in prompts) + max_new_tokens + self.k + 2
+        width = -(-longest // BLOCK_SIZE)
+        first = self.tgen.prefill(ids, prompts)
+        states = []
+        for sid, p, t in zip(ids, prompts, first.cpu().tolist()):
+            s = SpecState(sid, list(p) + [int(t)], kv_len=len(p), generated=1)
+            if self.drafter is None:
+                s.ngram = NGramDraft(self.k)
+                s.ngram.extend(s.tokens)
+            s.done = max_new_tokens <= 1 or int(t) in eos
+            states.append(s)
+        while True:
+            live = [s for s in states if not s.done]
+            if not live:
+                break
+            if self.drafter is not None:
+                drafts = self.drafter.propose([s.sid for s in live], [s.tokens for s in live],
+                                              self.k, width)
+            else:
+                drafts = [s.ngram.propose(self.k) for s in live]
+            # Never draft past the token budget.
+            drafts = [d[:max(0, max_new_tokens - s.generated - 1)] for s, d in zip(live, drafts)]
+            accepted = verify_batch(m, [s.sid for s in live], [s.tokens[-1] for s in live],
+                                    drafts, [s.kv_len for s in live])
+            self.stats.rounds += 1
+            for s, d, acc in zip(live, drafts, accepted):
+                a = len(acc) - 1
+                self.stats.drafted += len(d)
+                self.stats.accepted += a
+                new = acc[:max_new_tokens - s.generated]
+                for j, t in enumerate(new):
+                    if t in eos:
+                        new = new[:j + 1]
+                        break
+                s.kv_len += 1 + a
+                m.kv.truncate(s.sid, s.kv_len)
+                if self.drafter is not None:
+                    self.drafter.accept(s.sid, a, self.k)
+                s.tokens.extend(new)
+                if s.ngram is not None:
+                    s.ngram.extend(new)
+                s.generated += len(new)
+                self.stats.emitted += len(new)
+                if s.generated >= max_new_tokens or (new and new[-1] in eos):
+                    s.done = True
+        out = []
+        for s, p in zip(states, prompts):
+            out.append(s.tokens[len(p):])
+            m.kv.free_sequence(s.sid)
+            if self.drafter is not None:
+                self.drafter.release(s.sid)
+        return out
