@@ -147,7 +147,15 @@ def main():
 
         tp.fused = FusedTP(group, rank, world, dev, cfg.hidden_size, max(64, args.batch))
     t0 = time.time()
-    model = LlamaModel(cfg, dev, tp=tp).init_random(seed=1234)
+    if cfg.is_moe:
+        # Sparse-MoE configs (bf16 attention, INT4 experts); one GPU holds
+        # every expert.
+        from cascadia_b200.models.moe import MoEModel
+
+        assert world == 1, "MoE bench: one GPU per process"
+        model = MoEModel(cfg, dev).init_random(seed=1234)
+    else:
+        model = LlamaModel(cfg, dev, tp=tp).init_random(seed=1234)
     torch.cuda.synchronize()
     load_s = time.time() - t0
     B, P = args.batch, args.prompt_len
@@ -161,7 +169,7 @@ def main():
     seq_ids = [f"b{i}" for i in range(B)]
     # Prefill (untimed), in chunks to bound activation memory.
     first = []
-    chunk = max(1, 16384 // P)
+    chunk = max(1, (4096 if cfg.is_moe else 16384) // P)
     for i in range(0, B, chunk):
         first.extend(gen.prefill(seq_ids[i:i + chunk], prompts[i:i + chunk]).tolist())
     torch.cuda.synchronize()
@@ -245,7 +253,8 @@ def main():
     status = ops.read_status(dev)
     if rank == 0:
         out = {
-            "metric": METRIC,
+            "metric": METRIC if not cfg.is_moe else
+            f"decode tok/s + p50 TTFT, {args.model} (sparse MoE, INT4 experts)",
             "value": round(value, 2),
             "unit": "tokens/s",
             "n_gpus": world,
@@ -254,8 +263,9 @@ def main():
             "ms_per_step": round(ms_step, 4),
             "higher_is_better": True,
             "scaling": "strong",
-            "vs_baseline": round(value / BASELINE_TOK_S, 1),
-            "dtype": "bf16 activations, int4-g128 weights",
+            "vs_baseline": round(value / BASELINE_TOK_S, 1) if not cfg.is_moe else None,
+            "dtype": "bf16 activations, int4-g128 weights" if not cfg.is_moe else
+            f"bf16 activations and attention, int4-g{cfg.group_size} experts",
             "data": "synthetic: random-init N(0,0.02) INT4 weights, seeded uniform prompt ids",
             "config": {"model": args.model + (f"-L{args.layers}" if args.layers else ""),
                        "global_batch": B, "seq_len": P, "decode_context": f"{P}..{P + args.warmup + 2 * args.steps}",

@@ -2,8 +2,9 @@
 
     python bench/bench_gemm.py [--m 64] [--shapes qkv,o,gate_up,down,lm_head] [--reps 20]
 
-Times each GEMM with CUDA events (after warm-up; the weight set of all shapes
-rotates so each launch reads its weights from HBM, not L2) and reports
+Times each GEMM with CUDA events around a CUDA graph of `reps` launches
+(after warm-up; weight copies rotate so each launch reads its weights from
+HBM, not L2; the graph removes the host launch cost, as in decode) and reports
 achieved HBM bandwidth of the weight stream against MEASURED_PEAKS.json.
 ``--reps 1 --shapes gate_up`` gives a single launch for an ncu capture.
 """
@@ -35,6 +36,7 @@ def main():
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--copies", type=int, default=4, help="weight copies rotated per shape")
     p.add_argument("--splits", type=int, default=0)
+    p.add_argument("--graph", type=int, default=1, help="time a CUDA graph of the reps launches")
     a = p.parse_args()
     dev = torch.device("cuda", 0)
     peak = 6543.4
@@ -62,20 +64,42 @@ def main():
         for i in range(min(3, a.reps)):
             run(i)
         torch.cuda.synchronize()
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(a.reps)]
-        for i in range(a.reps):
-            ev[i][0].record()
-            run(i)
-            ev[i][1].record()
-        torch.cuda.synchronize()
-        ts = sorted(s.elapsed_time(e) * 1000 for s, e in ev)
+        if a.graph and a.reps > 1:
+            # Launch-overhead-free timing: the reps launches captured in one
+            # CUDA graph, replayed; per-launch time = replay time / reps.
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                for i in range(a.reps):
+                    run(i)
+            gr.replay()
+            torch.cuda.synchronize()
+            ts = []
+            for _ in range(5):
+                s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s0.record()
+                gr.replay()
+                s1.record()
+                torch.cuda.synchronize()
+                ts.append(s0.elapsed_time(s1) * 1000 / a.reps)
+            ts.sort()
+            del gr
+        else:
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(a.reps)]
+            for i in range(a.reps):
+                ev[i][0].record()
+                run(i)
+                ev[i][1].record()
+            torch.cuda.synchronize()
+            ts = sorted(s.elapsed_time(e) * 1000 for s, e in ev)
         med = ts[len(ts) // 2]
         nbytes = blob_bytes(n, k, 128) + a.m * k * 2 + a.m * n * 2
         plan = ops.w4a16_plan(a.m, n, k, a.splits)
         res[name] = {"us": round(med, 2), "GBps": round(nbytes / med / 1e3, 1),
                      "frac_of_measured_hbm": round(nbytes / med / 1e3 / peak, 3),
-                     "plan[MT,splits,kbps,tt,rt]": plan}
+                     "plan[MT,splits,kbps,tt,rt]": plan,
+                     "path": "small-M" if (a.splits <= 0 and a.m <= int(os.environ.get(
+                         "CASCADIA_GEMV_MAX_M", "8"))) else "tcgen05"}
         print(name, json.dumps(res[name]), flush=True)
     print("status", ops.read_status(dev))
 

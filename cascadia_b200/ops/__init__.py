@@ -142,7 +142,9 @@ def w4a16_gemm(x: torch.Tensor, blob: torch.Tensor, n: int, group_size: int = 12
                epilogue: int = EPI_STORE, residual: Optional[torch.Tensor] = None,
                out: Optional[torch.Tensor] = None, workspace: Optional[GemmWorkspace] = None,
                splits: int = 0) -> torch.Tensor:
-    """Y = X @ dequant(W)^T with a fused epilogue, on tcgen05 tensor cores."""
+    """Y = X @ dequant(W)^T with a fused epilogue.  Up to 8 rows run the
+    small-M kernel (register-fed warp MMAs), larger M the tcgen05 kernel;
+    ``splits > 0`` forces the tcgen05 kernel with that split-K factor."""
     m, k = x.shape
     e = ext()
     n_out = n // 2 if epilogue == EPI_SILU else n

@@ -15,6 +15,12 @@ std::vector<int64_t> w4a16_plan(int64_t M, int64_t N, int64_t K, int64_t forced_
 void w4a16_gemm_grouped(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t N,
                         int64_t group_size, int64_t epilogue, torch::Tensor group_offsets,
                         int64_t num_groups, int64_t max_rows_per_group, torch::Tensor status);
+// gemv_w4a16.cu
+void w4a16_gemv(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t N,
+                int64_t group_size, int64_t epilogue, c10::optional<torch::Tensor> residual,
+                torch::Tensor ws, torch::Tensor counters, torch::Tensor status,
+                int64_t forced_splits);
+int64_t gemv_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t forced_splits);
 // moe.cu
 void moe_topk_gate(torch::Tensor x, torch::Tensor wg, c10::optional<torch::Tensor> bias,
                    int64_t k, int64_t scoring, bool norm_topk, double routed_scale,
@@ -75,4 +81,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_permute", &cb::moe_permute);
   m.def("moe_combine", &cb::moe_combine);
   m.def("head_rmsnorm", &cb::head_rmsnorm);
+  m.def("w4a16_gemv", &cb::w4a16_gemv);
+  m.def("gemv_workspace_floats", &cb::gemv_workspace_floats);
 }

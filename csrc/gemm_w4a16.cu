@@ -36,6 +36,8 @@
 
 #include <cstdlib>
 #include <mutex>
+
+#include "gemv_w4a16.h"
 #include <unordered_map>
 
 #include "common.cuh"
@@ -911,7 +913,22 @@ static GemmPlanInfo plan_gemm(int M, int N, int K, int forced_splits) {
 }
 
 // Workspace floats needed for a GEMM of this shape (0 when no split).
+// Decode batches of up to CASCADIA_GEMV_MAX_M (default 8) rows run the
+// small-M kernel (gemv_w4a16.cu); 0 disables it.
+static int gemv_max_m() {
+  static const int v = [] {
+    const char* e = std::getenv("CASCADIA_GEMV_MAX_M");
+    return e ? std::atoi(e) : 8;
+  }();
+  return v;
+}
+
+static bool use_gemv(int64_t M, int64_t forced_splits) {
+  return forced_splits <= 0 && M <= gemv_max_m() && gemv_eligible(M);
+}
+
 int64_t w4a16_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t forced_splits) {
+  if (use_gemv(M, forced_splits)) return gemv_workspace_floats(M, N, K, 0);
   GemmPlanInfo p = plan_gemm((int)M, (int)N, (int)K, (int)forced_splits);
   if (p.persistent)
     return (int64_t)p.row_tiles * p.token_tiles * p.max_contrib * p.MT * 128;
@@ -944,6 +961,18 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
   TORCH_CHECK(wblob.numel() == blob_bytes, "weight blob has wrong size");
   if (M == 0) return;
   const c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(epilogue != kEpiResid || residual.has_value(), "residual epilogue needs residual");
+  if (use_gemv(M, forced_splits)) {
+    const int64_t need = gemv_workspace_floats(M, N, K, 0);
+    TORCH_CHECK(ws.numel() >= need, "workspace too small");
+    TORCH_CHECK(need == 0 || counters.numel() >= N / 128, "counters too small");
+    gemv_launch(x.data_ptr(), x.stride(0), wblob.data_ptr<uint8_t>(), out.data_ptr(),
+                out.stride(0), residual.has_value() ? residual->data_ptr() : nullptr,
+                residual.has_value() ? residual->stride(0) : 0, M, (int)N, K, (int)group_size,
+                (int)epilogue, ws.data_ptr<float>(), counters.data_ptr<int>(),
+                status.data_ptr<int>(), 0, at::cuda::getCurrentCUDAStream());
+    return;
+  }
   GemmPlanInfo p = plan_gemm(M, (int)N, K, (int)forced_splits);
   if (p.persistent) {
     TORCH_CHECK(ws.numel() >= (int64_t)p.row_tiles * p.token_tiles * p.max_contrib * p.MT * 128,

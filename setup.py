@@ -25,6 +25,7 @@ SOURCES = [
     "elementwise.cu",
     "comm.cu",
     "moe.cu",
+    "gemv_w4a16.cu",
 ]
 
 NVCC_FLAGS = [

@@ -87,6 +87,58 @@ def test_w4a16_gemm_residual(m):
     _close(y, expect)
 
 
+@pytest.mark.parametrize("m", [1, 3, 8, 9, 16])
+@pytest.mark.parametrize("gs", [128, 32])
+@pytest.mark.parametrize("epi", [0, 1, 2])
+@pytest.mark.parametrize("n,k", [(384, 1024), (256, 14336)])
+def test_w4a16_gemv_small_m(m, gs, epi, n, k):
+    """The small-M kernel (warp MMAs fed straight from registers) against the
+    fp32 reference, for every epilogue, with and without split-K."""
+    g = torch.Generator().manual_seed(m * 131 + gs + epi + k)
+    qw = Int4Weight.random(n, k, group_size=gs, generator=g, std=0.05)
+    x = (torch.randn(m, k, generator=g) * 0.5).to(torch.bfloat16)
+    r = torch.randn(m, n, generator=g).to(torch.bfloat16)
+    blob = qw.blob(interleave_gate_up=(epi == ops.EPI_SILU)).to(DEV)
+    e = ops.ext()
+    ws = ops.default_workspace(torch.device(DEV))
+    ws.ensure(e.gemv_workspace_floats(m, n, k, 0), n // 128)
+    n_out = n // 2 if epi == ops.EPI_SILU else n
+    out = torch.full((m, n_out), float("nan"), dtype=torch.bfloat16, device=DEV)
+    rd = r.to(DEV) if epi == ops.EPI_RESID else None
+    for _ in range(2):  # twice: the split-K counters must come back to zero
+        e.w4a16_gemv(x.to(DEV), blob, out, n, gs, epi, rd, ws.ws, ws.counters,
+                     ops.status_buffer(torch.device(DEV)), 0)
+    torch.cuda.synchronize()
+    _status_ok()
+    # Group 128 applies the scale in fp32 after the k-block sum (no bf16
+    # rounding of (q-8)*scale): compare against the exact fp32 dequant.
+    if gs == 128:
+        wq = (qw.unpack().float() - 8.0) * qw.scales.float().repeat_interleave(gs, dim=1)
+    else:
+        wq = qw.dequant_bf16().float()
+    full = x.float() @ wq.t()
+    if epi == ops.EPI_SILU:
+        expect = ref.silu_mul(full[:, :n // 2], full[:, n // 2:])
+    elif epi == ops.EPI_RESID:
+        expect = full + r.float()
+    else:
+        expect = full
+    _close(out, expect, rtol=1e-2, atol=2e-2)
+
+
+def test_gemv_and_tcgen05_paths_agree():
+    g = torch.Generator().manual_seed(3)
+    n, k, m = 1024, 4096, 5
+    qw = Int4Weight.random(n, k, generator=g, std=0.05)
+    x = (torch.randn(m, k, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+    blob = qw.blob().to(DEV)
+    y_small = ops.w4a16_gemm(x, blob, n)            # small-M path (M <= 8)
+    y_tc = ops.w4a16_gemm(x, blob, n, splits=4)     # forced splits: tcgen05 path
+    torch.cuda.synchronize()
+    _status_ok()
+    _close(y_small, y_tc.float(), rtol=1e-2, atol=1e-2)
+
+
 def test_rmsnorm_and_residual():
     g = torch.Generator().manual_seed(3)
     for h in (2048, 4096, 7168):
