@@ -37,6 +37,8 @@ def main():
     p.add_argument("--copies", type=int, default=4, help="weight copies rotated per shape")
     p.add_argument("--splits", type=int, default=0)
     p.add_argument("--graph", type=int, default=1, help="time a CUDA graph of the reps launches")
+    p.add_argument("--trace", action="store_true",
+                   help="tcgen05 path: print per-CTA phase times of one launch")
     a = p.parse_args()
     dev = torch.device("cuda", 0)
     peak = 6543.4
@@ -101,6 +103,29 @@ def main():
                      "path": "small-M" if (a.splits <= 0 and a.m <= int(os.environ.get(
                          "CASCADIA_GEMV_MAX_M", "8"))) else "tcgen05"}
         print(name, json.dumps(res[name]), flush=True)
+        if a.trace:
+            buf = torch.zeros(1 << 20, dtype=torch.int64, device=dev)
+            ops.ext().w4a16_set_trace(buf)
+            run(0)
+            torch.cuda.synchronize()
+            ops.ext().w4a16_set_trace(None)
+            mt, sp, _, tt, rt = plan
+            n = rt * max(sp, 1) * tt
+            tr = buf[:n * 8].view(n, 8).double().cpu()
+            t0 = tr[:, 0].min()
+            rel = tr - tr[:, :1]
+            names = ["setup", "first_w", "issued", "last_mma", "acc_ready", "partials", "end"]
+            med = {nm: round(float(rel[:, i + 1].median()) / 1000, 2) for i, nm in enumerate(names)}
+            print("  trace (us from CTA start, median over CTAs):", json.dumps(med))
+            print("  CTA start skew us: max", round(float(tr[:, 0].max() - t0) / 1000, 2),
+                  "kernel span us", round(float(tr[:, 7].max() - t0) / 1000, 2), flush=True)
+            for i, nm in enumerate(names):
+                col = rel[:, i + 1] / 1000
+                q = torch.quantile(col, torch.tensor([0.1, 0.5, 0.9, 1.0], dtype=col.dtype))
+                print(f"    {nm:10s} p10/p50/p90/max us:", [round(float(v), 2) for v in q])
+            slow = int(torch.argmax(rel[:, 7]))
+            print("    slowest CTA", slow, "(rt, split, tt) =", (slow % rt, (slow // rt) % max(sp, 1),
+                  slow // (rt * max(sp, 1))), [round(float(v) / 1000, 2) for v in rel[slow, 1:]])
     print("status", ops.read_status(dev))
 
 

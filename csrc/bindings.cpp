@@ -11,6 +11,7 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
                 int64_t forced_splits);
 int64_t w4a16_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t forced_splits);
 int64_t w4a16_counter_count(int64_t M, int64_t N);
+void w4a16_set_trace(c10::optional<torch::Tensor> buf);
 std::vector<int64_t> w4a16_plan(int64_t M, int64_t N, int64_t K, int64_t forced_splits);
 void w4a16_gemm_grouped(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t N,
                         int64_t group_size, int64_t epilogue, torch::Tensor group_offsets,
@@ -67,6 +68,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("w4a16_workspace_floats", &cb::w4a16_workspace_floats);
   m.def("w4a16_counter_count", &cb::w4a16_counter_count);
   m.def("w4a16_plan", &cb::w4a16_plan);
+  m.def("w4a16_set_trace", &cb::w4a16_set_trace);
   m.def("attn_decode", &cb::attn_decode);
   m.def("attn_prefill", &cb::attn_prefill);
   m.def("embedding", &cb::embedding);

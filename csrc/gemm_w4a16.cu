@@ -65,16 +65,22 @@ struct BlobInfo {
 
 template <int MT, int GS>
 struct SmemPlan {
-  static constexpr int kXBytes = 2 * MT * 128;  // two 64-wide K sub-tiles
-  static constexpr int kStageRaw = kXBytes + BlobInfo<GS>::kBytes;
+  static constexpr int kXBytes = 2 * MT * 128;  // one k-block of X: two 64-wide K sub-tiles
+  // A stage holds TWO consecutive k-blocks: their X tiles, then both weight
+  // blobs, which are adjacent in the blob layout and arrive with ONE bulk
+  // copy of 16.9 KiB (an SM completes about one bulk copy per ~350 ns, so
+  // 8.4 KiB copies cap the weight stream near 3.5 TB/s; 16.9 KiB ones do not).
+  static constexpr int kBlobOff = 2 * kXBytes;
+  static constexpr int kStageRaw = kBlobOff + 2 * BlobInfo<GS>::kBytes;
   static constexpr int kStage = (kStageRaw + 1023) / 1024 * 1024;
   static constexpr int kBudget = 210 * 1024;
-  // Stage count: a multiple of the number of dequant groups, so that every
-  // use of a stage is consumed by the same group (a group then never waits on
-  // a barrier more than one phase ahead of what it observed, which the
-  // mbarrier parity test could not tell apart).
-  static constexpr int kSLraw = (kBudget / kStage) / 4 * 4;
-  static constexpr int kSL = kSLraw > 16 ? 16 : kSLraw;
+  // Stage count: even, so that every use of a stage is consumed by the same
+  // two dequant groups (k-block it goes to group it % 4 and stage
+  // (it / 2) % kSL); a group then never waits on a barrier more than one
+  // phase ahead of what it observed, which the parity test could not tell
+  // apart.
+  static constexpr int kSLraw = (kBudget / kStage) / 2 * 2;
+  static constexpr int kSL = kSLraw > 8 ? 8 : kSLraw;
   // Independent TMEM accumulators the MMAs rotate over (dependent MMAs into
   // one accumulator serialise on its read-modify-write latency).
   static constexpr int kNAcc = MT <= 32 ? 8 : MT <= 64 ? 4 : 2;
@@ -84,7 +90,7 @@ struct SmemPlan {
   static constexpr int kLOff = 0;
   static constexpr int kBarOff = kSL * kStage;
   static constexpr int kTileBytes = 128 * (MT + 1) * 4;
-  static_assert(kSL >= 4 && kSL % 4 == 0, "load stages must be a positive multiple of 4");
+  static_assert(kSL >= 2 && kSL % 2 == 0, "load stages must be a positive even number");
   static_assert(kNAcc * MT <= 256, "accumulators must fit next to the A buffers in TMEM");
   static_assert(kTileBytes <= kBarOff, "epilogue tile must fit in the stage area");
   static constexpr int kTotal = kBarOff + 1024 + 1024;  // barriers + alignment slack
@@ -113,7 +119,20 @@ struct GemmArgs {
   const int* group_offsets;
   long long group_blob_stride;
   int group_tiles;
+  // Diagnostics only: when set, 8 %globaltimer stamps per CTA (start, after
+  // set-up, first weights in, all copies issued, last MMA issued,
+  // accumulators ready, partials written, end).
+  unsigned long long* trace;
+  // out (and residual) rows are 16-byte aligned: vectorised epilogue.
+  int vec_out;
 };
+
+__device__ __forceinline__ void gemm_stamp(const GemmArgs& a, int k) {
+  if (a.trace != nullptr) {
+    const size_t cta = ((size_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    a.trace[cta * 8 + k] = globaltimer();
+  }
+}
 
 template <int MT, int GS, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -164,9 +183,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   if (tid == 0) {
+    gemm_stamp(args, 0);
     for (int s = 0; s < SL; ++s) {
       mbar_init(&full_l[s], 1);
-      mbar_init(&empty_l[s], 4 + 1);  // the consuming dequant group's 4 warps + MMA commit
+      // Per k-block of the stage: the consuming dequant group's 4 warps + an
+      // MMA commit.  (A final stage holding one k-block never completes: no
+      // one waits for it again.)
+      mbar_init(&empty_l[s], 2 * (4 + 1));
     }
     for (int g = 0; g < kGroups; ++g) {
       mbar_init(&full_a[g], 4);
@@ -186,6 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t tmem_acc = tmem_base + kAccCol;
+  if (tid == 0) gemm_stamp(args, 1);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -193,21 +217,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tmap_x);
       const uint8_t* wsrc = wbase + ((size_t)rt * KB + kb0) * BLOB;
       int issued = 0;
-      for (int it = 0; it < nkb; ++it) {
-        const int s = it % SL;
-        const uint32_t ph = (it / SL) & 1;
+      const int nst = (nkb + 1) / 2;
+      for (int sti = 0; sti < nst; ++sti) {
+        const int s = sti % SL;
+        const uint32_t ph = (sti / SL) & 1;
         if (!mbar_wait(&empty_l[s], ph ^ 1, args.status, kStatusGemmLoadTimeout, abort_flag)) break;
         uint8_t* st = l_smem + s * Plan::kStage;
-        mbar_arrive_expect_tx(&full_l[s], Plan::kXBytes + BLOB);
-        bulk_g2s(st + Plan::kXBytes, wsrc + (size_t)it * BLOB, BLOB, &full_l[s]);
-        const int k = (kb0 + it) * 128;
-        tma_load_2d(st, &tmap_x, k, m0, &full_l[s]);
-        tma_load_2d(st + MT * 128, &tmap_x, k + 64, m0, &full_l[s]);
+        const int nb = min(2, nkb - 2 * sti);
+        mbar_arrive_expect_tx(&full_l[s], nb * (Plan::kXBytes + BLOB));
+        bulk_g2s(st + Plan::kBlobOff, wsrc + (size_t)(2 * sti) * BLOB, nb * BLOB, &full_l[s]);
+        for (int b = 0; b < nb; ++b) {
+          const int k = (kb0 + 2 * sti + b) * 128;
+          tma_load_2d(st + b * Plan::kXBytes, &tmap_x, k, m0, &full_l[s]);
+          tma_load_2d(st + b * Plan::kXBytes + MT * 128, &tmap_x, k + 64, m0, &full_l[s]);
+        }
         ++issued;
       }
+      gemm_stamp(args, 3);
       // Drain: never leave the CTA while our copies still write into smem.
-      for (int it = max(0, issued - SL); it < issued; ++it) {
-        mbar_wait(&full_l[it % SL], (it / SL) & 1, nullptr, 0, nullptr);
+      for (int sti = max(0, issued - SL); sti < issued; ++sti) {
+        mbar_wait(&full_l[sti % SL], (sti / SL) & 1, nullptr, 0, nullptr);
       }
     }
   } else if (warp == 1 || warp >= kMmaExtraWarp) {
@@ -219,15 +248,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int who = warp == 1 ? 0 : warp - kMmaExtraWarp + 1;
     if (lane == 0 && who < NI) {
       for (int it = who; it < nkb; it += NI) {
-        const int s = it % SL;
-        const uint32_t phl = (it / SL) & 1;
+        const int s = (it >> 1) % SL;
+        const uint32_t phl = ((it >> 1) / SL) & 1;
         const int g = it % kGroups;
         const uint32_t pha = (it / kGroups) & 1;
         if (!mbar_wait(&full_a[g], pha, args.status, kStatusGemmMmaTimeout, abort_flag)) break;
         if (!mbar_wait(&full_l[s], phl, args.status, kStatusGemmMmaTimeout, abort_flag)) break;
         tc_fence_after();
         const uint32_t a_tm = tmem_base + g * kACols;
-        const uint32_t x_addr = smem_u32(l_smem + s * Plan::kStage);
+        const uint32_t x_addr = smem_u32(l_smem + s * Plan::kStage + (it & 1) * Plan::kXBytes);
         const uint32_t d_tm = tmem_acc + who * MT;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
@@ -238,6 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&empty_a[g]);
         mma_commit(&empty_l[s]);
       }
+      if (who == 0) gemm_stamp(args, 4);
       mma_commit(acc_full);
     }
   } else {
@@ -253,18 +283,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int r = q * 32 + lane;
     const __nv_bfloat162 k136 = __floats2bfloat162_rn(136.0f, 136.0f);
-    const uint32_t l_base = smem_u32(l_smem) + Plan::kXBytes;
+    const uint32_t l_base = smem_u32(l_smem) + Plan::kBlobOff;
     const uint32_t a_tm = tmem_base + grp * kACols + ((uint32_t)(q * 32) << 16);
     bool ok = true;
     for (int it = grp; it < nkb && ok; it += kGroups) {
-      const int s = it % SL;
-      const uint32_t phl = (it / SL) & 1;
+      const int s = (it >> 1) % SL;
+      const uint32_t phl = ((it >> 1) / SL) & 1;
       const uint32_t pha = (it / kGroups) & 1;
       if (!mbar_wait(&full_l[s], phl, args.status, kStatusGemmDequantTimeout, abort_flag)) {
         ok = false;
         break;
       }
-      const uint32_t wb = l_base + s * Plan::kStage;
+      if (t == 0 && it == 0) gemm_stamp(args, 2);
+      const uint32_t wb = l_base + s * Plan::kStage + (it & 1) * BLOB;
       uint4 p[4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) p[c] = lds128(wb + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
@@ -311,6 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const bool have_acc =
         ok && nkb > 0 && mbar_wait(acc_full, 0, args.status, kStatusGemmEpiTimeout, abort_flag);
+    if (t == 0) gemm_stamp(args, 5);
     const int cg = grp;                   // which quarter of the MT columns
     const int row = r;                    // weight row inside the tile
     const int n0 = rt * 128;
@@ -363,6 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc_fence_before();
     named_bar_sync(1, kDequantThreads);
+    if (t == 0) gemm_stamp(args, 6);
     if (!have_acc && args.splits == 1) {
       // Nothing to write (error path); leave outputs untouched.
     } else {
@@ -381,13 +414,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         do_final = *is_last_flag != 0;
         if (do_final) {
           __threadfence();
-          for (int idx = t; idx < 128 * MT; idx += kDequantThreads) {
-            const int rr = idx & 127;
-            const int m = idx >> 7;
-            float acc = 0.f;
-            for (int sp = 0; sp < args.splits; ++sp)
-              acc += __ldcg(&dst_ws[((size_t)sp * Mpad + m_base + m) * args.N + n0 + rr]);
-            tile[rr * (MT + 1) + m] = acc;
+          // Sum the splits with 16-byte loads, a batch of U splits in flight
+          // at once: a load-then-add chain per element would pay the L2
+          // latency (~0.7 us) once per element row (13 us at MT = 64).
+          constexpr int IT = (32 * MT) / kDequantThreads;  // float4s per thread
+          float4 acc[IT];
+#pragma unroll
+          for (int i = 0; i < IT; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          constexpr int U = IT >= 8 ? 1 : IT >= 4 ? 2 : 4;  // splits per batch of loads
+          for (int sp0 = 0; sp0 < args.splits; sp0 += U) {
+            float4 v[U][IT];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+              for (int i = 0; i < IT; ++i) {
+                const int idx = t + i * kDequantThreads;
+                const int r4 = (idx & 31) * 4, m = idx >> 5;
+                v[u][i] = sp0 + u < args.splits
+                              ? __ldcg(reinterpret_cast<const float4*>(
+                                    &dst_ws[((size_t)(sp0 + u) * Mpad + m_base + m) * args.N +
+                                            n0 + r4]))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+              for (int i = 0; i < IT; ++i) {
+                acc[i].x += v[u][i].x;
+                acc[i].y += v[u][i].y;
+                acc[i].z += v[u][i].z;
+                acc[i].w += v[u][i].w;
+              }
+          }
+#pragma unroll
+          for (int i = 0; i < IT; ++i) {
+            const int idx = t + i * kDequantThreads;
+            const int r4 = (idx & 31) * 4, m = idx >> 5;
+            tile[(r4 + 0) * (MT + 1) + m] = acc[i].x;
+            tile[(r4 + 1) * (MT + 1) + m] = acc[i].y;
+            tile[(r4 + 2) * (MT + 1) + m] = acc[i].z;
+            tile[(r4 + 3) * (MT + 1) + m] = acc[i].w;
           }
           named_bar_sync(1, kDequantThreads);
         }
@@ -404,6 +470,41 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float u = tile[(2 * j + 1) * (MT + 1) + m];
               const float y = g / (1.f + __expf(-g)) * u;
               args.out[(size_t)gm * args.ldo + rt * 64 + j] = __float2bfloat16(y);
+            }
+          }
+        } else if (args.vec_out) {
+          // 8 outputs (16 bytes) per thread and step, token index fastest
+          // (conflict-free tile reads); residual loads all issued up front.
+          constexpr int IT = (16 * MT + kDequantThreads - 1) / kDequantThreads;
+          uint4 res[IT];
+          if constexpr (EPI == kEpiResid) {
+#pragma unroll
+            for (int i = 0; i < IT; ++i) {
+              const int idx = t + i * kDequantThreads;
+              const int m = idx % MT, r8 = (idx / MT) * 8;
+              const int gm = m_base + m;
+              res[i] = (idx < 16 * MT && gm < m_lim)
+                           ? *reinterpret_cast<const uint4*>(
+                                 &args.residual[(size_t)gm * args.ldr + n0 + r8])
+                           : make_uint4(0, 0, 0, 0);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < IT; ++i) {
+            const int idx = t + i * kDequantThreads;
+            const int m = idx % MT, r8 = (idx / MT) * 8;
+            const int gm = m_base + m;
+            if (idx < 16 * MT && gm < m_lim) {
+              uint4 o;
+              __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&o);
+              const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&res[i]);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                float y = tile[(r8 + e) * (MT + 1) + m];
+                if constexpr (EPI == kEpiResid) y += __bfloat162float(re[e]);
+                oe[e] = __float2bfloat16(y);
+              }
+              *reinterpret_cast<uint4*>(&args.out[(size_t)gm * args.ldo + n0 + r8]) = o;
             }
           }
         } else {
@@ -423,6 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if (tid == 64) gemm_stamp(args, 7);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -913,6 +1015,22 @@ static GemmPlanInfo plan_gemm(int M, int N, int K, int forced_splits) {
 }
 
 // Workspace floats needed for a GEMM of this shape (0 when no split).
+static int vec_rows_ok(const torch::Tensor& out, const c10::optional<torch::Tensor>& residual) {
+  auto ok = [](const torch::Tensor& t) {
+    return (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0 && t.stride(0) % 8 == 0;
+  };
+  return ok(out) && (!residual.has_value() || ok(*residual)) ? 1 : 0;
+}
+
+// Diagnostics: per-CTA phase stamps of the tcgen05 kernel (nullptr = off).
+static unsigned long long* g_gemm_trace = nullptr;
+
+void w4a16_set_trace(c10::optional<torch::Tensor> buf) {
+  g_gemm_trace = buf.has_value()
+                     ? reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>())
+                     : nullptr;
+}
+
 // Decode batches of up to CASCADIA_GEMV_MAX_M (default 8) rows run the
 // small-M kernel (gemv_w4a16.cu); 0 disables it.
 static int gemv_max_m() {
@@ -1008,6 +1126,8 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
     return e ? std::atoi(e) : 0;
   }();
   a.diag = diag;
+  a.trace = g_gemm_trace;
+  a.vec_out = vec_rows_ok(out, residual);
   TORCH_CHECK(epilogue != kEpiResid || residual.has_value(), "residual epilogue needs residual");
 
   CUtensorMap tmap = make_tmap_2d_bf16(x.data_ptr(), (uint64_t)K, (uint64_t)M,
@@ -1070,6 +1190,7 @@ void w4a16_gemm_grouped(torch::Tensor x, torch::Tensor wblob, torch::Tensor out,
   a.group_offsets = group_offsets.data_ptr<int>();
   a.group_blob_stride = per;
   a.group_tiles = tiles;
+  a.vec_out = vec_rows_ok(out, c10::nullopt);
   CUtensorMap tmap = make_tmap_2d_bf16(x.data_ptr(), (uint64_t)K, (uint64_t)M,
                                        (uint64_t)x.stride(0) * 2, 64, (uint32_t)MT,
                                        CU_TENSOR_MAP_SWIZZLE_128B);
