@@ -89,10 +89,14 @@ class MoELayer:
 class MoEModel(LlamaModel):
     def __init__(self, cfg: ModelConfig, device, tp: Optional[TPGroup] = None,
                  layer_start: int = 0, layer_end: Optional[int] = None,
-                 has_embed: bool = True, has_head: bool = True, bf16_attention: bool = True):
+                 has_embed: bool = True, has_head: bool = True, bf16_attention: bool = True,
+                 ep=None):
         super().__init__(cfg, device, tp, layer_start, layer_end, has_embed, has_head)
         assert self.tp.size == 1, "MoE model: expert parallelism replaces TP (see parallel.ep)"
         self.bf16_attention = bf16_attention
+        # parallel.ep.ExpertParallel: this rank holds experts [ep.lo, ep.hi)
+        # of every MoE layer and attends over its own sequences.
+        self.ep = ep
         self.layers: List[MoELayer] = []
 
     def init_random(self, seed: int = 0, std: float = 0.02, gen_device=None):
@@ -132,10 +136,16 @@ class MoEModel(LlamaModel):
                     bias = (torch.randn(cfg.num_experts, generator=g, device=dev) * 0.1).float().to(
                         self.device)
                 gus, dns = [], []
-                for _ in range(cfg.num_experts):
-                    gus.append(Int4Weight.cat_rows([random_int4(I, h, g, dev, std, gs),
-                                                    random_int4(I, h, g, dev, std, gs)]))
-                    dns.append(random_int4(h, I, g, dev, std, gs))
+                lo, hi = (self.ep.lo, self.ep.hi) if self.ep is not None else (0, cfg.num_experts)
+                for ei in range(cfg.num_experts):
+                    # Every expert is drawn (the generator stream stays the
+                    # same for every EP size); only the local ones are kept.
+                    gu = Int4Weight.cat_rows([random_int4(I, h, g, dev, std, gs),
+                                              random_int4(I, h, g, dev, std, gs)])
+                    dn = random_int4(h, I, g, dev, std, gs)
+                    if lo <= ei < hi:
+                        gus.append(gu)
+                        dns.append(dn)
                 bank = ExpertBank(gus, dns, self.device)
                 del gus, dns
                 if cfg.num_shared_experts:
@@ -192,6 +202,17 @@ class MoEModel(LlamaModel):
         shared_out = None
         if lw.shared is not None:
             shared_out = lw.shared[1](lw.shared[0](h, ops.EPI_SILU))
+        if self.ep is not None:
+            if self.device.type == "cuda":
+                ids, w = ops.moe_topk_gate(h, lw.router, k, scoring, cfg.norm_topk_prob,
+                                           cfg.routed_scaling_factor, lw.router_bias)
+            else:
+                ids, w = ref_topk_gate(h, lw.router, lw.router_bias, k, scoring,
+                                       cfg.norm_topk_prob, cfg.routed_scaling_factor)
+            add = hidden if shared_out is None else (hidden.float() + shared_out.float()).to(
+                torch.bfloat16)
+            self.ep.moe(bank, h, ids, w.float(), add, hidden)
+            return
         if self.device.type == "cuda":
             ids, w = ops.moe_topk_gate(h, lw.router, k, scoring, cfg.norm_topk_prob,
                                        cfg.routed_scaling_factor, lw.router_bias)

@@ -278,13 +278,17 @@ def moe_permute(ids, num_experts: int, x=None):
 
 
 def w4a16_gemm_grouped(x, blob, n: int, group_size: int, epilogue: int, offsets,
-                       num_groups: int, max_rows: int, out=None):
+                       num_groups: int, max_rows: int, out=None, out_rows=None):
+    """Grouped (per-expert) W4A16 GEMM.  ``out_rows`` (int64 [rows], optional):
+    row m of the result is stored at address out_rows[m] (peer memory for
+    expert parallelism) instead of into ``out``."""
     m = x.shape[0]
     n_out = n // 2 if epilogue == EPI_SILU else n
     if out is None:
-        out = torch.empty(m, n_out, dtype=torch.bfloat16, device=x.device)
+        out = torch.empty(1 if out_rows is not None else m, n_out, dtype=torch.bfloat16,
+                          device=x.device)
     ext().w4a16_gemm_grouped(x, blob, out, n, group_size, epilogue, offsets, num_groups,
-                             max_rows, status_buffer(x.device))
+                             max_rows, status_buffer(x.device), out_rows)
     LAUNCHES.add(1)
     return out
 

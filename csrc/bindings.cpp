@@ -15,7 +15,24 @@ void w4a16_set_trace(c10::optional<torch::Tensor> buf);
 std::vector<int64_t> w4a16_plan(int64_t M, int64_t N, int64_t K, int64_t forced_splits);
 void w4a16_gemm_grouped(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t N,
                         int64_t group_size, int64_t epilogue, torch::Tensor group_offsets,
-                        int64_t num_groups, int64_t max_rows_per_group, torch::Tensor status);
+                        int64_t num_groups, int64_t max_rows_per_group, torch::Tensor status,
+                        c10::optional<torch::Tensor> out_rows);
+// ep.cu
+void ep_dispatch(torch::Tensor x, torch::Tensor ids, torch::Tensor dest, torch::Tensor pos,
+                 torch::Tensor send_cnt, torch::Tensor xbuf_ptrs, torch::Tensor rbuf_ptrs,
+                 torch::Tensor meta_ptrs, torch::Tensor sig_ptrs, torch::Tensor epoch,
+                 torch::Tensor done, torch::Tensor status, int64_t rank, int64_t world,
+                 int64_t cap, int64_t e_local);
+void ep_receive(torch::Tensor xp, torch::Tensor offsets, torch::Tensor src_row,
+                torch::Tensor out_rows, torch::Tensor total, torch::Tensor xbuf_ptrs,
+                torch::Tensor rbuf_ptrs, torch::Tensor meta_ptrs, torch::Tensor sig_ptrs,
+                torch::Tensor epoch, torch::Tensor done, torch::Tensor status, int64_t rank,
+                int64_t world, int64_t cap, int64_t e_local);
+void ep_combine(torch::Tensor w, torch::Tensor dest, torch::Tensor pos,
+                c10::optional<torch::Tensor> add, torch::Tensor out, torch::Tensor xbuf_ptrs,
+                torch::Tensor rbuf_ptrs, torch::Tensor meta_ptrs, torch::Tensor sig_ptrs,
+                torch::Tensor epoch, torch::Tensor done, torch::Tensor status, int64_t rank,
+                int64_t world, int64_t cap, int64_t e_local);
 // gemv_w4a16.cu
 void w4a16_gemv(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t N,
                 int64_t group_size, int64_t epilogue, c10::optional<torch::Tensor> residual,
@@ -82,6 +99,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_topk_gate", &cb::moe_topk_gate);
   m.def("moe_permute", &cb::moe_permute);
   m.def("moe_combine", &cb::moe_combine);
+  m.def("ep_dispatch", &cb::ep_dispatch);
+  m.def("ep_receive", &cb::ep_receive);
+  m.def("ep_combine", &cb::ep_combine);
   m.def("head_rmsnorm", &cb::head_rmsnorm);
   m.def("w4a16_gemv", &cb::w4a16_gemv);
   m.def("gemv_workspace_floats", &cb::gemv_workspace_floats);

@@ -125,7 +125,16 @@ struct GemmArgs {
   unsigned long long* trace;
   // out (and residual) rows are 16-byte aligned: vectorised epilogue.
   int vec_out;
+  // Optional: output row m is stored at out_rows[m] instead of out + m * ldo
+  // (expert parallelism: result rows go straight to the source rank's
+  // return region in peer memory).
+  const long long* out_rows;
 };
+
+__device__ __forceinline__ __nv_bfloat16* gemm_out_row(const GemmArgs& a, int gm) {
+  return a.out_rows != nullptr ? reinterpret_cast<__nv_bfloat16*>(a.out_rows[gm])
+                               : a.out + (size_t)gm * a.ldo;
+}
 
 __device__ __forceinline__ void gemm_stamp(const GemmArgs& a, int k) {
   if (a.trace != nullptr) {
@@ -469,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float g = tile[(2 * j) * (MT + 1) + m];
               const float u = tile[(2 * j + 1) * (MT + 1) + m];
               const float y = g / (1.f + __expf(-g)) * u;
-              args.out[(size_t)gm * args.ldo + rt * 64 + j] = __float2bfloat16(y);
+              gemm_out_row(args, gm)[rt * 64 + j] = __float2bfloat16(y);
             }
           }
         } else if (args.vec_out) {
@@ -504,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if constexpr (EPI == kEpiResid) y += __bfloat162float(re[e]);
                 oe[e] = __float2bfloat16(y);
               }
-              *reinterpret_cast<uint4*>(&args.out[(size_t)gm * args.ldo + n0 + r8]) = o;
+              *reinterpret_cast<uint4*>(gemm_out_row(args, gm) + n0 + r8) = o;
             }
           }
         } else {
@@ -516,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               float y = tile[rr * (MT + 1) + m];
               if constexpr (EPI == kEpiResid)
                 y += __bfloat162float(args.residual[(size_t)gm * args.ldr + n0 + rr]);
-              args.out[(size_t)gm * args.ldo + n0 + rr] = __float2bfloat16(y);
+              gemm_out_row(args, gm)[n0 + rr] = __float2bfloat16(y);
             }
           }
         }
@@ -1164,7 +1173,8 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
 // the tiles launched per expert (CTAs of empty tiles exit at once).
 void w4a16_gemm_grouped(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t N,
                         int64_t group_size, int64_t epilogue, torch::Tensor group_offsets,
-                        int64_t num_groups, int64_t max_rows_per_group, torch::Tensor status) {
+                        int64_t num_groups, int64_t max_rows_per_group, torch::Tensor status,
+                        c10::optional<torch::Tensor> out_rows) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(1) == 1, "x");
   TORCH_CHECK(epilogue != kEpiResid, "grouped GEMM supports store and SiLU epilogues");
   const int M = (int)x.size(0);
@@ -1191,6 +1201,13 @@ void w4a16_gemm_grouped(torch::Tensor x, torch::Tensor wblob, torch::Tensor out,
   a.group_blob_stride = per;
   a.group_tiles = tiles;
   a.vec_out = vec_rows_ok(out, c10::nullopt);
+  if (out_rows.has_value()) {
+    TORCH_CHECK(out_rows->scalar_type() == at::kLong && out_rows->numel() >= M,
+                "out_rows: int64 row addresses, one per row of x");
+    // Row addresses must keep 16-byte alignment for the vectorised epilogue.
+    TORCH_CHECK(N % 8 == 0, "out_rows needs N % 8 == 0");
+    a.out_rows = reinterpret_cast<const long long*>(out_rows->data_ptr<int64_t>());
+  }
   CUtensorMap tmap = make_tmap_2d_bf16(x.data_ptr(), (uint64_t)K, (uint64_t)M,
                                        (uint64_t)x.stride(0) * 2, 64, (uint32_t)MT,
                                        CU_TENSOR_MAP_SWIZZLE_128B);

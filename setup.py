@@ -26,6 +26,7 @@ SOURCES = [
     "comm.cu",
     "moe.cu",
     "gemv_w4a16.cu",
+    "ep.cu",
 ]
 
 NVCC_FLAGS = [
