@@ -147,22 +147,33 @@ def main():
 
         tp.fused = FusedTP(group, rank, world, dev, cfg.hidden_size, max(64, args.batch))
     t0 = time.time()
+    ep = None
     if cfg.is_moe:
-        # Sparse-MoE configs (bf16 attention, INT4 experts); one GPU holds
-        # every expert.
+        # Sparse-MoE configs (bf16 attention, INT4 experts).  N > 1: expert
+        # parallel over the N GPUs (each holds E/N experts) with data-parallel
+        # attention: the global batch is split over the ranks.
         from cascadia_b200.models.moe import MoEModel
 
-        assert world == 1, "MoE bench: one GPU per process"
-        model = MoEModel(cfg, dev).init_random(seed=1234)
+        if world > 1:
+            from cascadia_b200.parallel.ep import ExpertParallel
+
+            assert args.batch % world == 0, "global batch must divide over the EP ranks"
+            ep = ExpertParallel(group, rank, world, dev, cfg.num_experts, cfg.hidden_size,
+                                cfg.num_experts_per_tok, max_tokens=4096,
+                                fused=args.tp_comm == "fused")
+        model = MoEModel(cfg, dev, ep=ep).init_random(seed=1234)
     else:
         model = LlamaModel(cfg, dev, tp=tp).init_random(seed=1234)
     torch.cuda.synchronize()
     load_s = time.time() - t0
-    B, P = args.batch, args.prompt_len
+    B_global, P = args.batch, args.prompt_len
+    B = B_global // world if ep is not None else B_global  # sequences on this rank
     total_len = P + args.warmup + 2 * args.steps + 4
     width = -(-total_len // BLOCK_SIZE)
     model.allocate_kv(B * width + 16 + width * (args.ttft_reps + 1))
-    gen = BatchGenerator(model, use_graph=not args.no_graph)
+    # The all-to-all EP baseline needs host-side counts each layer: no graph.
+    graph_ok = not args.no_graph and not (ep is not None and not ep.fused)
+    gen = BatchGenerator(model, use_graph=graph_ok)
 
     g = torch.Generator().manual_seed(42)
     prompts = torch.randint(0, cfg.vocab_size, (B, P), generator=g).tolist()
@@ -170,6 +181,8 @@ def main():
     # Prefill (untimed), in chunks to bound activation memory.
     first = []
     chunk = max(1, (4096 if cfg.is_moe else 16384) // P)
+    if ep is not None:
+        ep.row_bound = chunk * P
     for i in range(0, B, chunk):
         first.extend(gen.prefill(seq_ids[i:i + chunk], prompts[i:i + chunk]).tolist())
     torch.cuda.synchronize()
@@ -180,6 +193,8 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
+    if ep is not None:
+        ep.row_bound = B  # decode: every rank feeds B tokens per step
     # Warm-up decode steps (also captures the CUDA graph).
     for _ in range(args.warmup):
         last = gen.decode(seq_ids, last, width).tolist()
@@ -248,8 +263,9 @@ def main():
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     gpu_ms, e2e_ms, ttft = vals.tolist()
     ms_step = gpu_ms / args.steps
-    value = B * args.steps / (gpu_ms / 1000.0)
-    e2e_val = B * args.steps / (e2e_ms / 1000.0)
+    B_all = B * world if ep is not None else B  # tokens per step over the whole job
+    value = B_all * args.steps / (gpu_ms / 1000.0)
+    e2e_val = B_all * args.steps / (e2e_ms / 1000.0)
     status = ops.read_status(dev)
     if rank == 0:
         out = {
@@ -268,8 +284,9 @@ def main():
             f"bf16 activations and attention, int4-g{cfg.group_size} experts",
             "data": "synthetic: random-init N(0,0.02) INT4 weights, seeded uniform prompt ids",
             "config": {"model": args.model + (f"-L{args.layers}" if args.layers else ""),
-                       "global_batch": B, "seq_len": P, "decode_context": f"{P}..{P + args.warmup + 2 * args.steps}",
-                       "parallelism": f"tp{world}", "kv_block": BLOCK_SIZE,
+                       "global_batch": B_all, "seq_len": P, "decode_context": f"{P}..{P + args.warmup + 2 * args.steps}",
+                       "parallelism": (f"ep{world}+dp-attention" if ep is not None
+                                       else f"tp{world}"), "kv_block": BLOCK_SIZE,
                        "tp_comm": args.tp_comm if world > 1 else None,
                        "l2": "inputs larger than L2 (weights+KV >> 126 MB)",
                        "cuda_graph": graph.graph is not None},

@@ -1,6 +1,6 @@
 """Decode-step profiling driver (for ncu launch lists and kernel captures).
 
-Builds the Llama-3.1-8B-shaped INT4 model (random init) on cuda:0, prefills
+Builds the Llama-3.1-8B-shaped INT4 model (or a MoE preset) on cuda:0, prefills
 `--batch` prompts of `--prompt-len` tokens, then runs `--steps` decode steps
 eagerly (no CUDA graph) inside cudaProfilerStart/Stop so that
 
@@ -40,7 +40,12 @@ def main():
         cfg.num_layers = a.layers
     dev = torch.device("cuda", 0)
     t0 = time.time()
-    m = LlamaModel(cfg, dev).init_random(seed=1)
+    if cfg.is_moe:
+        from cascadia_b200.models.moe import MoEModel
+
+        m = MoEModel(cfg, dev).init_random(seed=1)
+    else:
+        m = LlamaModel(cfg, dev).init_random(seed=1)
     width = -(-(a.prompt_len + a.steps + 8) // BLOCK_SIZE)
     m.allocate_kv(a.batch * width + 8)
     gen = BatchGenerator(m, use_graph=False)
@@ -55,7 +60,7 @@ def main():
         torch.cuda.cudart().cudaProfilerStop()
         print("prefill done", time.time() - t0)
         return
-    chunk = max(1, 16384 // a.prompt_len)
+    chunk = max(1, (4096 if cfg.is_moe else 16384) // a.prompt_len)
     last = []
     for i in range(0, a.batch, chunk):
         last.extend(gen.prefill(ids[i:i + chunk], prompts[i:i + chunk]).tolist())

@@ -30,6 +30,10 @@ from .config import ModelConfig, rope_table
 from .llama import Batch, LlamaModel, QLinear, TPGroup, _layer_generator, random_int4
 
 
+# Token counts up to this use the grouped small-M expert kernel (decode).
+SMALL_M_TOKENS = 64
+
+
 class BF16Linear:
     """Plain bf16 projection (the MoE config's attention is bf16); on CUDA
     this is a cuBLAS GEMM through torch.matmul."""
@@ -216,12 +220,24 @@ class MoEModel(LlamaModel):
         if self.device.type == "cuda":
             ids, w = ops.moe_topk_gate(h, lw.router, k, scoring, cfg.norm_topk_prob,
                                        cfg.routed_scaling_factor, lw.router_bias)
-            offsets, perm, inv, xp = ops.moe_permute(ids, bank.E, h)
             T = h.shape[0]
-            act = ops.w4a16_gemm_grouped(xp, bank.gu_blob, 2 * bank.inter, bank.gs, ops.EPI_SILU,
-                                         offsets, bank.E, T)
-            y = ops.w4a16_gemm_grouped(act, bank.dn_blob, bank.hidden, bank.gs, ops.EPI_STORE,
-                                       offsets, bank.E, T)
+            if T <= SMALL_M_TOKENS and bank.gs == 128:
+                # Decode: a few rows per expert -> grouped small-M kernel on
+                # fp16-prepared activations (gathered into expert order).
+                offsets, perm, inv, _ = ops.moe_permute(ids, bank.E)
+                n = T * k
+                x16, xs = ops.moe_prep_fp16(h, n, perm, k)
+                act = ops.w4a16_gemv_grouped(x16, xs, bank.gu_blob, 2 * bank.inter,
+                                             ops.EPI_SILU, offsets, bank.E)
+                a16, a_s = ops.moe_prep_fp16(act, n)
+                y = ops.w4a16_gemv_grouped(a16, a_s, bank.dn_blob, bank.hidden, ops.EPI_STORE,
+                                           offsets, bank.E)
+            else:
+                offsets, perm, inv, xp = ops.moe_permute(ids, bank.E, h)
+                act = ops.w4a16_gemm_grouped(xp, bank.gu_blob, 2 * bank.inter, bank.gs,
+                                             ops.EPI_SILU, offsets, bank.E, T)
+                y = ops.w4a16_gemm_grouped(act, bank.dn_blob, bank.hidden, bank.gs,
+                                           ops.EPI_STORE, offsets, bank.E, T)
             add = hidden if shared_out is None else (hidden.float() + shared_out.float()).to(
                 torch.bfloat16)
             ops.moe_combine(y, inv, w, add=add, out=hidden)

@@ -251,13 +251,31 @@ def spec_verify(target, draft, out):
 
 
 # ----------------------------------------------------------------- MoE
+_GATE_CNT: dict = {}
+
+
+def _gate_counters(device, n: int) -> torch.Tensor:
+    """Per-token completion counters of the gate kernel (zero between
+    launches: the kernel resets each one it uses)."""
+    key = torch.device(device).index or 0
+    buf = _GATE_CNT.get(key)
+    if buf is None or buf.numel() < n:
+        buf = torch.zeros(max(n, 4096), dtype=torch.int32, device=device)
+        _GATE_CNT[key] = buf
+    return buf
+
+
 def moe_topk_gate(x, wg, k: int, scoring: int = 0, norm_topk: bool = True,
                   routed_scale: float = 1.0, bias=None, logits_out=None):
     """Router + top-k: returns (ids int32 [T, k], weights fp32 [T, k])."""
     T = x.shape[0]
+    E = wg.shape[0]
     ids = torch.empty(T, k, dtype=torch.int32, device=x.device)
     w = torch.empty(T, k, dtype=torch.float32, device=x.device)
-    ext().moe_topk_gate(x, wg, bias, k, scoring, norm_topk, routed_scale, ids, w, logits_out)
+    logits = logits_out if logits_out is not None else torch.empty(
+        max(1, T * E), dtype=torch.float32, device=x.device)
+    ext().moe_topk_gate(x, wg, bias, k, scoring, norm_topk, routed_scale, ids, w, logits,
+                        _gate_counters(x.device, T))
     LAUNCHES.add(1)
     return ids, w
 
@@ -289,6 +307,33 @@ def w4a16_gemm_grouped(x, blob, n: int, group_size: int, epilogue: int, offsets,
                           device=x.device)
     ext().w4a16_gemm_grouped(x, blob, out, n, group_size, epilogue, offsets, num_groups,
                              max_rows, status_buffer(x.device), out_rows)
+    LAUNCHES.add(1)
+    return out
+
+
+def moe_prep_fp16(x, rows: int, perm=None, topk: int = 1):
+    """Prepared activations for the grouped small-M GEMM: fp16 rows (scaled
+    by a power of two per row) and per-k-block offset corrections.  Row r is
+    x[perm[r] // topk] when ``perm`` is given (gather into expert order)."""
+    K = x.shape[1]
+    ld16, lds = ext().moe_prep_shape(K)
+    x16 = torch.empty(max(1, rows), ld16, dtype=torch.float16, device=x.device)
+    xs = torch.empty(max(1, rows), lds, dtype=torch.float32, device=x.device)
+    ext().moe_prep_fp16(x, perm, topk, rows, x16, xs)
+    LAUNCHES.add(1)
+    return x16, xs
+
+
+def w4a16_gemv_grouped(x16, xs, blob, n: int, epilogue: int, offsets, num_groups: int,
+                       out=None, out_rows=None):
+    """Grouped small-M W4A16 GEMM (group 128) on prepared activations; the
+    decode path of the MoE experts (few rows per expert)."""
+    rows = x16.shape[0]
+    n_out = n // 2 if epilogue == EPI_SILU else n
+    if out is None:
+        out = torch.empty(rows, n_out, dtype=torch.bfloat16, device=x16.device)
+    ext().w4a16_gemv_grouped(x16, xs, blob, out, n, epilogue, offsets, num_groups,
+                             status_buffer(x16.device), out_rows)
     LAUNCHES.add(1)
     return out
 

@@ -46,6 +46,10 @@ class ExpertParallel:
         self.k = top_k
         self.max_tokens = max_tokens
         self.cap = max_tokens * top_k  # rows one source can send one destination
+        # Upper bound on any rank's tokens per call: sizes the grouped GEMM
+        # grid (world * row_bound rows per expert at most).  Callers that run
+        # smaller batches in lockstep (decode) may lower it.
+        self.row_bound = max_tokens
         if fused is None:
             fused = self.dev.type == "cuda" and world > 1
         self.fused = fused
@@ -106,7 +110,7 @@ class ExpertParallel:
         c = self._common()
         e.ep_dispatch(h, ids, self.dest, self.pos, self.send_cnt, *c)
         e.ep_receive(self.xp, self.offsets, self.src_row, self.out_rows, self.total, *c)
-        max_rows = self.world * self.max_tokens  # each token reaches an expert at most once
+        max_rows = self.world * self.row_bound  # each token reaches an expert at most once
         act = ops.w4a16_gemm_grouped(self.xp, bank.gu_blob, 2 * bank.inter, bank.gs,
                                      ops.EPI_SILU, self.offsets, self.e_local, max_rows)
         ops.w4a16_gemm_grouped(act, bank.dn_blob, bank.hidden, bank.gs, ops.EPI_STORE,

@@ -39,11 +39,18 @@ void w4a16_gemv(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
                 torch::Tensor ws, torch::Tensor counters, torch::Tensor status,
                 int64_t forced_splits);
 int64_t gemv_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t forced_splits);
+void moe_prep_fp16(torch::Tensor x, c10::optional<torch::Tensor> perm, int64_t topk,
+                   int64_t rows, torch::Tensor x16, torch::Tensor xsum);
+std::vector<int64_t> moe_prep_shape(int64_t K);
+void w4a16_gemv_grouped(torch::Tensor x16, torch::Tensor xsum, torch::Tensor wblob,
+                        torch::Tensor out, int64_t N, int64_t epilogue, torch::Tensor offsets,
+                        int64_t num_groups, torch::Tensor status,
+                        c10::optional<torch::Tensor> out_rows);
 // moe.cu
 void moe_topk_gate(torch::Tensor x, torch::Tensor wg, c10::optional<torch::Tensor> bias,
                    int64_t k, int64_t scoring, bool norm_topk, double routed_scale,
-                   torch::Tensor topk_ids, torch::Tensor topk_w,
-                   c10::optional<torch::Tensor> logits_out);
+                   torch::Tensor topk_ids, torch::Tensor topk_w, torch::Tensor logits,
+                   torch::Tensor counters);
 void moe_permute(torch::Tensor topk_ids, int64_t E, torch::Tensor offsets, torch::Tensor perm,
                  torch::Tensor inv, c10::optional<torch::Tensor> x,
                  c10::optional<torch::Tensor> xp);
@@ -105,4 +112,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("head_rmsnorm", &cb::head_rmsnorm);
   m.def("w4a16_gemv", &cb::w4a16_gemv);
   m.def("gemv_workspace_floats", &cb::gemv_workspace_floats);
+  m.def("moe_prep_fp16", &cb::moe_prep_fp16);
+  m.def("moe_prep_shape", &cb::moe_prep_shape);
+  m.def("w4a16_gemv_grouped", &cb::w4a16_gemv_grouped);
 }

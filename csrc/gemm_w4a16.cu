@@ -166,6 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * SL + 2 * kGroups + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* is_last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* acc_ok = reinterpret_cast<volatile int*>(tmem_slot + 3);
   float* tile = reinterpret_cast<float*>(smem);  // reused after the main loop
 
   const int tid = threadIdx.x;
@@ -207,6 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(acc_full, SmemPlan<MT, GS>::kIssuers);  // every MMA issuer commits
     *abort_flag = 0;
     *is_last_flag = 0;
+    *acc_ok = 1;
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -351,6 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const bool have_acc =
         ok && nkb > 0 && mbar_wait(acc_full, 0, args.status, kStatusGemmEpiTimeout, abort_flag);
+    if (!have_acc) *acc_ok = 0;  // made uniform after the next barrier
     if (t == 0) gemm_stamp(args, 5);
     const int cg = grp;                   // which quarter of the MT columns
     const int row = r;                    // weight row inside the tile
@@ -405,7 +408,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     named_bar_sync(1, kDequantThreads);
     if (t == 0) gemm_stamp(args, 6);
-    if (!have_acc && args.splits == 1) {
+    // Every dequant thread takes the same branch (barriers below).  With
+    // split-K the counter protocol still runs, so the per-tile counters stay
+    // consistent for the next launch.
+    if (!*acc_ok && args.splits == 1) {
       // Nothing to write (error path); leave outputs untouched.
     } else {
       bool do_final = true;

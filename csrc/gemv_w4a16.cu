@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_kernel(const GvArgs 
   uint64_t* xbar = bars + 2 * S;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * S + 1);
   int* s_last = reinterpret_cast<int*>(bars + 2 * S + 2);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(bars + 2 * S + 3);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -364,10 +365,12 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_kernel(const GvArgs 
         }
       }
     }
-    if (!ok) break;
-
     // ---------------------------------------------------------- reduction
+    // Every consumer warp reaches these barriers on every tile, also after a
+    // failed wait; the abort decision is taken uniformly from a snapshot of
+    // the abort flag (the producer may raise it at any time).
     named_bar_sync(1, kCons);  // previous tile's epilogue is done with red/tile
+    if (tid == 0) *s_abort = *abort_flag;
     if (par == 1) {
 #pragma unroll
       for (int t = 0; t < NT; ++t)
@@ -375,6 +378,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_kernel(const GvArgs 
         for (int q = 0; q < 4; ++q) red[(rg * 32 + lane) * NT * 4 + t * 4 + q] = acc[t][q];
     }
     named_bar_sync(1, kCons);
+    if (*s_abort) break;
     if (par == 0) {
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
@@ -512,6 +516,316 @@ void gv_launch_nt(int NT, const GvArgs& a, dim3 grid, int smem, cudaStream_t s) 
   else gv_launch_t<GS, EPI, 2>(a, grid, smem, s);
 }
 
+
+// ---------------------------------------------------------------- grouped
+// MoE decode: every expert e multiplies its own few rows
+// [offsets[e], offsets[e+1]) of a prepared activation matrix with its own
+// weights (group 128).  Work units (expert, 128-row weight tile) are spread
+// over persistent CTAs; a unit with more than 8 rows runs in chunks of 8.
+// The activations come prepared by moe_prep_fp16 (fp16, power-of-two scaled
+// per row, with the per-k-block offset corrections and the row exponent in
+// `xsum`), so a unit only copies its rows in: one bulk copy for the X rows,
+// one for their corrections, into a double-buffered X tile.
+struct GvgArgs {
+  const uint8_t* wblob;
+  long long blob_stride;     // bytes per expert
+  const __half* x16;         // [R, ldx16] fp16 rows
+  const float* xsum;         // [R, ldxs]: -sum (c(k) + 8) x per k-block, then the exponent
+  const int* offsets;        // [E + 1]
+  __nv_bfloat16* out;        // [R, ldo]
+  const long long* out_rows; // optional per-row destination addresses
+  int* status;
+  int E, N, K, ldx16, ldxs, ldo, stages;
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_grouped_kernel(const GvgArgs a) {
+  constexpr int MP = 8;
+  constexpr int kCons = 32 * kGvConsumerWarps;
+  using Blob = GvBlob<128>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KB = a.K / 128;
+  const int RT = a.N / 128;
+  const int spt = (KB + 1) / 2;
+  const int S = a.stages;
+  const int xbytes = MP * a.ldx16 * 2;  // one X buffer
+  const int sbytes = MP * a.ldxs * 4;   // one correction buffer
+  uint8_t* ring = smem;
+  float* red = reinterpret_cast<float*>(smem + S * Blob::kStage);  // [8][32][4]
+  float* tile = red + 8 * 32 * 4;                                   // [128][MP + 1]
+  uint8_t* xs = reinterpret_cast<uint8_t*>(tile + 128 * (MP + 1));  // 2 X buffers
+  float* xsm = reinterpret_cast<float*>(xs + 2 * xbytes);           // 2 correction buffers
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xsm) + 2 * sbytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* xfull = bars + 2 * S;
+  uint64_t* xempty = bars + 2 * S + 2;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * S + 4);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(bars + 2 * S + 5);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kGvConsumerWarps);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&xfull[i], 1);
+      mbar_init(&xempty[i], kGvConsumerWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kGvConsumerWarps) {
+    if (lane == 0) {
+      int slot = 0, sub = 0, issued = 0;
+      uint32_t phase = 0;
+      bool go = true;
+      for (int u = blockIdx.x; u < a.E * RT && go; u += gridDim.x) {
+        const int e = u / RT, rt = u % RT;
+        const int r0 = a.offsets[e], n = a.offsets[e + 1] - r0;
+        const uint8_t* wsrc = a.wblob + (size_t)e * a.blob_stride + (size_t)rt * KB * Blob::kBytes;
+        for (int c0 = 0; c0 < n && go; c0 += MP, ++sub) {
+          const int rows = min(MP, n - c0);
+          const int xb = sub & 1;
+          if (sub >= 2 && !mbar_wait(&xempty[xb], ((sub >> 1) - 1) & 1, a.status,
+                                     kStatusGemmLoadTimeout, abort_flag)) {
+            go = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&xfull[xb], (uint32_t)(rows * (a.ldx16 * 2 + a.ldxs * 4)));
+          bulk_g2s(xs + xb * xbytes, a.x16 + (size_t)(r0 + c0) * a.ldx16,
+                   (uint32_t)(rows * a.ldx16 * 2), &xfull[xb]);
+          bulk_g2s(reinterpret_cast<uint8_t*>(xsm) + xb * sbytes,
+                   a.xsum + (size_t)(r0 + c0) * a.ldxs, (uint32_t)(rows * a.ldxs * 4),
+                   &xfull[xb]);
+          for (int st = 0; st < spt; ++st) {
+            if (issued >= S &&
+                !mbar_wait(&empty[slot], phase ^ 1u, a.status, kStatusGemmLoadTimeout, abort_flag)) {
+              go = false;
+              break;
+            }
+            const int nb = min(2, KB - 2 * st);
+            mbar_arrive_expect_tx(&full[slot], (uint32_t)(nb * Blob::kBytes));
+            bulk_g2s(ring + slot * Blob::kStage, wsrc + (size_t)(2 * st) * Blob::kBytes,
+                     (uint32_t)(nb * Blob::kBytes), &full[slot]);
+            ++issued;
+            if (++slot == S) {
+              slot = 0;
+              phase ^= 1u;
+            }
+          }
+        }
+      }
+      // Wait (bounded) for the copies still in flight before leaving.
+      for (int g = max(0, issued - S); g < issued; ++g)
+        mbar_wait(&full[g % S], (g / S) & 1, nullptr, 0, nullptr);
+      for (int sb = max(0, sub - 2); sb < sub; ++sb)
+        mbar_wait(&xfull[sb & 1], (sb >> 1) & 1, nullptr, 0, nullptr);
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumers
+  const int tid = threadIdx.x;
+  const int rg = warp & 7, par = warp >> 3;
+  const int g = lane >> 2, c = lane & 3;
+  const int r0w = rg * 16 + g, r1w = r0w + 8;
+  const int sw0 = ((c ^ ((r0w >> 1) & 3)) << 4), sw1 = ((c ^ ((r1w >> 1) & 3)) << 4);
+  const uint32_t ring_u = smem_u32(ring);
+  const uint32_t xs_u = smem_u32(xs);
+  int slot = 0, sub = 0;
+  uint32_t phase = 0;
+  bool ok = true;
+  for (int u = blockIdx.x; u < a.E * RT && ok; u += gridDim.x) {
+    const int e = u / RT, rt = u % RT;
+    const int r0 = a.offsets[e], n = a.offsets[e + 1] - r0;
+    for (int c0 = 0; c0 < n && ok; c0 += MP, ++sub) {
+      const int rows = min(MP, n - c0);
+      const int xb = sub & 1;
+      if (ok && !mbar_wait(&xfull[xb], (sub >> 1) & 1, a.status, kStatusGemmMmaTimeout,
+                           abort_flag))
+        ok = false;
+      const uint32_t xbase = xs_u + xb * xbytes;
+      const float* cs = xsm + xb * (sbytes / 4);
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int st = 0; st < spt && ok; ++st) {
+        const int cur = slot;
+        const uint32_t ph = phase;
+        if (++slot == S) {
+          slot = 0;
+          phase ^= 1u;
+        }
+        if (!mbar_wait(&full[cur], ph, a.status, kStatusGemmMmaTimeout, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int i = 2 * st + par;
+        if (i >= KB) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[cur]);
+          continue;
+        }
+        const uint32_t base = ring_u + cur * Blob::kStage + par * Blob::kBytes;
+        const uint4 wa = lds128(base + r0w * 64 + sw0);
+        const uint4 wb = lds128(base + r1w * 64 + sw1);
+        const uint16_t sa = lds16(base + Blob::kPacked + r0w * 2);
+        const uint16_t sb = lds16(base + Blob::kPacked + r1w * 2);
+        uint32_t xr[16];
+        if (g < rows) {
+          const uint32_t xa = xbase + g * a.ldx16 * 2 + (i * 128 + 32 * c) * 2;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 v = lds128(xa + q * 16);
+            xr[4 * q + 0] = v.x;
+            xr[4 * q + 1] = v.y;
+            xr[4 * q + 2] = v.z;
+            xr[4 * q + 3] = v.w;
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 16; ++q) xr[q] = 0u;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[cur]);
+        const uint32_t wa_w[4] = {wa.x, wa.y, wa.z, wa.w};
+        const uint32_t wb_w[4] = {wb.x, wb.y, wb.z, wb.w};
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const int wi = jj >> 1;
+          uint32_t va = wa_w[wi], vb = wb_w[wi];
+          if (jj & 1) {
+            va = __umulhi(va, 1u << 24);
+            vb = __umulhi(vb, 1u << 24);
+          }
+          const uint32_t A[4] = {magic_lo(va), magic_lo(vb), magic_hi(va), magic_hi(vb)};
+          mma_16816_f16(d, A, xr[2 * jj], xr[2 * jj + 1]);
+        }
+        const float fa = __bfloat162float(__ushort_as_bfloat16(sa));
+        const float fb = __bfloat162float(__ushort_as_bfloat16(sb));
+        const int n0 = 2 * c, n1 = 2 * c + 1;
+        const float x0 = n0 < rows ? cs[n0 * a.ldxs + i] : 0.f;
+        const float x1 = n1 < rows ? cs[n1 * a.ldxs + i] : 0.f;
+        acc[0] = fmaf(fa, d[0] + x0, acc[0]);
+        acc[1] = fmaf(fa, d[1] + x1, acc[1]);
+        acc[2] = fmaf(fb, d[2] + x0, acc[2]);
+        acc[3] = fmaf(fb, d[3] + x1, acc[3]);
+      }
+      // Per-row exponents of the X scaling (last column of the corrections).
+      const int n0 = 2 * c, n1 = 2 * c + 1;
+      const float e0 = n0 < rows ? exp2f(cs[n0 * a.ldxs + KB]) : 0.f;
+      const float e1 = n1 < rows ? exp2f(cs[n1 * a.ldxs + KB]) : 0.f;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xempty[xb]);  // X rows of this sub-unit consumed
+
+      // Every consumer warp reaches these barriers for every sub-unit, also
+      // after a failed wait; the abort decision is uniform (snapshot).
+      named_bar_sync(1, kCons);  // previous epilogue done with red / tile
+      if (tid == 0) *s_abort = *abort_flag;
+      if (par == 1) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) red[(rg * 32 + lane) * 4 + q] = acc[q];
+      }
+      named_bar_sync(1, kCons);
+      if (*s_abort) {
+        ok = false;
+        break;
+      }
+      if (par == 0) {
+        float v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[q] = acc[q] + red[(rg * 32 + lane) * 4 + q];
+        tile[r0w * (MP + 1) + n0] = v[0] * e0;
+        tile[r0w * (MP + 1) + n1] = v[1] * e1;
+        tile[r1w * (MP + 1) + n0] = v[2] * e0;
+        tile[r1w * (MP + 1) + n1] = v[3] * e1;
+      }
+      named_bar_sync(1, kCons);
+      if constexpr (EPI == kGvEpiSilu) {
+        for (int idx = tid; idx < 64 * rows; idx += kCons) {
+          const int jj = idx & 63, m = idx >> 6;
+          const float gt = tile[(2 * jj) * (MP + 1) + m];
+          const float up = tile[(2 * jj + 1) * (MP + 1) + m];
+          const int row = r0 + c0 + m;
+          __nv_bfloat16* orow = a.out_rows != nullptr
+                                    ? reinterpret_cast<__nv_bfloat16*>(a.out_rows[row])
+                                    : a.out + (size_t)row * a.ldo;
+          orow[rt * 64 + jj] = __float2bfloat16(gt / (1.f + __expf(-gt)) * up);
+        }
+      } else {
+        for (int idx = tid; idx < 16 * rows; idx += kCons) {
+          const int r8 = (idx & 15) * 8, m = idx >> 4;
+          const int row = r0 + c0 + m;
+          __nv_bfloat16* orow = a.out_rows != nullptr
+                                    ? reinterpret_cast<__nv_bfloat16*>(a.out_rows[row])
+                                    : a.out + (size_t)row * a.ldo;
+          uint4 o;
+          __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) oe[q] = __float2bfloat16(tile[(r8 + q) * (MP + 1) + m]);
+          *reinterpret_cast<uint4*>(orow + rt * 128 + r8) = o;
+        }
+      }
+    }
+  }
+}
+
+// Prepared activations for the grouped small-M kernel: one CTA per row.
+//   x16[r]  = fp16(x[src(r)] * 2^-e_r)  (e_r: smallest e >= 0 with max |x| <= 2^14 * 2^e)
+//   xsum[r] = [-sum_{k in kb} (c(k) + 8) * x16[r][k] for kb < K/128, e_r, 0...]
+// src(r) = perm[r] / k when perm is given (expert-order gather), else r.
+__global__ void moe_prep_fp16_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
+                                     const int* __restrict__ perm, int topk, int K,
+                                     __half* __restrict__ x16, int ldx16,
+                                     float* __restrict__ xsum, int ldxs) {
+  __shared__ float red[32];
+  __shared__ float s_exp;
+  const int r = blockIdx.x;
+  const int src = perm != nullptr ? perm[r] / topk : r;
+  const __nv_bfloat16* xr = x + (size_t)src * ldx;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float m = 0.f;
+  for (int i = threadIdx.x * 8; i < K; i += blockDim.x * 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(xr + i);
+    const __nv_bfloat16* v = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) m = fmaxf(m, fabsf(__bfloat162float(v[q])));
+  }
+  m = warp_max(m);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mx = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
+    s_exp = mx > 16384.f ? ceilf(log2f(mx / 16384.f)) : 0.f;
+  }
+  __syncthreads();
+  const float sc = exp2f(-s_exp);
+  // One warp per k-block: convert its 128 values and sum the corrections.
+  const int KB = K / 128;
+  for (int kb = warp; kb < KB; kb += blockDim.x >> 5) {
+    const int k0 = kb * 128 + lane * 4;
+    const uint2 u = *reinterpret_cast<const uint2*>(xr + k0);
+    const __nv_bfloat16* v = reinterpret_cast<const __nv_bfloat16*>(&u);
+    const __half2 h0 = __floats2half2_rn(__bfloat162float(v[0]) * sc, __bfloat162float(v[1]) * sc);
+    const __half2 h1 = __floats2half2_rn(__bfloat162float(v[2]) * sc, __bfloat162float(v[3]) * sc);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&h0);
+    o.y = *reinterpret_cast<const uint32_t*>(&h1);
+    *reinterpret_cast<uint2*>(x16 + (size_t)r * ldx16 + k0) = o;
+    // k % 8 = (lane * 4) % 8 + {0..3}: pairs z = (k % 8) / 2 -> c = {1032, 72, 1032, 72}
+    const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+    const float cz0 = ((lane & 1) == 0) ? 1032.f : 1032.f;  // pair (k%8)/2 = 0 or 2
+    const float cz1 = 72.f;                                   // pair 1 or 3
+    float sum = cz0 * (f0.x + f0.y) + cz1 * (f1.x + f1.y);
+    sum = warp_sum(sum);
+    if (lane == 0) xsum[(size_t)r * ldxs + kb] = -sum;
+  }
+  if (threadIdx.x == 0) xsum[(size_t)r * ldxs + KB] = s_exp;
+}
 }  // namespace
 
 bool gemv_eligible(int64_t M) { return M >= 1 && M <= kGemvMaxM; }
@@ -564,6 +878,82 @@ void gemv_launch(const void* x, int64_t ldx, const uint8_t* wblob, void* out, in
     else if (epilogue == kGvEpiSilu) gv_launch_nt<32, kGvEpiSilu>(NT, a, grid, smem, stream);
     else gv_launch_nt<32, kGvEpiResid>(NT, a, grid, smem, stream);
   }
+}
+
+// Prepared-activation layout of the grouped small-M kernel.
+static inline int gvg_ldx16(int K) { return K + 8; }                   // halves
+static inline int gvg_ldxs(int K) { return ((K / 128 + 1) + 3) / 4 * 4; }  // floats
+
+void moe_prep_fp16(torch::Tensor x, c10::optional<torch::Tensor> perm, int64_t topk,
+                   int64_t rows, torch::Tensor x16, torch::Tensor xsum) {
+  const int K = (int)x.size(1);
+  TORCH_CHECK(K % 128 == 0 && x.stride(1) == 1 && (x.stride(0) * 2) % 16 == 0, "x layout");
+  TORCH_CHECK(x16.size(1) == gvg_ldx16(K) && xsum.size(1) == gvg_ldxs(K), "prep buffers");
+  if (rows == 0) return;
+  const c10::cuda::CUDAGuard guard(x.device());
+  moe_prep_fp16_kernel<<<(unsigned)rows, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0),
+      perm.has_value() ? perm->data_ptr<int>() : nullptr, (int)topk, K,
+      reinterpret_cast<__half*>(x16.data_ptr()), (int)x16.size(1), xsum.data_ptr<float>(),
+      (int)xsum.size(1));
+  CB_CUDA_CHECK(cudaGetLastError());
+}
+
+std::vector<int64_t> moe_prep_shape(int64_t K) { return {gvg_ldx16((int)K), gvg_ldxs((int)K)}; }
+
+template <int EPI>
+static void gvg_launch(const GvgArgs& a, int grid, int smem, cudaStream_t stream) {
+  static int configured[64] = {};
+  int dev = 0;
+  CB_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    CB_CUDA_CHECK(cudaFuncSetAttribute(w4a16_gemv_grouped_kernel<EPI>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kGvSmemBudget + 4096));
+    if (dev >= 0 && dev < 64) configured[dev] = 1;
+  }
+  w4a16_gemv_grouped_kernel<EPI><<<grid, kGvThreads, smem, stream>>>(a);
+  CB_CUDA_CHECK(cudaGetLastError());
+}
+
+// Grouped small-M W4A16 (group 128): x16 / xsum from moe_prep_fp16, rows of
+// expert e are [offsets[e], offsets[e+1]); epilogue store or SiLU(gate)*up.
+void w4a16_gemv_grouped(torch::Tensor x16, torch::Tensor xsum, torch::Tensor wblob,
+                        torch::Tensor out, int64_t N, int64_t epilogue, torch::Tensor offsets,
+                        int64_t num_groups, torch::Tensor status,
+                        c10::optional<torch::Tensor> out_rows) {
+  const int K = (int)(x16.size(1) - 8);
+  TORCH_CHECK(K % 128 == 0 && N % 128 == 0, "K and N must be multiples of 128");
+  TORCH_CHECK(epilogue == kGvEpiStore || epilogue == kGvEpiSilu, "store or SiLU epilogue");
+  const int64_t per = (int64_t)(N / 128) * (K / 128) * GvBlob<128>::kBytes;
+  TORCH_CHECK(wblob.numel() == per * num_groups, "weight blob has wrong size");
+  if (num_groups == 0) return;
+  const c10::cuda::CUDAGuard guard(x16.device());
+  GvgArgs a{};
+  a.wblob = wblob.data_ptr<uint8_t>();
+  a.blob_stride = per;
+  a.x16 = reinterpret_cast<const __half*>(x16.data_ptr());
+  a.xsum = xsum.data_ptr<float>();
+  a.offsets = offsets.data_ptr<int>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.out_rows = out_rows.has_value()
+                   ? reinterpret_cast<const long long*>(out_rows->data_ptr<int64_t>())
+                   : nullptr;
+  a.status = status.data_ptr<int>();
+  a.E = (int)num_groups;
+  a.N = (int)N;
+  a.K = K;
+  a.ldx16 = (int)x16.size(1);
+  a.ldxs = (int)xsum.size(1);
+  a.ldo = (int)out.stride(0);
+  const int fixed = (8 * 32 * 4 + 128 * 9) * 4 + 2 * (8 * a.ldx16 * 2 + 8 * a.ldxs * 4) + 1024;
+  a.stages = std::max(2, std::min(10, (kGvSmemBudget - fixed) / GvBlob<128>::kStage));
+  const int smem = a.stages * GvBlob<128>::kStage + fixed;
+  const int units = (int)num_groups * (int)(N / 128);
+  const int grid = std::max(1, std::min(units, num_sms()));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (epilogue == kGvEpiSilu) gvg_launch<kGvEpiSilu>(a, grid, smem, stream);
+  else gvg_launch<kGvEpiStore>(a, grid, smem, stream);
 }
 
 // Python binding: explicit small-M path (tests and the microbenchmark).

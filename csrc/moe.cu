@@ -30,21 +30,31 @@ constexpr int kGateThreads = 256;
 constexpr int kMaxExperts = 512;
 constexpr int kMaxTopK = 16;
 
+// Grid (T, G): CTA (t, g) computes the logits of experts [32g, 32g + 32)
+// for token t (one warp per 4 experts, 16-byte loads) into the fp32
+// workspace; the last CTA of token t (per-token counter, left at zero again)
+// then applies the score function and picks the top-k.  Splitting the
+// experts over G CTAs puts T * G CTAs on the router GEMV instead of T.
+constexpr int kGateExpertsPerCta = 32;
+
 __global__ void __launch_bounds__(kGateThreads) moe_topk_gate_kernel(
     const bf16* __restrict__ x, int ldx, const bf16* __restrict__ wg,
     const float* __restrict__ bias, int H, int E, int k, int scoring, int norm_topk,
     float routed_scale, int* __restrict__ topk_ids, float* __restrict__ topk_w,
-    float* __restrict__ logits_out) {
+    float* __restrict__ logits, int* __restrict__ counters) {
   __shared__ float s_score[kMaxExperts];
   __shared__ float s_sel[kMaxExperts];
   __shared__ float s_red_v[32];
   __shared__ int s_red_i[32];
+  __shared__ int s_last;
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nw = blockDim.x >> 5;
   const bf16* xr = x + (size_t)t * ldx;
-  // 1. logits: each warp owns experts e = warp, warp + nw, ...
-  for (int e = warp; e < E; e += nw) {
+  // 1. logits of this CTA's experts.
+  const int e0 = blockIdx.y * kGateExpertsPerCta;
+  const int e1 = min(E, e0 + kGateExpertsPerCta);
+  for (int e = e0 + warp; e < e1; e += nw) {
     const bf16* wr = wg + (size_t)e * H;
     float acc = 0.f;
     for (int i = lane * 8; i < H; i += 32 * 8) {
@@ -56,11 +66,20 @@ __global__ void __launch_bounds__(kGateThreads) moe_topk_gate_kernel(
       for (int q = 0; q < 8; ++q) acc += __bfloat162float(xv[q]) * __bfloat162float(wv[q]);
     }
     acc = warp_sum(acc);
-    if (lane == 0) s_score[e] = acc;
+    if (lane == 0) logits[(size_t)t * E + e] = acc;
   }
   __syncthreads();
-  if (logits_out != nullptr)
-    for (int e = threadIdx.x; e < E; e += blockDim.x) logits_out[(size_t)t * E + e] = s_score[e];
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int prev = atomicAdd(&counters[t], 1);
+    s_last = prev == (int)gridDim.y - 1;
+    if (s_last) counters[t] = 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_score[e] = __ldcg(&logits[(size_t)t * E + e]);
+  __syncthreads();
   // 2. score function.
   if (scoring == 0) {
     float mx = -INFINITY;
@@ -149,21 +168,23 @@ __global__ void __launch_bounds__(kGateThreads) moe_topk_gate_kernel(
 
 void moe_topk_gate(torch::Tensor x, torch::Tensor wg, c10::optional<torch::Tensor> bias,
                    int64_t k, int64_t scoring, bool norm_topk, double routed_scale,
-                   torch::Tensor topk_ids, torch::Tensor topk_w,
-                   c10::optional<torch::Tensor> logits_out) {
+                   torch::Tensor topk_ids, torch::Tensor topk_w, torch::Tensor logits,
+                   torch::Tensor counters) {
   const int T = (int)x.size(0);
   const int H = (int)x.size(1);
   const int E = (int)wg.size(0);
   TORCH_CHECK(E <= kMaxExperts && k <= kMaxTopK && k <= E, "unsupported expert count / top-k");
   TORCH_CHECK(H % 8 == 0 && x.stride(1) == 1 && wg.is_contiguous(), "layout");
+  TORCH_CHECK(logits.numel() >= (int64_t)T * E && counters.numel() >= T, "gate workspace");
   if (T == 0) return;
   const c10::cuda::CUDAGuard guard(x.device());
-  moe_topk_gate_kernel<<<T, kGateThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+  const dim3 grid(T, (E + kGateExpertsPerCta - 1) / kGateExpertsPerCta);
+  moe_topk_gate_kernel<<<grid, kGateThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const bf16*>(x.data_ptr()), (int)x.stride(0),
       reinterpret_cast<const bf16*>(wg.data_ptr()),
       bias.has_value() ? bias->data_ptr<float>() : nullptr, H, E, (int)k, (int)scoring,
       norm_topk ? 1 : 0, (float)routed_scale, topk_ids.data_ptr<int>(), topk_w.data_ptr<float>(),
-      logits_out.has_value() ? logits_out->data_ptr<float>() : nullptr);
+      logits.data_ptr<float>(), counters.data_ptr<int>());
   CB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -97,6 +97,40 @@ def test_grouped_gemm_large_groups():
     _grouped_case(len(rows), rows, 256, 512, 128, ops.EPI_STORE, seed=3)
 
 
+@pytest.mark.parametrize("rows", [[3, 0, 1, 7, 0, 0, 12, 2], [1, 1, 1, 1], [0, 0, 20, 0]])
+@pytest.mark.parametrize("epi", [ops.EPI_STORE, ops.EPI_SILU])
+def test_grouped_small_m(rows, epi):
+    """Grouped small-M kernel on prepared activations (fp16, scaled, with
+    offset corrections), including experts with more than 8 rows."""
+    g = torch.Generator().manual_seed(sum(rows) + epi)
+    G, N, K = len(rows), 512, 768
+    ws = [Int4Weight.random(N, K, 0.05, 128, generator=g) for _ in range(G)]
+    offs = [0]
+    for r in rows:
+        offs.append(offs[-1] + r)
+    M = offs[-1]
+    x = (torch.randn(M, K, generator=g) * 0.5).to(torch.bfloat16)
+    x[0, :5] = 3e4  # one huge activation: exercises the per-row fp16 scaling
+    inter = epi == ops.EPI_SILU
+    blob = torch.cat([w.to(DEV).blob(interleave_gate_up=inter) for w in ws])
+    x16, xs = ops.moe_prep_fp16(x.to(DEV), M)
+    out = ops.w4a16_gemv_grouped(x16, xs, blob, N, epi,
+                                 torch.tensor(offs, dtype=torch.int32, device=DEV), G)
+    torch.cuda.synchronize()
+    assert ops.read_status(DEV) == 0
+    out = out.float().cpu()
+    for e in range(G):
+        if rows[e] == 0:
+            continue
+        wq = (ws[e].unpack().float() - 8.0) * ws[e].scales.float().repeat_interleave(128, dim=1)
+        y = x[offs[e]:offs[e + 1]].float() @ wq.t()
+        if inter:
+            y = ref.silu_mul(y[:, :N // 2], y[:, N // 2:])
+        got = out[offs[e]:offs[e + 1]]
+        err = (got - y).abs().max().item()
+        assert err <= 0.01 * y.abs().max().item() + 1e-2, (e, err)
+
+
 def test_combine():
     g = torch.Generator().manual_seed(4)
     T, k, H = 33, 4, 384
