@@ -242,6 +242,8 @@ def main():
     clocks = sampler.stop()
 
     # ---- TTFT: batch-1 prefill of a P-token prompt, through the API ----
+    if ep is not None:
+        ep.row_bound = P
     ttfts = []
     for r in range(args.ttft_reps):
         sid = f"ttft{r}"

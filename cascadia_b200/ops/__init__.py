@@ -311,15 +311,18 @@ def w4a16_gemm_grouped(x, blob, n: int, group_size: int, epilogue: int, offsets,
     return out
 
 
-def moe_prep_fp16(x, rows: int, perm=None, topk: int = 1):
+def moe_prep_fp16(x, rows: int, perm=None, topk: int = 1, rows_dev=None, out=None):
     """Prepared activations for the grouped small-M GEMM: fp16 rows (scaled
     by a power of two per row) and per-k-block offset corrections.  Row r is
     x[perm[r] // topk] when ``perm`` is given (gather into expert order)."""
     K = x.shape[1]
     ld16, lds = ext().moe_prep_shape(K)
-    x16 = torch.empty(max(1, rows), ld16, dtype=torch.float16, device=x.device)
-    xs = torch.empty(max(1, rows), lds, dtype=torch.float32, device=x.device)
-    ext().moe_prep_fp16(x, perm, topk, rows, x16, xs)
+    if out is not None:
+        x16, xs = out
+    else:
+        x16 = torch.empty(max(1, rows), ld16, dtype=torch.float16, device=x.device)
+        xs = torch.empty(max(1, rows), lds, dtype=torch.float32, device=x.device)
+    ext().moe_prep_fp16(x, perm, topk, rows, x16, xs, rows_dev)
     LAUNCHES.add(1)
     return x16, xs
 

@@ -30,6 +30,9 @@ import torch.distributed as dist
 
 from .. import ops
 
+# Tokens per rank up to this use the grouped small-M expert kernel (decode).
+SMALL_M_TOKENS = 64
+
 
 class ExpertParallel:
     def __init__(self, group, rank: int, world: int, device, num_experts: int, hidden: int,
@@ -106,17 +109,30 @@ class ExpertParallel:
         this for every MoE layer, in the same order)."""
         T = h.shape[0]
         assert T <= self.max_tokens, f"{T} tokens > EP capacity {self.max_tokens}"
+        assert T <= self.row_bound, f"{T} tokens > the row bound {self.row_bound} set for this call"
         e = ops.ext()
         c = self._common()
         e.ep_dispatch(h, ids, self.dest, self.pos, self.send_cnt, *c)
         e.ep_receive(self.xp, self.offsets, self.src_row, self.out_rows, self.total, *c)
         max_rows = self.world * self.row_bound  # each token reaches an expert at most once
-        act = ops.w4a16_gemm_grouped(self.xp, bank.gu_blob, 2 * bank.inter, bank.gs,
-                                     ops.EPI_SILU, self.offsets, self.e_local, max_rows)
-        ops.w4a16_gemm_grouped(act, bank.dn_blob, bank.hidden, bank.gs, ops.EPI_STORE,
-                               self.offsets, self.e_local, max_rows, out_rows=self.out_rows)
+        if self.row_bound <= SMALL_M_TOKENS and bank.gs == 128:
+            # Decode: grouped small-M kernel on fp16-prepared rows; the down
+            # projection's epilogue still stores into the sources' regions.
+            rows = min(self.world * self.row_bound * self.k, self.xp.shape[0])
+            x16, xs = ops.moe_prep_fp16(self.xp, rows, rows_dev=self.total)
+            act = ops.w4a16_gemv_grouped(x16, xs, bank.gu_blob, 2 * bank.inter, ops.EPI_SILU,
+                                         self.offsets, self.e_local)
+            a16, a_s = ops.moe_prep_fp16(act, rows, rows_dev=self.total)
+            ops.w4a16_gemv_grouped(a16, a_s, bank.dn_blob, bank.hidden, ops.EPI_STORE,
+                                   self.offsets, self.e_local, out=act[:1, :0],
+                                   out_rows=self.out_rows)
+        else:
+            act = ops.w4a16_gemm_grouped(self.xp, bank.gu_blob, 2 * bank.inter, bank.gs,
+                                         ops.EPI_SILU, self.offsets, self.e_local, max_rows)
+            ops.w4a16_gemm_grouped(act, bank.dn_blob, bank.hidden, bank.gs, ops.EPI_STORE,
+                                   self.offsets, self.e_local, max_rows, out_rows=self.out_rows)
         e.ep_combine(w, self.dest, self.pos, add, out, *c)
-        ops.LAUNCHES.add(8)
+        ops.LAUNCHES.add(6)
         return out
 
     def moe_a2a(self, bank, h, ids, w, add, out):

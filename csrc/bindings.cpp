@@ -40,7 +40,8 @@ void w4a16_gemv(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
                 int64_t forced_splits);
 int64_t gemv_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t forced_splits);
 void moe_prep_fp16(torch::Tensor x, c10::optional<torch::Tensor> perm, int64_t topk,
-                   int64_t rows, torch::Tensor x16, torch::Tensor xsum);
+                   int64_t rows, torch::Tensor x16, torch::Tensor xsum,
+                   c10::optional<torch::Tensor> rows_dev);
 std::vector<int64_t> moe_prep_shape(int64_t K);
 void w4a16_gemv_grouped(torch::Tensor x16, torch::Tensor xsum, torch::Tensor wblob,
                         torch::Tensor out, int64_t N, int64_t epilogue, torch::Tensor offsets,

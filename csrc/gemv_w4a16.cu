@@ -532,6 +532,7 @@ struct GvgArgs {
   const __half* x16;         // [R, ldx16] fp16 rows
   const float* xsum;         // [R, ldxs]: -sum (c(k) + 8) x per k-block, then the exponent
   const int* offsets;        // [E + 1]
+  int R;                     // prepared rows: rows at or past R are never read
   __nv_bfloat16* out;        // [R, ldo]
   const long long* out_rows; // optional per-row destination addresses
   int* status;
@@ -585,7 +586,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_grouped_kernel(const
       bool go = true;
       for (int u = blockIdx.x; u < a.E * RT && go; u += gridDim.x) {
         const int e = u / RT, rt = u % RT;
-        const int r0 = a.offsets[e], n = a.offsets[e + 1] - r0;
+        const int r0 = a.offsets[e], n = min(a.offsets[e + 1], a.R) - r0;
         const uint8_t* wsrc = a.wblob + (size_t)e * a.blob_stride + (size_t)rt * KB * Blob::kBytes;
         for (int c0 = 0; c0 < n && go; c0 += MP, ++sub) {
           const int rows = min(MP, n - c0);
@@ -641,7 +642,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_grouped_kernel(const
   bool ok = true;
   for (int u = blockIdx.x; u < a.E * RT && ok; u += gridDim.x) {
     const int e = u / RT, rt = u % RT;
-    const int r0 = a.offsets[e], n = a.offsets[e + 1] - r0;
+    const int r0 = a.offsets[e], n = min(a.offsets[e + 1], a.R) - r0;
     for (int c0 = 0; c0 < n && ok; c0 += MP, ++sub) {
       const int rows = min(MP, n - c0);
       const int xb = sub & 1;
@@ -780,10 +781,13 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_grouped_kernel(const
 __global__ void moe_prep_fp16_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                                      const int* __restrict__ perm, int topk, int K,
                                      __half* __restrict__ x16, int ldx16,
-                                     float* __restrict__ xsum, int ldxs) {
+                                     float* __restrict__ xsum, int ldxs, int rows,
+                                     const int* __restrict__ rows_dev) {
   __shared__ float red[32];
   __shared__ float s_exp;
-  const int r = blockIdx.x;
+  const int nrows = rows_dev != nullptr ? min(rows, *rows_dev) : rows;
+  for (int r = blockIdx.x; r < nrows; r += gridDim.x) {
+  __syncthreads();
   const int src = perm != nullptr ? perm[r] / topk : r;
   const __nv_bfloat16* xr = x + (size_t)src * ldx;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -825,6 +829,7 @@ __global__ void moe_prep_fp16_kernel(const __nv_bfloat16* __restrict__ x, int ld
     if (lane == 0) xsum[(size_t)r * ldxs + kb] = -sum;
   }
   if (threadIdx.x == 0) xsum[(size_t)r * ldxs + KB] = s_exp;
+  }
 }
 }  // namespace
 
@@ -885,17 +890,21 @@ static inline int gvg_ldx16(int K) { return K + 8; }                   // halves
 static inline int gvg_ldxs(int K) { return ((K / 128 + 1) + 3) / 4 * 4; }  // floats
 
 void moe_prep_fp16(torch::Tensor x, c10::optional<torch::Tensor> perm, int64_t topk,
-                   int64_t rows, torch::Tensor x16, torch::Tensor xsum) {
+                   int64_t rows, torch::Tensor x16, torch::Tensor xsum,
+                   c10::optional<torch::Tensor> rows_dev) {
   const int K = (int)x.size(1);
   TORCH_CHECK(K % 128 == 0 && x.stride(1) == 1 && (x.stride(0) * 2) % 16 == 0, "x layout");
   TORCH_CHECK(x16.size(1) == gvg_ldx16(K) && xsum.size(1) == gvg_ldxs(K), "prep buffers");
   if (rows == 0) return;
   const c10::cuda::CUDAGuard guard(x.device());
-  moe_prep_fp16_kernel<<<(unsigned)rows, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  // Grid-stride over rows; with rows_dev (a device row count, e.g. the rows
+  // an expert-parallel receive produced) only that many rows are prepared.
+  const unsigned grid = (unsigned)std::min<int64_t>(rows, rows_dev.has_value() ? 592 : rows);
+  moe_prep_fp16_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0),
       perm.has_value() ? perm->data_ptr<int>() : nullptr, (int)topk, K,
       reinterpret_cast<__half*>(x16.data_ptr()), (int)x16.size(1), xsum.data_ptr<float>(),
-      (int)xsum.size(1));
+      (int)xsum.size(1), (int)rows, rows_dev.has_value() ? rows_dev->data_ptr<int>() : nullptr);
   CB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -928,6 +937,9 @@ void w4a16_gemv_grouped(torch::Tensor x16, torch::Tensor xsum, torch::Tensor wbl
   const int64_t per = (int64_t)(N / 128) * (K / 128) * GvBlob<128>::kBytes;
   TORCH_CHECK(wblob.numel() == per * num_groups, "weight blob has wrong size");
   if (num_groups == 0) return;
+  TORCH_CHECK(out_rows.has_value() || out.size(0) >= std::min(x16.size(0), xsum.size(0)),
+              "out has fewer rows than the prepared activations");
+  TORCH_CHECK(!out_rows.has_value() || out_rows->numel() >= x16.size(0), "out_rows too short");
   const c10::cuda::CUDAGuard guard(x16.device());
   GvgArgs a{};
   a.wblob = wblob.data_ptr<uint8_t>();
@@ -935,6 +947,7 @@ void w4a16_gemv_grouped(torch::Tensor x16, torch::Tensor xsum, torch::Tensor wbl
   a.x16 = reinterpret_cast<const __half*>(x16.data_ptr());
   a.xsum = xsum.data_ptr<float>();
   a.offsets = offsets.data_ptr<int>();
+  a.R = (int)std::min(x16.size(0), xsum.size(0));
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   a.out_rows = out_rows.has_value()
                    ? reinterpret_cast<const long long*>(out_rows->data_ptr<int64_t>())
