@@ -94,6 +94,27 @@ def _hold_back(text: str, stops: List[str]) -> int:
     return hold
 
 
+# Self-contained status page: polls the two JSON routes (no assets, no
+# graphics API; the reference serves a placeholder page the same way,
+# crates/cascadia-dashboard/src/lib.rs:85-93).
+DASHBOARD_HTML = """<!doctype html><html><head><meta charset="utf-8">
+<title>cascadia-b200</title><style>body{font-family:sans-serif;margin:2em}
+table{border-collapse:collapse}td,th{border:1px solid #999;padding:4px 8px}</style></head>
+<body><h2>cascadia-b200</h2><div id="stats"></div><h3>Nodes</h3><table id="nodes"></table>
+<h3>Links</h3><table id="edges"></table><script>
+async function refresh(){
+ const s=await (await fetch('/api/stats')).json();
+ document.getElementById('stats').textContent=JSON.stringify(s);
+ const t=await (await fetch('/api/topology')).json();
+ let h='<tr><th>node</th><th>device</th><th>memory MB</th><th>engines</th></tr>';
+ for(const n of t.nodes){h+=`<tr><td>${n.node_id}</td><td>${n.device}</td><td>${n.memory_mb}</td><td>${(n.engines||[]).join(',')}</td></tr>`;}
+ document.getElementById('nodes').innerHTML=h;
+ h='<tr><th>src</th><th>dst</th><th>latency ms</th><th>bandwidth MB/s</th></tr>';
+ for(const e of t.edges){h+=`<tr><td>${e.src}</td><td>${e.dst}</td><td>${e.latency_ms.toFixed(4)}</td><td>${e.bandwidth_mbps.toFixed(0)}</td></tr>`;}
+ document.getElementById('edges').innerHTML=h;}
+refresh();setInterval(refresh,5000);</script></body></html>"""
+
+
 def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStats] = None,
              topology=None) -> FastAPI:
     cfg = config or ApiConfig()
@@ -150,6 +171,12 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
     @app.get("/api/topology")
     async def topology_route():
         return topology.to_json() if topology is not None else {"nodes": [], "edges": []}
+
+    @app.get("/")
+    async def dashboard_route():
+        from fastapi.responses import HTMLResponse
+
+        return HTMLResponse(DASHBOARD_HTML)
 
     def _sampling(body: dict) -> (SamplingParams, float):
         stop = body.get("stop")

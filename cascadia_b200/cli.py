@@ -66,8 +66,15 @@ def _serve(runner, api: str, model_name: str, max_concurrent: int):
     from .api.server import ApiConfig, make_app
 
     host, port = _parse_hostport(api, "0.0.0.0")
+    topo = None
+    try:
+        from .topology import local_gpu_topology
+
+        topo = local_gpu_topology(api_port=port, engines=[model_name])
+    except Exception:  # no GPU / no CUDA: serve an empty topology
+        topo = None
     app = make_app(runner, ApiConfig(model_name=model_name,
-                                     max_concurrent_requests=max_concurrent))
+                                     max_concurrent_requests=max_concurrent), topology=topo)
     uvicorn.run(app, host=host, port=port, log_level="warning")
 
 
@@ -213,6 +220,14 @@ def cmd_doctor(args):
     sys.exit(0 if report.get("ok") else 1)
 
 
+def cmd_topology(args):
+    """Print this host's GPU topology (with --probe: measured NVLink edges)."""
+    from .topology import local_gpu_topology
+
+    print(json.dumps(local_gpu_topology(probe=args.probe, probe_mb=args.probe_mb).to_json(),
+                     indent=1))
+
+
 def cmd_place(args):
     from .utils.placement import choose_parallelism
 
@@ -254,6 +269,10 @@ def main(argv=None):
 
     sub.add_parser("engines", help="list engines").set_defaults(fn=cmd_engines)
     sub.add_parser("doctor", help="check CUDA / NCCL / NVLink").set_defaults(fn=cmd_doctor)
+    tp_ = sub.add_parser("topology", help="GPU nodes and measured NVLink links (JSON)")
+    tp_.add_argument("--probe", action="store_true", help="measure peer bandwidth / latency")
+    tp_.add_argument("--probe-mb", type=int, default=256)
+    tp_.set_defaults(fn=cmd_topology)
 
     pl = sub.add_parser("place", help="choose a PP x TP x EP split")
     pl.add_argument("--model", required=True)
