@@ -161,7 +161,12 @@ def main():
             ep = ExpertParallel(group, rank, world, dev, cfg.num_experts, cfg.hidden_size,
                                 cfg.num_experts_per_tok, max_tokens=4096,
                                 fused=args.tp_comm == "fused")
-        model = MoEModel(cfg, dev, ep=ep).init_random(seed=1234)
+        if cfg.is_mla:
+            from cascadia_b200.models.mla import MLAModel
+
+            model = MLAModel(cfg, dev, ep=ep).init_random(seed=1234)
+        else:
+            model = MoEModel(cfg, dev, ep=ep).init_random(seed=1234)
     else:
         model = LlamaModel(cfg, dev, tp=tp).init_random(seed=1234)
     torch.cuda.synchronize()

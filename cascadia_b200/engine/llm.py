@@ -418,6 +418,10 @@ class LLMBuilder(Builder):
 
     def model_class(self, cfg):
         """Dense Llama-family model, or the sparse-MoE model for MoE configs."""
+        if cfg.is_mla:
+            from ..models.mla import MLAModel
+
+            return MLAModel
         if cfg.is_moe:
             from ..models.moe import MoEModel
 

@@ -22,4 +22,8 @@ class MoEBuilder(LLMBuilder):
 
         if not cfg.is_moe:
             raise InvalidConfig(f"{self.model_name}: not a sparse-MoE config")
+        if cfg.is_mla:
+            from ..models.mla import MLAModel
+
+            return MLAModel
         return MoEModel

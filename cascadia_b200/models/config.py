@@ -145,6 +145,9 @@ PRESETS = {
                            routed_scaling_factor=2.827, first_k_dense_replace=1,
                            q_lora_rank=1536, kv_lora_rank=512, qk_rope_head_dim=64,
                            qk_nope_head_dim=128, v_head_dim=128, group_size=32,
+                           rope_scaling={"rope_type": "yarn", "factor": 64.0, "beta_fast": 32.0,
+                                         "beta_slow": 1.0, "mscale": 1.0, "mscale_all_dim": 1.0,
+                                         "original_max_position_embeddings": 4096},
                            eos_token_ids=(163586,)),
     # Small shapes for tests (same code paths).
     "tiny-llama": ModelConfig(vocab_size=512, hidden_size=256, num_layers=2, num_heads=4,
@@ -157,13 +160,20 @@ PRESETS = {
                             num_heads=4, num_kv_heads=2, head_dim=64, intermediate_size=512,
                             num_experts=8, num_experts_per_tok=2, moe_intermediate_size=128,
                             router="softmax", qk_norm=True, eos_token_ids=(1,)),
-    "tiny-mla": ModelConfig(arch="kimi_k2", vocab_size=512, hidden_size=256, num_layers=2,
-                            num_heads=4, num_kv_heads=4, head_dim=96, intermediate_size=512,
+    # Kimi-K2 layer structure at small width; the MLA latent (512) and rope
+    # (64) widths are the real ones (the decode kernel is built for them).
+    "tiny-mla": ModelConfig(arch="kimi_k2", vocab_size=512, hidden_size=256, num_layers=3,
+                            num_heads=20, num_kv_heads=20, head_dim=192, intermediate_size=512,
                             num_experts=8, num_experts_per_tok=2, moe_intermediate_size=128,
                             num_shared_experts=1, router="sigmoid", routed_scaling_factor=2.5,
-                            first_k_dense_replace=1, q_lora_rank=128, kv_lora_rank=128,
-                            qk_rope_head_dim=32, qk_nope_head_dim=64, v_head_dim=64,
-                            group_size=32, eos_token_ids=(1,)),
+                            first_k_dense_replace=1, q_lora_rank=128, kv_lora_rank=512,
+                            qk_rope_head_dim=64, qk_nope_head_dim=128, v_head_dim=128,
+                            group_size=32, rope_theta=50000.0,
+                            rope_scaling={"rope_type": "yarn", "factor": 64.0, "beta_fast": 32.0,
+                                          "beta_slow": 1.0, "mscale": 1.0,
+                                          "mscale_all_dim": 1.0,
+                                          "original_max_position_embeddings": 4096},
+                            eos_token_ids=(1,)),
 }
 
 
@@ -189,7 +199,38 @@ def rope_inv_freq(cfg: ModelConfig, rot: Optional[int] = None) -> torch.Tensor:
         smooth = (old / wl - low) / (high - low)
         mid = (1 - smooth) * inv / factor + smooth * inv
         inv = torch.where(wl < high_wl, inv, torch.where(wl > low_wl, inv / factor, mid))
+    elif sc and sc.get("rope_type", sc.get("type")) == "yarn":
+        # YaRN blend of extrapolated and interpolated frequencies
+        # (crates/cascadia-int4-gemm/src/shell.rs:395-429, the published
+        # YaRN correction-dimension ramp).
+        factor = float(sc["factor"])
+        base = cfg.rope_theta
+        old = float(sc.get("original_max_position_embeddings", 4096))
+        beta_fast = float(sc.get("beta_fast", 32.0))
+        beta_slow = float(sc.get("beta_slow", 1.0))
+
+        def corr_dim(n_rot):
+            return (rot * math.log(old / (n_rot * 2 * math.pi))) / (2 * math.log(base))
+        low = max(math.floor(corr_dim(beta_fast)), 0.0)
+        high = min(math.ceil(corr_dim(beta_slow)), rot - 1.0)
+        denom = high - low if abs(high - low) > 1e-6 else 0.001
+        i = torch.arange(rot // 2, dtype=torch.float64)
+        ramp = ((i - low) / denom).clamp(0.0, 1.0)
+        inv_mask = 1.0 - ramp
+        inv = (inv / factor) * (1.0 - inv_mask) + inv * inv_mask
     return inv.float()
+
+
+def rope_mscale(cfg: ModelConfig) -> float:
+    """Attention scale factor folded into cos / sin (YaRN mscale ratio)."""
+    sc = cfg.rope_scaling
+    if not (sc and sc.get("rope_type", sc.get("type")) == "yarn"):
+        return 1.0
+
+    def get(scale, m):
+        return 1.0 if scale <= 1.0 else 0.1 * m * math.log(scale) + 1.0
+    f = float(sc["factor"])
+    return get(f, float(sc.get("mscale", 1.0))) / get(f, float(sc.get("mscale_all_dim", 1.0)))
 
 
 def rope_table(cfg: ModelConfig, max_pos: int, rot: Optional[int] = None,
@@ -197,4 +238,5 @@ def rope_table(cfg: ModelConfig, max_pos: int, rot: Optional[int] = None,
     """[max_pos, rot] fp32: cos in the first rot/2 columns, sin in the rest."""
     inv = rope_inv_freq(cfg, rot)
     ang = torch.outer(torch.arange(max_pos, dtype=torch.float32), inv)
-    return torch.cat([ang.cos(), ang.sin()], dim=1).to(device)
+    ms = rope_mscale(cfg)
+    return (torch.cat([ang.cos(), ang.sin()], dim=1) * ms).to(device)

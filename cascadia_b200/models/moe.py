@@ -116,15 +116,7 @@ class MoEModel(LlamaModel):
         ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=self.device)  # noqa: E731
         for li in range(self.layer_start, self.layer_end):
             g = _layer_generator(seed, li, dev)
-            qkv_rows = (cfg.num_heads + 2 * cfg.num_kv_heads) * d
-            if self.bf16_attention:
-                qkv = BF16Linear(torch.randn(qkv_rows, h, generator=g, device=dev) * std,
-                                 self.device)
-                o = BF16Linear(torch.randn(h, cfg.num_heads * d, generator=g, device=dev) * std,
-                               self.device)
-            else:
-                qkv = QLinear(random_int4(qkv_rows, h, g, dev, std, gs), self.device)
-                o = QLinear(random_int4(h, cfg.num_heads * d, g, dev, std, gs), self.device)
+            qkv, o = self._init_attention(g, dev, std)
             dense = router = bias = bank = shared = None
             if li < cfg.first_k_dense_replace:
                 I = cfg.intermediate_size
@@ -167,6 +159,20 @@ class MoEModel(LlamaModel):
             g = _layer_generator(seed, 100001, dev)
             self.lm_head = QLinear(random_int4(cfg.vocab_size, h, g, dev, std, gs), self.device)
         return self
+
+    def _init_attention(self, g, dev, std):
+        """(qkv, o) projections of one layer, drawn from the layer generator."""
+        cfg = self.cfg
+        h, d, gs = cfg.hidden_size, cfg.head_dim, cfg.group_size
+        qkv_rows = (cfg.num_heads + 2 * cfg.num_kv_heads) * d
+        if self.bf16_attention:
+            qkv = BF16Linear(torch.randn(qkv_rows, h, generator=g, device=dev) * std, self.device)
+            o = BF16Linear(torch.randn(h, cfg.num_heads * d, generator=g, device=dev) * std,
+                           self.device)
+        else:
+            qkv = QLinear(random_int4(qkv_rows, h, g, dev, std, gs), self.device)
+            o = QLinear(random_int4(h, cfg.num_heads * d, g, dev, std, gs), self.device)
+        return qkv, o
 
     # ------------------------------------------------------------ forward
     def forward(self, batch: Batch, hidden: torch.Tensor) -> torch.Tensor:

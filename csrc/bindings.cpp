@@ -17,6 +17,15 @@ void w4a16_gemm_grouped(torch::Tensor x, torch::Tensor wblob, torch::Tensor out,
                         int64_t group_size, int64_t epilogue, torch::Tensor group_offsets,
                         int64_t num_groups, int64_t max_rows_per_group, torch::Tensor status,
                         c10::optional<torch::Tensor> out_rows);
+// mla.cu
+void mla_rope_write(torch::Tensor ckv, torch::Tensor kr, torch::Tensor qrope,
+                    int64_t q_head_stride, torch::Tensor q_out, torch::Tensor positions,
+                    torch::Tensor cos_sin, torch::Tensor slots, torch::Tensor cache,
+                    int64_t layer, int64_t heads);
+void mla_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables,
+                torch::Tensor seq_lens, torch::Tensor out, int64_t layer, int64_t num_splits,
+                int64_t blocks_per_split, torch::Tensor part_o, torch::Tensor part_ml,
+                double scale, torch::Tensor status);
 // ep.cu
 void ep_dispatch(torch::Tensor x, torch::Tensor ids, torch::Tensor dest, torch::Tensor pos,
                  torch::Tensor send_cnt, torch::Tensor xbuf_ptrs, torch::Tensor rbuf_ptrs,
@@ -108,6 +117,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_permute", &cb::moe_permute);
   m.def("moe_combine", &cb::moe_combine);
   m.def("ep_dispatch", &cb::ep_dispatch);
+  m.def("mla_rope_write", &cb::mla_rope_write);
+  m.def("mla_decode", &cb::mla_decode);
   m.def("ep_receive", &cb::ep_receive);
   m.def("ep_combine", &cb::ep_combine);
   m.def("head_rmsnorm", &cb::head_rmsnorm);

@@ -27,6 +27,7 @@ SOURCES = [
     "moe.cu",
     "gemv_w4a16.cu",
     "ep.cu",
+    "mla.cu",
 ]
 
 NVCC_FLAGS = [
