@@ -32,6 +32,7 @@ from ..ops import reference as ref
 from ..runtime.generator import DecodeGraph
 from ..runtime.kv_cache import BLOCK_SIZE
 from ..runtime.scheduler import PrefixCache, SchedulerState, Sequence
+from ..utils.trace import span, task_done
 from ..types import Chunk, FinishReason, GenerationTask, LoadProgress, PeerLayout, ShardSpec
 from .base import Builder, Engine, EngineError, InvalidConfig, NotLoaded, PromptTooLong, QueueFull
 
@@ -126,6 +127,7 @@ class LLMEngine(Engine):
         if blocks_needed > self.model.kv.num_blocks:
             raise PromptTooLong(f"{len(ids)} tokens exceed the KV cache")
         seq = Sequence(task=task, prompt_ids=ids, seq_id=task.task_id)
+        seq.submitted_at = time.monotonic()
         self.sched.add(seq)
         self.decoders[task.task_id] = IncrementalDecoder(self.tok)
 
@@ -145,14 +147,16 @@ class LLMEngine(Engine):
         t0 = time.perf_counter()
         work = self.sched.admit()
         if work:
-            self._prefill(work, out)
+            with span("prefill"):
+                self._prefill(work, out)
         dec = self.sched.decode_set()
         # Sequences whose first token came from this step's prefill are not
         # decoded again in the same iteration.
         just = {s.seq_id for s, st, n in work}
         dec = [s for s in dec if s.seq_id not in just]
         if dec:
-            self._decode(dec, out)
+            with span("decode"):
+                self._decode(dec, out)
         self.last_step_ms = (time.perf_counter() - t0) * 1000
         kv = self.model.kv
         metrics.KV_BLOCKS_USED.labels(model=self.model_id).set(
@@ -380,6 +384,8 @@ class LLMEngine(Engine):
             out.append((tid, Chunk.token(tid, tok, text).with_n_tokens(1)))
         fin = Chunk.final_marker(tid, "").with_finish_reason(finish).with_prompt_tokens(
             len(s.prompt_ids))
+        task_done(tid, getattr(s, "submitted_at", 0.0) or 0.0, s.first_token_at or 0.0,
+                  time.monotonic(), len(s.output_ids), len(s.prompt_ids))
         out.append((tid, fin))
         s.finished = True
         self.sched.remove(s.seq_id)

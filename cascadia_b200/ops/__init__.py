@@ -14,6 +14,8 @@ from typing import Optional
 
 import torch
 
+from . import debug as _dbg
+
 _EXT = None
 _EXT_ERR: Optional[BaseException] = None
 _LOCK = threading.Lock()
@@ -165,6 +167,8 @@ def w4a16_plan(m: int, n: int, k: int, splits: int = 0):
 # ----------------------------------------------------------------- attention
 def attn_decode(q, k_cache, v_cache, block_tables, seq_lens, out, layer: int, num_splits: int,
                 blocks_per_split: int, part_o, part_ml, scale: float):
+    if _dbg.ENABLED and not torch.cuda.is_current_stream_capturing():
+        _dbg.check_paged(block_tables, seq_lens, k_cache.shape[1])
     ext().attn_decode(q, k_cache, v_cache, block_tables, seq_lens, out, layer, num_splits,
                       blocks_per_split, part_o, part_ml, scale, status_buffer(q.device))
     LAUNCHES.add(2 if num_splits > 1 else 1)
@@ -206,6 +210,8 @@ def prefill_tiles(q_lens, ctx_lens, device) -> torch.Tensor:
 
 # ----------------------------------------------------------------- small ops
 def embedding(ids, table, out, vocab_lo: int = 0):
+    if _dbg.ENABLED and not torch.cuda.is_current_stream_capturing():
+        _dbg.check_range("token ids", ids, 0, 1 << 31)
     ext().embedding(ids, table, out, vocab_lo)
     LAUNCHES.add(1)
     return out
@@ -227,6 +233,9 @@ def head_rmsnorm(qkv, q_w, k_w, hq, hkv, d, eps):
 
 def rope_kv_write(qkv, positions, cos_sin, slots, k_cache, v_cache, layer, hq, hkv, d, rot,
                   interleaved=False):
+    if _dbg.ENABLED and not torch.cuda.is_current_stream_capturing():
+        _dbg.check_range("kv slots", slots, 0, k_cache.shape[1] * 16, allow=(-1,))
+        _dbg.check_range("positions", positions, 0, cos_sin.shape[0])
     ext().rope_kv_write(qkv, positions, cos_sin, slots, k_cache, v_cache, layer, hq, hkv, d, rot,
                         interleaved)
     LAUNCHES.add(1)
@@ -282,6 +291,8 @@ def moe_topk_gate(x, wg, k: int, scoring: int = 0, norm_topk: bool = True,
 
 def moe_permute(ids, num_experts: int, x=None):
     """Counting sort of (token, slot) pairs by expert; optionally gathers x."""
+    if _dbg.ENABLED and not torch.cuda.is_current_stream_capturing():
+        _dbg.check_range("expert ids", ids, 0, num_experts)
     n = ids.numel()
     dev = ids.device
     offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)

@@ -72,3 +72,19 @@ def test_blob_gate_up_interleave():
     dec = _decode_blob(qw.blob(interleave_gate_up=True), 256, 128, 128, True)
     ref = interleave_rows(qw.dequant_bf16().float())
     assert torch.equal(dec, ref)
+
+
+def test_debug_index_checks():
+    import pytest
+    import torch
+
+    from cascadia_b200.ops import debug
+
+    debug.check_range("ok", torch.tensor([0, 3, -1]), 0, 4, allow=(-1,))
+    with pytest.raises(debug.IndexCheckError):
+        debug.check_range("bad", torch.tensor([0, 4]), 0, 4)
+    debug.check_paged(torch.tensor([[2, 5, 0]]), torch.tensor([20]), 8)
+    with pytest.raises(debug.IndexCheckError):
+        debug.check_paged(torch.tensor([[2, 9, 0]]), torch.tensor([20]), 8)
+    with pytest.raises(debug.IndexCheckError):
+        debug.check_paged(torch.tensor([[2, 5]]), torch.tensor([40]), 8)
