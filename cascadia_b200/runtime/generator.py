@@ -32,7 +32,8 @@ class DecodeGraph:
         self.dev = dev
         # Layout of the staging row: ids | positions | slots | seq_lens | table
         self.n_int = 4 * batch + batch * width
-        self.host = torch.zeros(self.n_int, dtype=torch.int32, pin_memory=True)
+        pin = torch.device(dev).type == "cuda"
+        self.host = torch.zeros(self.n_int, dtype=torch.int32, pin_memory=pin)
         self.dev_in = torch.zeros(self.n_int, dtype=torch.int32, device=dev)
         b = batch
         self.ids = self.dev_in[0:b]
@@ -40,7 +41,7 @@ class DecodeGraph:
         self.slots = self.dev_in[2 * b:3 * b]
         self.seq_lens = self.dev_in[3 * b:4 * b]
         self.table = self.dev_in[4 * b:].view(b, width)
-        self.out_host = torch.zeros(batch, dtype=torch.int32, pin_memory=True)
+        self.out_host = torch.zeros(batch, dtype=torch.int32, pin_memory=pin)
         self.hidden = torch.zeros(batch, model.cfg.hidden_size, dtype=torch.bfloat16, device=dev)
         if num_splits is None:
             num_splits, bps = ops.decode_split_plan(batch, model.hkv, width)
@@ -63,11 +64,16 @@ class DecodeGraph:
         self.use_graph = use_graph and dev.type == "cuda"
 
     def _step(self):
+        """Embedding (first stage), this stage's layers, LM head + argmax (last
+        stage).  A middle or last pipeline stage finds its input rows in
+        ``self.hidden`` (received before the replay)."""
         m = self.model
-        m.embed_tokens(self.ids, out=self.hidden)
+        if m.has_embed:
+            m.embed_tokens(self.ids, out=self.hidden)
         m.forward(self.batch_view, self.hidden)
-        self.logits = m.head(self.hidden)
-        self.next_ids = m.greedy(self.logits)
+        if m.has_head:
+            self.logits = m.head(self.hidden)
+            self.next_ids = m.greedy(self.logits)
         return self.next_ids
 
     def capture(self, warmup: int = 2):
