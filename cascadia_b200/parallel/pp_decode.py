@@ -91,7 +91,7 @@ class PipelinedDecoder:
             b = g.B
             g.dev_in[b:].copy_(g.host[b:], non_blocking=True)
             if not self.first:
-                dist.irecv(g.hidden, self._peer(self.stage - 1), group=self.group).wait()
+                dist.irecv(g.hidden_in, self._peer(self.stage - 1), group=self.group).wait()
             if g.use_graph and g.graph is None and capture_now:
                 g.capture()
             g.run()

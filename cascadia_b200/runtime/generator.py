@@ -43,6 +43,10 @@ class DecodeGraph:
         self.table = self.dev_in[4 * b:].view(b, width)
         self.out_host = torch.zeros(batch, dtype=torch.int32, pin_memory=pin)
         self.hidden = torch.zeros(batch, model.cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+        # Pipeline stages after the first receive their input rows here; the
+        # step copies them into `hidden` (the layers update it in place), so
+        # replaying or re-running a step is idempotent.
+        self.hidden_in = None if model.has_embed else torch.zeros_like(self.hidden)
         if num_splits is None:
             num_splits, bps = ops.decode_split_plan(batch, model.hkv, width)
         else:
@@ -66,10 +70,12 @@ class DecodeGraph:
     def _step(self):
         """Embedding (first stage), this stage's layers, LM head + argmax (last
         stage).  A middle or last pipeline stage finds its input rows in
-        ``self.hidden`` (received before the replay)."""
+        ``self.hidden_in`` (received before the replay)."""
         m = self.model
         if m.has_embed:
             m.embed_tokens(self.ids, out=self.hidden)
+        else:
+            self.hidden.copy_(self.hidden_in)
         m.forward(self.batch_view, self.hidden)
         if m.has_head:
             self.logits = m.head(self.hidden)
