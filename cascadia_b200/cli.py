@@ -200,6 +200,19 @@ def cmd_shard(args):
     from .shard.format import write_random_shards
 
     cfg = get_config(args.model)
+    if cfg.is_moe:
+        # Sparse-MoE directory (manifest + shells + F1 expert bins).
+        from .models import llama
+        from .models.mla import MLAModel
+        from .models.moe import MoEModel
+        from .shard.moe_format import write_moe_model
+
+        llama.KEEP_INT4 = True
+        cls = MLAModel if cfg.is_mla else MoEModel
+        m = cls(cfg, "cpu").init_random(seed=args.seed, gen_device="cpu")
+        write_moe_model(m, args.output_dir)
+        print(json.dumps({"output_dir": args.output_dir, "format": "sparse-moe int4_bin"}))
+        return
     split = [int(x) for x in args.layer_split.split(",")] if args.layer_split else None
     meta = write_random_shards(cfg, args.output_dir, args.num_stages, args.model,
                                seed=args.seed, layer_split=split, device=args.device,

@@ -443,7 +443,13 @@ class LLMBuilder(Builder):
         from ..models.config import get_config
 
         yield LoadProgress.msg(f"loading {self.model_name}")
-        if os.path.isdir(self.model_name):
+        if os.path.isdir(self.model_name) and os.path.exists(
+                os.path.join(self.model_name, "manifest.json")):
+            from ..shard.moe_format import load_moe_model
+
+            self.model = load_moe_model(self.model_name, self.device)
+            tok_dir = self.tokenizer_path
+        elif os.path.isdir(self.model_name):
             from ..shard.format import load_stage_model
 
             self.model = load_stage_model(self.model_name, shard, self.device, tp=self.tp)

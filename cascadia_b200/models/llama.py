@@ -32,12 +32,17 @@ from ..runtime.kv_cache import BLOCK_SIZE, KVCache
 from .config import ModelConfig, rope_table
 
 
+# When set (model writers), every QLinear keeps its Int4Weight in `.int4`.
+KEEP_INT4 = False
+
+
 class QLinear:
     """An INT4 weight ready for its device: kernel blob on CUDA, fp32 on CPU."""
 
     def __init__(self, w: Int4Weight, device, interleave_gate_up: bool = False):
         self.n, self.k, self.group_size = w.n, w.k, w.group_size
         self.interleaved = interleave_gate_up
+        self.int4 = w if KEEP_INT4 else None
         device = torch.device(device)
         if device.type == "cuda":
             self.blob = w.to(device).blob(interleave_gate_up)

@@ -60,6 +60,9 @@ class ExpertBank:
     fp32 weights (CPU oracle)."""
 
     def __init__(self, gate_up: List[Int4Weight], down: List[Int4Weight], device):
+        from . import llama
+
+        self.int4 = (list(gate_up), list(down)) if llama.KEEP_INT4 else None
         self.E = len(gate_up)
         self.inter = gate_up[0].n // 2
         self.hidden = gate_up[0].k
