@@ -423,7 +423,12 @@ class LLMBuilder(Builder):
         pass
 
     def model_class(self, cfg):
-        """Dense Llama-family model, or the sparse-MoE model for MoE configs."""
+        """Dense Llama-family model, or the sparse-MoE model for MoE configs
+        (hybrid Gated-DeltaNet MoE, MLA MoE, plain MoE)."""
+        if cfg.is_hybrid:
+            from ..models.qwen36 import HybridMoEModel
+
+            return HybridMoEModel
         if cfg.is_mla:
             from ..models.mla import MLAModel
 
@@ -469,14 +474,23 @@ class LLMBuilder(Builder):
         cfg = self.model.cfg
         self.tokenizer = load_tokenizer(tok_dir, cfg.vocab_size, cfg.eos_token_ids[0])
         blocks = self.kv_blocks
+        hybrid = cfg.is_hybrid
+        if hybrid and (self.spec or self.prefix_cache_blocks):
+            raise InvalidConfig("the linear-attention state of this model cannot be shared or "
+                                "rewound: no prefix cache, no speculative decoding")
         if blocks <= 0:
             per = self.model.kv_bytes_per_block()
             if torch.device(self.device).type == "cuda":
                 free, _ = torch.cuda.mem_get_info(torch.device(self.device))
+                if hybrid:  # recurrent state of every running sequence first
+                    free -= self.max_running * self.model.state_bytes_per_seq()
                 blocks = max(64, int(free * self.kv_fraction) // per)
             else:
                 blocks = max(64, (self.max_running * self.max_model_len) // BLOCK_SIZE // 4)
-        self.model.allocate_kv(blocks)
+        if hybrid:
+            self.model.allocate_kv(blocks, max_seqs=self.max_running)
+        else:
+            self.model.allocate_kv(blocks)
         yield LoadProgress.msg(f"kv cache: {blocks} blocks")
         if self.spec == "draft":
             if not self.draft_name:

@@ -48,6 +48,25 @@ class ModelConfig:
     qk_rope_head_dim: int = 0
     qk_nope_head_dim: int = 0
     v_head_dim: int = 0
+    # --- hybrid linear attention (Qwen3.5 / Qwen3.6: Gated DeltaNet layers,
+    # every full_attention_interval-th layer full attention) ---
+    full_attention_interval: int = 0   # 0: no linear-attention layers
+    linear_num_key_heads: int = 0
+    linear_num_value_heads: int = 0
+    linear_key_head_dim: int = 128
+    linear_value_head_dim: int = 128
+    linear_conv_kernel_dim: int = 4
+    attn_output_gate: bool = False     # full attention output * sigmoid(gate)
+    shared_expert_gate: bool = False   # shared expert output * sigmoid(w . x)
+    shared_expert_intermediate_size: int = 0
+
+    @property
+    def is_hybrid(self) -> bool:
+        return self.full_attention_interval > 0
+
+    def is_linear_layer(self, li: int) -> bool:
+        """Layer li is a Gated DeltaNet layer (the rest are full attention)."""
+        return self.is_hybrid and (li + 1) % self.full_attention_interval != 0
 
     @property
     def is_moe(self) -> bool:
@@ -115,6 +134,26 @@ class ModelConfig:
             c.v_head_dim = d["v_head_dim"]
         if mt.startswith("qwen3"):
             c.qk_norm = True
+        if mt.startswith("qwen3_5") or mt.startswith("qwen3_next"):
+            rp = d.get("rope_parameters") or {}
+            c.arch = "qwen3_5_moe"
+            c.rope_theta = float(rp.get("rope_theta", d.get("rope_theta", 10000000.0)))
+            c.partial_rotary_factor = float(rp.get("partial_rotary_factor",
+                                                   d.get("partial_rotary_factor", 0.25)))
+            c.rope_scaling = None
+            types = d.get("layer_types")
+            c.full_attention_interval = (types.index("full_attention") + 1) if types else int(
+                d.get("full_attention_interval", 4))
+            c.linear_num_key_heads = d["linear_num_key_heads"]
+            c.linear_num_value_heads = d["linear_num_value_heads"]
+            c.linear_key_head_dim = d.get("linear_key_head_dim", 128)
+            c.linear_value_head_dim = d.get("linear_value_head_dim", 128)
+            c.linear_conv_kernel_dim = d.get("linear_conv_kernel_dim", 4)
+            c.attn_output_gate = True
+            if d.get("shared_expert_intermediate_size"):
+                c.shared_expert_gate = True
+                c.shared_expert_intermediate_size = d["shared_expert_intermediate_size"]
+                c.num_shared_experts = 1
         return c
 
 
@@ -149,6 +188,20 @@ PRESETS = {
                                          "beta_slow": 1.0, "mscale": 1.0, "mscale_all_dim": 1.0,
                                          "original_max_position_embeddings": 4096},
                            eos_token_ids=(163586,)),
+    # Qwen3.6-35B-A3B (HF qwen3_5_moe): 30 Gated DeltaNet + 10 gated
+    # full-attention layers (head_dim 256, rotary on 64 dims), 256 experts
+    # top-8 + a sigmoid-gated shared expert.
+    "qwen3.6-35b-a3b": ModelConfig(arch="qwen3_5_moe", vocab_size=248320, hidden_size=2048,
+                                   num_layers=40, num_heads=16, num_kv_heads=2, head_dim=256,
+                                   intermediate_size=512, rope_theta=10000000.0,
+                                   partial_rotary_factor=0.25, rms_eps=1e-6, num_experts=256,
+                                   num_experts_per_tok=8, moe_intermediate_size=512,
+                                   num_shared_experts=1, router="softmax", norm_topk_prob=True,
+                                   qk_norm=True, full_attention_interval=4,
+                                   linear_num_key_heads=16, linear_num_value_heads=32,
+                                   attn_output_gate=True, shared_expert_gate=True,
+                                   shared_expert_intermediate_size=512,
+                                   max_position=262144, eos_token_ids=(248046, 248044)),
     # Small shapes for tests (same code paths).
     "tiny-llama": ModelConfig(vocab_size=512, hidden_size=256, num_layers=2, num_heads=4,
                               num_kv_heads=2, head_dim=64, intermediate_size=512,
@@ -174,6 +227,17 @@ PRESETS = {
                                           "mscale_all_dim": 1.0,
                                           "original_max_position_embeddings": 4096},
                             eos_token_ids=(1,)),
+    # Qwen3.6 layer structure at small width (linear head dims are the real
+    # 128; full attention head_dim 256 as in the real model).
+    "tiny-qwen36": ModelConfig(arch="qwen3_5_moe", vocab_size=512, hidden_size=256, num_layers=4,
+                               num_heads=4, num_kv_heads=2, head_dim=256, intermediate_size=128,
+                               rope_theta=10000000.0, partial_rotary_factor=0.25, rms_eps=1e-6,
+                               num_experts=8, num_experts_per_tok=2, moe_intermediate_size=128,
+                               num_shared_experts=1, router="softmax", norm_topk_prob=True,
+                               qk_norm=True, full_attention_interval=4, linear_num_key_heads=2,
+                               linear_num_value_heads=4, attn_output_gate=True,
+                               shared_expert_gate=True, shared_expert_intermediate_size=128,
+                               eos_token_ids=(1,)),
 }
 
 

@@ -207,14 +207,18 @@ class MoEModel(LlamaModel):
             x = part.float().view(T, nh, d)
             part.copy_(ref.rmsnorm(x, w, self.cfg.rms_eps).to(torch.bfloat16).view(T, nh * d))
 
+    def _shared_expert(self, lw: MoELayer, h: torch.Tensor) -> Optional[torch.Tensor]:
+        """Output of the layer's shared expert(s), or None."""
+        if lw.shared is None:
+            return None
+        return lw.shared[1](lw.shared[0](h, ops.EPI_SILU))
+
     def _moe(self, lw: MoELayer, h: torch.Tensor, hidden: torch.Tensor):
         cfg = self.cfg
         k = cfg.num_experts_per_tok
         scoring = 0 if cfg.router == "softmax" else 1
         bank = lw.experts
-        shared_out = None
-        if lw.shared is not None:
-            shared_out = lw.shared[1](lw.shared[0](h, ops.EPI_SILU))
+        shared_out = self._shared_expert(lw, h)
         if self.ep is not None:
             if self.device.type == "cuda":
                 ids, w = ops.moe_topk_gate(h, lw.router, k, scoring, cfg.norm_topk_prob,

@@ -259,6 +259,34 @@ def spec_verify(target, draft, out):
     return out
 
 
+# ----------------------------------------------------------------- Gated DeltaNet
+def gdn_conv(x, channels: int, w, state, seq_start, block_tables, block_slot):
+    """Causal depthwise conv (width 4) + SiLU of x[:, :channels] in place,
+    per sequence (token ranges seq_start[b]..seq_start[b+1]), with the conv
+    state of each sequence's slot (block_slot[block_tables[b, 0]]) read and
+    updated."""
+    ext().gdn_conv(x, channels, w, state, seq_start, block_tables, block_slot)
+    LAUNCHES.add(1)
+    return x
+
+
+def gdn_recurrent(qkv, z, ab, a_log, dt_bias, norm_w, state, seq_start, block_tables,
+                  block_slot, out, hk: int, hv: int, eps: float):
+    """Gated delta-rule recurrence of every (sequence, value head) over its
+    tokens, fp32 state updated in place, gated RMSNorm of the output fused."""
+    ext().gdn_recurrent(qkv, z, ab, a_log, dt_bias, norm_w, state, seq_start, block_tables,
+                        block_slot, out, hk, hv, eps)
+    LAUNCHES.add(1)
+    return out
+
+
+def sigmoid_gate(x, gate):
+    """x *= sigmoid(gate[:, :x.shape[1]]) in place."""
+    ext().sigmoid_gate(x, gate)
+    LAUNCHES.add(1)
+    return x
+
+
 # ----------------------------------------------------------------- MoE
 _GATE_CNT: dict = {}
 

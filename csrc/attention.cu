@@ -52,6 +52,9 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
   constexpr int KV_BYTES = 16 * D * 2;  // one block of K (or V)
   constexpr int STAGE = 2 * KV_BYTES;
   constexpr int NKS = D / 16;
+  // head_dim 256: Q fragments come from shared memory per k-step (the
+  // output accumulators alone take 128 registers).
+  constexpr bool QS = D > 128;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -63,6 +66,9 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
   uint8_t* wbuf = smem + warp * 2 * STAGE;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 4 * 2 * STAGE);
   uint64_t* full = bars + warp * 2;
+  uint8_t* qsm = smem + 4 * 2 * STAGE + 128;  // [16][D] bf16, chunk-swizzled (QS)
+  grid_dep_launch();
+  grid_dep_wait();  // q, the cache rows and the lengths come from earlier kernels
 
   const int seq_len = a.seq_lens[b];
   const int nblocks = (seq_len + 15) >> 4;
@@ -100,16 +106,27 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
   const int g = lane >> 2;
   const int t4 = lane & 3;
   // Q fragments (rows = query heads of the group, padded to 16).
-  uint32_t qa[NKS][4];
+  uint32_t qa[QS ? 1 : NKS][4];
   {
     const __nv_bfloat16* qb = a.q + (size_t)b * a.q_stride + (size_t)h * a.G * D;
+    if constexpr (QS) {
+      for (int idx = threadIdx.x; idx < 16 * (D / 8); idx += 128) {
+        const int r = idx / (D / 8), c = idx % (D / 8);
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (r < a.G) v = *reinterpret_cast<const uint4*>(qb + r * D + c * 8);
+        *reinterpret_cast<uint4*>(qsm + r * D * 2 + (((c & ~7) | ((c & 7) ^ (r & 7))) << 4)) = v;
+      }
+      __syncthreads();
+    } else {
 #pragma unroll
-    for (int ks = 0; ks < NKS; ++ks) {
-      const int c0 = ks * 16 + 2 * t4;
-      qa[ks][0] = g < a.G ? *reinterpret_cast<const uint32_t*>(qb + g * D + c0) : 0u;
-      qa[ks][1] = g + 8 < a.G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * D + c0) : 0u;
-      qa[ks][2] = g < a.G ? *reinterpret_cast<const uint32_t*>(qb + g * D + c0 + 8) : 0u;
-      qa[ks][3] = g + 8 < a.G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * D + c0 + 8) : 0u;
+      for (int ks = 0; ks < NKS; ++ks) {
+        const int c0 = ks * 16 + 2 * t4;
+        qa[ks][0] = g < a.G ? *reinterpret_cast<const uint32_t*>(qb + g * D + c0) : 0u;
+        qa[ks][1] = g + 8 < a.G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * D + c0) : 0u;
+        qa[ks][2] = g < a.G ? *reinterpret_cast<const uint32_t*>(qb + g * D + c0 + 8) : 0u;
+        qa[ks][3] =
+            g + 8 < a.G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * D + c0 + 8) : 0u;
+      }
     }
   }
 
@@ -137,8 +154,18 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
       const int chunk = 2 * ks + ((lane >> 3) & 1);
       uint32_t b00, b01, b10, b11;
       ldsm_x4(kaddr + sw128_off(row, chunk, 16), b00, b01, b10, b11);
-      mma_16816(s[0], qa[ks], b00, b01);
-      mma_16816(s[1], qa[ks], b10, b11);
+      if constexpr (QS) {
+        uint32_t qf[4];
+        const int qr = (lane & 7) + (((lane >> 3) & 1) << 3);
+        const int qc = 2 * ks + (lane >> 4);
+        ldsm_x4(smem_u32(qsm) + qr * D * 2 + (((qc & ~7) | ((qc & 7) ^ (qr & 7))) << 4), qf[0],
+                qf[1], qf[2], qf[3]);
+        mma_16816(s[0], qf, b00, b01);
+        mma_16816(s[1], qf, b10, b11);
+      } else {
+        mma_16816(s[0], qa[ks], b00, b01);
+        mma_16816(s[1], qa[ks], b10, b11);
+      }
     }
     const int j = blk0 + warp + 4 * i;
     const int pos0 = j * 16;
@@ -260,6 +287,8 @@ __global__ void attn_decode_combine_kernel(const float* __restrict__ part_o,
                                            const float* __restrict__ part_ml,
                                            __nv_bfloat16* __restrict__ out, int out_stride, int Hkv,
                                            int G, int splits) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int b = blockIdx.x;
   const int hq = blockIdx.y;
   const int h = hq / G;
@@ -305,16 +334,20 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __grid_constant
   constexpr int TILE_BYTES = 4 * BLK_BYTES;  // 64 tokens
   constexpr int STAGE = 2 * TILE_BYTES;      // K and V
   constexpr int NKS = D / 16;
+  constexpr bool QS = D > 128;               // Q fragments from shared memory
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * STAGE);
+  uint8_t* qsm = smem + 2 * STAGE + 128;     // [64][D] bf16, chunk-swizzled (QS)
   __shared__ int s_abort;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int hq = blockIdx.y;
   const int h = hq / a.G;
+  grid_dep_launch();
+  grid_dep_wait();
   const int4 tinfo = a.tiles[blockIdx.x];
   const int b = tinfo.x, qrow0 = tinfo.y, pos0 = tinfo.z, nq = tinfo.w;
   const int kv_len = pos0 + nq;  // causal: the last query sees everything before it
@@ -353,8 +386,20 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __grid_constant
   const int t4 = lane & 3;
   const int r_lo = warp * 16 + g;  // query rows of this thread inside the tile
   const int r_hi = r_lo + 8;
-  uint32_t qa[NKS][4];
-  {
+  uint32_t qa[QS ? 1 : NKS][4];
+  if constexpr (QS) {
+    // This warp's 16 query rows into its slab of the Q tile.
+    uint8_t* slab = qsm + warp * 16 * D * 2;
+    for (int idx = lane; idx < 16 * (D / 8); idx += 32) {
+      const int r = idx / (D / 8), c = idx % (D / 8);
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (warp * 16 + r < nq)
+        v = *reinterpret_cast<const uint4*>(a.q + (size_t)(qrow0 + warp * 16 + r) * a.q_stride +
+                                            (size_t)hq * D + c * 8);
+      *reinterpret_cast<uint4*>(slab + r * D * 2 + (((c & ~7) | ((c & 7) ^ (r & 7))) << 4)) = v;
+    }
+    __syncwarp();
+  } else {
     const __nv_bfloat16* q_lo = a.q + (size_t)(qrow0 + r_lo) * a.q_stride + (size_t)hq * D;
     const __nv_bfloat16* q_hi = a.q + (size_t)(qrow0 + r_hi) * a.q_stride + (size_t)hq * D;
 #pragma unroll
@@ -387,14 +432,27 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __grid_constant
       for (int nt = 0; nt < 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
 #pragma unroll
       for (int ks = 0; ks < NKS; ++ks) {
+        uint32_t qf[4];
+        if constexpr (QS) {
+          const int qr = (lane & 7) + (((lane >> 3) & 1) << 3);
+          const int qc = 2 * ks + (lane >> 4);
+          ldsm_x4(smem_u32(qsm) + (warp * 16 + qr) * D * 2 +
+                      (((qc & ~7) | ((qc & 7) ^ (qr & 7))) << 4),
+                  qf[0], qf[1], qf[2], qf[3]);
+        } else {
+          qf[0] = qa[ks][0];
+          qf[1] = qa[ks][1];
+          qf[2] = qa[ks][2];
+          qf[3] = qa[ks][3];
+        }
 #pragma unroll
         for (int np = 0; np < 4; ++np) {  // pairs of 8-token n-tiles = one 16-token block
           const int row = ((lane >> 4) << 3) + (lane & 7);  // token within block np
           const int chunk = 2 * ks + ((lane >> 3) & 1);
           uint32_t b00, b01, b10, b11;
           ldsm_x4(kaddr + np * BLK_BYTES + sw128_off(row, chunk, 16), b00, b01, b10, b11);
-          mma_16816(s[2 * np], qa[ks], b00, b01);
-          mma_16816(s[2 * np + 1], qa[ks], b10, b11);
+          mma_16816(s[2 * np], qf, b00, b01);
+          mma_16816(s[2 * np + 1], qf, b10, b11);
         }
       }
       float p[8][4];
@@ -543,11 +601,24 @@ void attn_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       cfg = true;
     }
-    attn_decode_kernel<128><<<grid, 128, smem, stream>>>(tk, tv, a);
-    CB_CUDA_CHECK(cudaGetLastError());
+    launch_kernel(attn_decode_kernel<128>, grid, dim3(128), smem, stream, tk, tv, a);
     if (num_splits > 1) {
-      attn_decode_combine_kernel<128><<<dim3(B, Hq), 128, 0, stream>>>(
-          a.part_o, a.part_ml, a.out, a.out_stride, Hkv, a.G, (int)num_splits);
+      launch_kernel(attn_decode_combine_kernel<128>, dim3(B, Hq), dim3(128), 0, stream, a.part_o,
+                    a.part_ml, a.out, a.out_stride, Hkv, a.G, (int)num_splits);
+    }
+  } else if (D == 256) {
+    // Stages + barriers + the [16][256] Q tile + alignment slack.
+    constexpr int smem = 4 * 2 * 2 * 16 * 256 * 2 + 128 + 16 * 256 * 2 + 1024;
+    static bool cfg = false;
+    if (!cfg) {
+      CB_CUDA_CHECK(cudaFuncSetAttribute(attn_decode_kernel<256>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      cfg = true;
+    }
+    launch_kernel(attn_decode_kernel<256>, grid, dim3(128), smem, stream, tk, tv, a);
+    if (num_splits > 1) {
+      launch_kernel(attn_decode_combine_kernel<256>, dim3(B, Hq), dim3(256), 0, stream, a.part_o,
+                    a.part_ml, a.out, a.out_stride, Hkv, a.G, (int)num_splits);
     }
   } else if (D == 64) {
     constexpr int smem = 4 * 2 * 2 * 16 * 64 * 2 + 1024 + 128;
@@ -558,14 +629,13 @@ void attn_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       cfg = true;
     }
-    attn_decode_kernel<64><<<grid, 128, smem, stream>>>(tk, tv, a);
-    CB_CUDA_CHECK(cudaGetLastError());
+    launch_kernel(attn_decode_kernel<64>, grid, dim3(128), smem, stream, tk, tv, a);
     if (num_splits > 1) {
-      attn_decode_combine_kernel<64><<<dim3(B, Hq), 64, 0, stream>>>(
-          a.part_o, a.part_ml, a.out, a.out_stride, Hkv, a.G, (int)num_splits);
+      launch_kernel(attn_decode_combine_kernel<64>, dim3(B, Hq), dim3(64), 0, stream, a.part_o,
+                    a.part_ml, a.out, a.out_stride, Hkv, a.G, (int)num_splits);
     }
   } else {
-    TORCH_CHECK(false, "head_dim must be 64 or 128");
+    TORCH_CHECK(false, "head_dim must be 64, 128 or 256");
   }
   CB_CUDA_CHECK(cudaGetLastError());
 }
@@ -609,7 +679,17 @@ void attn_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       cfg = true;
     }
-    attn_prefill_kernel<128><<<grid, 128, smem, stream>>>(tk, tv, a);
+    launch_kernel(attn_prefill_kernel<128>, grid, dim3(128), smem, stream, tk, tv, a);
+  } else if (D == 256) {
+    // Two K/V stages + barriers + the [64][256] Q tile + alignment slack.
+    constexpr int smem = 2 * 2 * 4 * 16 * 256 * 2 + 128 + 64 * 256 * 2 + 1024;
+    static bool cfg = false;
+    if (!cfg) {
+      CB_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<256>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      cfg = true;
+    }
+    launch_kernel(attn_prefill_kernel<256>, grid, dim3(128), smem, stream, tk, tv, a);
   } else if (D == 64) {
     constexpr int smem = 2 * 2 * 4 * 16 * 64 * 2 + 1024 + 64;
     static bool cfg = false;
@@ -618,9 +698,9 @@ void attn_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       cfg = true;
     }
-    attn_prefill_kernel<64><<<grid, 128, smem, stream>>>(tk, tv, a);
+    launch_kernel(attn_prefill_kernel<64>, grid, dim3(128), smem, stream, tk, tv, a);
   } else {
-    TORCH_CHECK(false, "head_dim must be 64 or 128");
+    TORCH_CHECK(false, "head_dim must be 64, 128 or 256");
   }
   CB_CUDA_CHECK(cudaGetLastError());
 }

@@ -10,6 +10,16 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
                 torch::Tensor ws, torch::Tensor counters, torch::Tensor status,
                 int64_t forced_splits);
 int64_t w4a16_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t forced_splits);
+void set_pdl(bool on);
+// gdn.cu
+void gdn_conv(torch::Tensor x, int64_t C, torch::Tensor w, torch::Tensor state,
+              torch::Tensor seq_start, torch::Tensor block_tables, torch::Tensor block_slot);
+void gdn_recurrent(torch::Tensor qkv, torch::Tensor z, torch::Tensor ab, torch::Tensor a_log,
+                   torch::Tensor dt_bias, torch::Tensor norm_w, torch::Tensor state,
+                   torch::Tensor seq_start, torch::Tensor block_tables, torch::Tensor block_slot,
+                   torch::Tensor out, int64_t Hk, int64_t Hv, double eps);
+void sigmoid_gate(torch::Tensor x, torch::Tensor gate);
+bool pdl_enabled();
 int64_t w4a16_counter_count(int64_t M, int64_t N);
 void w4a16_set_trace(c10::optional<torch::Tensor> buf);
 std::vector<int64_t> w4a16_plan(int64_t M, int64_t N, int64_t K, int64_t forced_splits);
@@ -103,6 +113,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("w4a16_counter_count", &cb::w4a16_counter_count);
   m.def("w4a16_plan", &cb::w4a16_plan);
   m.def("w4a16_set_trace", &cb::w4a16_set_trace);
+  m.def("set_pdl", &cb::set_pdl);
+  m.def("gdn_conv", &cb::gdn_conv);
+  m.def("gdn_recurrent", &cb::gdn_recurrent);
+  m.def("sigmoid_gate", &cb::sigmoid_gate);
+  m.def("pdl_enabled", &cb::pdl_enabled);
   m.def("attn_decode", &cb::attn_decode);
   m.def("attn_prefill", &cb::attn_prefill);
   m.def("embedding", &cb::embedding);

@@ -23,6 +23,8 @@ using bf16 = __nv_bfloat16;
 __global__ void embedding_kernel(const int* __restrict__ ids, const bf16* __restrict__ table,
                                  bf16* __restrict__ out, int H, int ldo, int vocab_lo,
                                  int vocab_hi) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int t = blockIdx.x;
   const int id = ids[t];
   const bool mine = id >= vocab_lo && id < vocab_hi;  // vocab-parallel shards
@@ -37,11 +39,10 @@ void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_
   TORCH_CHECK(H % 8 == 0, "hidden must be a multiple of 8");
   if (T == 0) return;
   const c10::cuda::CUDAGuard guard(ids.device());
-  embedding_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
-      ids.data_ptr<int>(), reinterpret_cast<const bf16*>(table.data_ptr()),
-      reinterpret_cast<bf16*>(out.data_ptr()), H, (int)out.stride(0), (int)vocab_lo,
-      (int)(vocab_lo + table.size(0)));
-  CB_CUDA_CHECK(cudaGetLastError());
+  launch_kernel(embedding_kernel, dim3(T), dim3(128), 0, at::cuda::getCurrentCUDAStream(),
+                ids.data_ptr<int>(), reinterpret_cast<const bf16*>(table.data_ptr()),
+                reinterpret_cast<bf16*>(out.data_ptr()), H, (int)out.stride(0), (int)vocab_lo,
+                (int)(vocab_lo + table.size(0)));
 }
 
 // ------------------------------------------------------------------ RMSNorm
@@ -64,6 +65,8 @@ __global__ void rmsnorm_kernel(const bf16* __restrict__ x, int ldx, bf16* __rest
                                int ldr, const bf16* __restrict__ w, bf16* __restrict__ out, int ldo,
                                int H, float eps) {
   __shared__ float red[32];
+  grid_dep_launch();
+  grid_dep_wait();
   const int row = blockIdx.x;
   const int nvec = H / 8;
   float v[MAXV][8];
@@ -122,17 +125,10 @@ void rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tens
   bf16* res = residual.has_value() ? reinterpret_cast<bf16*>(residual->data_ptr()) : nullptr;
   const int ldr = residual.has_value() ? (int)residual->stride(0) : 0;
   auto stream = at::cuda::getCurrentCUDAStream();
-  if (H / 8 <= threads) {
-    rmsnorm_kernel<1><<<M, threads, 0, stream>>>(
-        reinterpret_cast<const bf16*>(x.data_ptr()), (int)x.stride(0), res, ldr,
-        reinterpret_cast<const bf16*>(w.data_ptr()), reinterpret_cast<bf16*>(out.data_ptr()),
-        (int)out.stride(0), H, (float)eps);
-  } else {
-    rmsnorm_kernel<2><<<M, threads, 0, stream>>>(
-        reinterpret_cast<const bf16*>(x.data_ptr()), (int)x.stride(0), res, ldr,
-        reinterpret_cast<const bf16*>(w.data_ptr()), reinterpret_cast<bf16*>(out.data_ptr()),
-        (int)out.stride(0), H, (float)eps);
-  }
+  launch_kernel(H / 8 <= threads ? rmsnorm_kernel<1> : rmsnorm_kernel<2>, dim3(M),
+                dim3(threads), 0, stream, reinterpret_cast<const bf16*>(x.data_ptr()),
+                (int)x.stride(0), res, ldr, reinterpret_cast<const bf16*>(w.data_ptr()),
+                reinterpret_cast<bf16*>(out.data_ptr()), (int)out.stride(0), H, (float)eps);
   CB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -159,6 +155,8 @@ __global__ void rope_kv_kernel(bf16* __restrict__ qkv, int ldq, const int* __res
                                const float* __restrict__ cos_sin, const int* __restrict__ slots,
                                bf16* __restrict__ k_cache, bf16* __restrict__ v_cache, int layer,
                                int NB, int Hq, int Hkv, int D, int rot, int interleaved) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int t = blockIdx.x;
   const int pos = positions[t];
   const int slot = slots[t];
@@ -247,12 +245,12 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos
   TORCH_CHECK(rot % 16 == 0 && D % 8 == 0, "rotary dim must be a multiple of 16");
   TORCH_CHECK((qkv.stride(0) * 2) % 16 == 0, "qkv rows must be 16-byte aligned");
   const c10::cuda::CUDAGuard guard(qkv.device());
-  rope_kv_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<bf16*>(qkv.data_ptr()), (int)qkv.stride(0), positions.data_ptr<int>(),
-      cos_sin.data_ptr<float>(), slots.data_ptr<int>(), reinterpret_cast<bf16*>(k_cache.data_ptr()),
-      reinterpret_cast<bf16*>(v_cache.data_ptr()), (int)layer, (int)k_cache.size(1), (int)Hq,
-      (int)Hkv, (int)D, (int)rot, interleaved ? 1 : 0);
-  CB_CUDA_CHECK(cudaGetLastError());
+  launch_kernel(rope_kv_kernel, dim3(T), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+                reinterpret_cast<bf16*>(qkv.data_ptr()), (int)qkv.stride(0),
+                positions.data_ptr<int>(), cos_sin.data_ptr<float>(), slots.data_ptr<int>(),
+                reinterpret_cast<bf16*>(k_cache.data_ptr()),
+                reinterpret_cast<bf16*>(v_cache.data_ptr()), (int)layer, (int)k_cache.size(1),
+                (int)Hq, (int)Hkv, (int)D, (int)rot, interleaved ? 1 : 0);
 }
 
 // ------------------------------------------------------------------ q/k norm
@@ -261,6 +259,8 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos
 __global__ void head_rmsnorm_kernel(bf16* __restrict__ qkv, int ldq, const bf16* __restrict__ qw,
                                     const bf16* __restrict__ kw, int Hq, int Hkv, int D,
                                     float eps) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int t = blockIdx.x;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nw = blockDim.x / 32;
@@ -295,11 +295,11 @@ void head_rmsnorm(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, int64
   TORCH_CHECK(qkv.stride(1) == 1 && (qkv.stride(0) * 2) % 16 == 0, "qkv rows must be aligned");
   TORCH_CHECK(D % 8 == 0 && D <= 256, "head_rmsnorm: D must be a multiple of 8, <= 256");
   const c10::cuda::CUDAGuard guard(qkv.device());
-  head_rmsnorm_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<bf16*>(qkv.data_ptr()), (int)qkv.stride(0),
-      reinterpret_cast<const bf16*>(q_w.data_ptr()), reinterpret_cast<const bf16*>(k_w.data_ptr()),
-      (int)Hq, (int)Hkv, (int)D, (float)eps);
-  CB_CUDA_CHECK(cudaGetLastError());
+  launch_kernel(head_rmsnorm_kernel, dim3(T), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+                reinterpret_cast<bf16*>(qkv.data_ptr()), (int)qkv.stride(0),
+                reinterpret_cast<const bf16*>(q_w.data_ptr()),
+                reinterpret_cast<const bf16*>(k_w.data_ptr()), (int)Hq, (int)Hkv, (int)D,
+                (float)eps);
 }
 
 // ------------------------------------------------------------------ argmax
@@ -309,6 +309,8 @@ void head_rmsnorm(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, int64
 template <typename T>
 __global__ void argmax_kernel(const T* __restrict__ logits, int ld, int V, int* __restrict__ out_idx,
                               float* __restrict__ out_val, int idx_offset) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int row = blockIdx.x;
   const T* x = logits + (size_t)row * ld;
   float best = -INFINITY;
@@ -389,14 +391,14 @@ void argmax(torch::Tensor logits, torch::Tensor out_idx, c10::optional<torch::Te
   float* ov = out_val.has_value() ? out_val->data_ptr<float>() : nullptr;
   auto stream = at::cuda::getCurrentCUDAStream();
   if (logits.scalar_type() == at::kFloat) {
-    argmax_kernel<float><<<M, 1024, 0, stream>>>(logits.data_ptr<float>(), (int)logits.stride(0), V,
-                                                 out_idx.data_ptr<int>(), ov, (int)idx_offset);
+    launch_kernel(argmax_kernel<float>, dim3(M), dim3(1024), 0, stream,
+                  logits.data_ptr<float>(), (int)logits.stride(0), V, out_idx.data_ptr<int>(), ov,
+                  (int)idx_offset);
   } else {
-    argmax_kernel<bf16><<<M, 1024, 0, stream>>>(reinterpret_cast<const bf16*>(logits.data_ptr()),
-                                                (int)logits.stride(0), V, out_idx.data_ptr<int>(),
-                                                ov, (int)idx_offset);
+    launch_kernel(argmax_kernel<bf16>, dim3(M), dim3(1024), 0, stream,
+                  reinterpret_cast<const bf16*>(logits.data_ptr()), (int)logits.stride(0), V,
+                  out_idx.data_ptr<int>(), ov, (int)idx_offset);
   }
-  CB_CUDA_CHECK(cudaGetLastError());
 }
 
 // ------------------------------------------------------------------ sampling

@@ -129,6 +129,9 @@ struct GemmArgs {
   // (expert parallelism: result rows go straight to the source rank's
   // return region in peer memory).
   const long long* out_rows;
+  // Launched with programmatic stream serialisation: the producer issues the
+  // first stages' weight copies (constant data) before griddepcontrol.wait.
+  int pdl;
 };
 
 __device__ __forceinline__ __nv_bfloat16* gemm_out_row(const GemmArgs& a, int gm) {
@@ -184,6 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   int m0 = tt * MT, m_lim = args.M;
   const uint8_t* wbase = args.wblob;
   if (args.group_offsets != nullptr) {
+    grid_dep_wait();  // the offsets come from the previous kernel
     const int e = blockIdx.z / args.group_tiles;
     const int lt = blockIdx.z % args.group_tiles;
     m0 = args.group_offsets[e] + lt * MT;
@@ -221,15 +225,38 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t tmem_acc = tmem_base + kAccCol;
   if (tid == 0) gemm_stamp(args, 1);
+  // TMEM is held: a dependent kernel's CTAs may now become resident (they
+  // cannot take this CTA's columns before it frees them, and it never waits
+  // for them).
+  if (args.pdl) grid_dep_launch();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       prefetch_tmap(&tmap_x);
       const uint8_t* wsrc = wbase + ((size_t)rt * KB + kb0) * BLOB;
-      int issued = 0;
       const int nst = (nkb + 1) / 2;
-      for (int sti = 0; sti < nst; ++sti) {
+      auto load_x = [&](int sti, uint8_t* st, uint64_t* bar) {
+        const int nb = min(2, nkb - 2 * sti);
+        for (int b = 0; b < nb; ++b) {
+          const int k = (kb0 + 2 * sti + b) * 128;
+          tma_load_2d(st + b * Plan::kXBytes, &tmap_x, k, m0, bar);
+          tma_load_2d(st + b * Plan::kXBytes + MT * 128, &tmap_x, k + 64, m0, bar);
+        }
+      };
+      // Weights of the first stages go out before the wait for the previous
+      // kernel; X (its output) only after it.
+      const int pre = args.pdl ? min(nst, SL) : 0;
+      for (int sti = 0; sti < pre; ++sti) {
+        const int nb = min(2, nkb - 2 * sti);
+        mbar_arrive_expect_tx(&full_l[sti], nb * (Plan::kXBytes + BLOB));
+        bulk_g2s(l_smem + sti * Plan::kStage + Plan::kBlobOff, wsrc + (size_t)(2 * sti) * BLOB,
+                 nb * BLOB, &full_l[sti]);
+      }
+      grid_dep_wait();
+      for (int sti = 0; sti < pre; ++sti) load_x(sti, l_smem + sti * Plan::kStage, &full_l[sti]);
+      int issued = pre;
+      for (int sti = pre; sti < nst; ++sti) {
         const int s = sti % SL;
         const uint32_t ph = (sti / SL) & 1;
         if (!mbar_wait(&empty_l[s], ph ^ 1, args.status, kStatusGemmLoadTimeout, abort_flag)) break;
@@ -237,11 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nb = min(2, nkb - 2 * sti);
         mbar_arrive_expect_tx(&full_l[s], nb * (Plan::kXBytes + BLOB));
         bulk_g2s(st + Plan::kBlobOff, wsrc + (size_t)(2 * sti) * BLOB, nb * BLOB, &full_l[s]);
-        for (int b = 0; b < nb; ++b) {
-          const int k = (kb0 + 2 * sti + b) * 128;
-          tma_load_2d(st + b * Plan::kXBytes, &tmap_x, k, m0, &full_l[s]);
-          tma_load_2d(st + b * Plan::kXBytes + MT * 128, &tmap_x, k + 64, m0, &full_l[s]);
-        }
+        load_x(sti, st, &full_l[s]);
         ++issued;
       }
       gemm_stamp(args, 3);
@@ -351,6 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // ------------------------------------------------------------ epilogue
+    grid_dep_wait();  // global reads and writes from here on
     const bool have_acc =
         ok && nkb > 0 && mbar_wait(acc_full, 0, args.status, kStatusGemmEpiTimeout, abort_flag);
     if (!have_acc) *acc_ok = 0;  // made uniform after the next barrier
@@ -930,6 +954,11 @@ void launch_w4a16(const CUtensorMap& tmap, const GemmArgs& a, dim3 grid, cudaStr
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, Plan::kTotal));
     configured = true;
   }
+  if (a.pdl) {
+    launch_kernel(w4a16_gemm_kernel<MT, GS, EPI>, grid, dim3(kThreads), Plan::kTotal, stream, tmap,
+                  a);
+    return;
+  }
   w4a16_gemm_kernel<MT, GS, EPI><<<grid, kThreads, Plan::kTotal, stream>>>(tmap, a);
   CB_CUDA_CHECK(cudaGetLastError());
 }
@@ -1056,6 +1085,11 @@ static int gemv_max_m() {
   return v;
 }
 
+// Programmatic dependent launch for the kernels launched from now on (a
+// CUDA graph keeps the setting it was captured with).
+void set_pdl(bool on) { pdl_flag() = on ? 1 : 0; }
+bool pdl_enabled() { return pdl_flag() != 0; }
+
 static bool use_gemv(int64_t M, int64_t forced_splits) {
   return forced_splits <= 0 && M <= gemv_max_m() && gemv_eligible(M);
 }
@@ -1143,6 +1177,7 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
   a.diag = diag;
   a.trace = g_gemm_trace;
   a.vec_out = vec_rows_ok(out, residual);
+  a.pdl = pdl_flag();
   TORCH_CHECK(epilogue != kEpiResid || residual.has_value(), "residual epilogue needs residual");
 
   CUtensorMap tmap = make_tmap_2d_bf16(x.data_ptr(), (uint64_t)K, (uint64_t)M,
@@ -1207,6 +1242,7 @@ void w4a16_gemm_grouped(torch::Tensor x, torch::Tensor wblob, torch::Tensor out,
   a.group_blob_stride = per;
   a.group_tiles = tiles;
   a.vec_out = vec_rows_ok(out, c10::nullopt);
+  a.pdl = pdl_flag();
   if (out_rows.has_value()) {
     TORCH_CHECK(out_rows->scalar_type() == at::kLong && out_rows->numel() >= M,
                 "out_rows: int64 row addresses, one per row of x");

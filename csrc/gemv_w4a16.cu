@@ -68,6 +68,7 @@ struct GvArgs {
   int* status;
   int M, N, K, ldx, ldo, ldr;
   int kbps, splits, stages;
+  int pdl;  // launched with programmatic stream serialisation
 };
 
 __device__ __forceinline__ uint32_t deq_pair(uint32_t w, int h, __nv_bfloat162 s2) {
@@ -122,7 +123,11 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_kernel(const GvArgs 
   const int ntiles = cta_in_split < row_tiles
                          ? (row_tiles - cta_in_split + ctas_per_split - 1) / ctas_per_split
                          : 0;
-  if (nkb <= 0 || ntiles <= 0) return;
+  if (a.pdl) grid_dep_launch();  // dependents may become resident; they wait for our end
+  if (nkb <= 0 || ntiles <= 0) {
+    grid_dep_wait();
+    return;
+  }
   const int spt = (nkb + 1) / 2;  // stages per tile
   const int total = ntiles * spt;
   const int S = a.stages;
@@ -163,13 +168,22 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_kernel(const GvArgs 
     // Producer warp: lane 0 issues all copies.
     if (lane == 0) {
       int issued = 0;
-      mbar_arrive_expect_tx(xbar, (uint32_t)(rows * nkb * 256));
-      for (int r = 0; r < rows; ++r)
-        bulk_g2s(xs + r * xstride, a.x + (size_t)r * a.ldx + (size_t)kb0 * 128,
-                 (uint32_t)(nkb * 256), xbar);
+      // X is the previous kernel's output: it is copied after the wait for
+      // that kernel.  With PDL the first S weight stages (constant data) are
+      // issued before it.
+      const int pre = a.pdl ? min(S, total) : 0;
+      auto load_x = [&] {
+        grid_dep_wait();
+        mbar_arrive_expect_tx(xbar, (uint32_t)(rows * nkb * 256));
+        for (int r = 0; r < rows; ++r)
+          bulk_g2s(xs + r * xstride, a.x + (size_t)r * a.ldx + (size_t)kb0 * 128,
+                   (uint32_t)(nkb * 256), xbar);
+      };
+      if (pre == 0) load_x();
       int slot = 0, st = 0, j = 0;
       uint32_t phase = 0;
       for (int g = 0; g < total; ++g) {
+        if (g == pre && pre > 0) load_x();
         const int rt = cta_in_split + j * ctas_per_split;
         if (g >= S &&
             !mbar_wait(&empty[slot], phase ^ 1u, a.status, kStatusGemmLoadTimeout, abort_flag))
@@ -189,6 +203,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_kernel(const GvArgs 
           phase ^= 1u;
         }
       }
+      if (pre > 0 && pre == total) load_x();  // every stage fitted in the ring
       // Do not leave while copies into this CTA's shared memory are in
       // flight (matters only when the consumers gave up early).
       for (int g = max(0, issued - S); g < issued; ++g)
@@ -199,6 +214,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_kernel(const GvArgs 
   }
 
   // ---------------------------------------------------------------- consumers
+  grid_dep_wait();  // before any global write
   const int tid = threadIdx.x;  // 0 .. kCons-1
   const int rg = warp & 7, par = warp >> 3;
   const int g = lane >> 2, c = lane & 3;
@@ -505,6 +521,10 @@ void gv_launch_t(const GvArgs& a, dim3 grid, int smem, cudaStream_t stream) {
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kGvSmemBudget + 4096));
     if (dev >= 0 && dev < 64) configured[dev] = 1;
+  }
+  if (a.pdl) {
+    launch_kernel(w4a16_gemv_kernel<GS, EPI, NT>, grid, dim3(kGvThreads), (size_t)smem, stream, a);
+    return;
   }
   w4a16_gemv_kernel<GS, EPI, NT><<<grid, kGvThreads, smem, stream>>>(a);
   CB_CUDA_CHECK(cudaGetLastError());
@@ -867,6 +887,7 @@ void gemv_launch(const void* x, int64_t ldx, const uint8_t* wblob, void* out, in
   a.ldr = (int)ldr;
   a.kbps = kbps;
   a.splits = splits;
+  a.pdl = pdl_flag();
   // Persistent CTAs: one per SM in total, each split gets an equal share.
   const int per_split = std::max(1, std::min(row_tiles, num_sms() / splits));
   const dim3 grid(per_split * splits, 1, 1);

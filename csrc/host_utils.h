@@ -6,9 +6,11 @@
 
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 #define CB_CUDA_CHECK(expr)                                                              \
   do {                                                                                   \
@@ -29,6 +31,44 @@ inline int num_sms() {
     return v > 0 ? v : 148;
   }();
   return n;
+}
+
+// Programmatic dependent launch (PDL).  A kernel launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization may become resident while
+// its predecessor in the stream still runs: as soon as every CTA of the
+// predecessor has executed griddepcontrol.launch_dependents (or exited).  Its
+// set-up (barrier init, TMEM allocation, tensor-map prefetch, the first
+// weight copies) then overlaps the predecessor's tail.  Every kernel launched
+// this way executes griddepcontrol.wait, in each thread that reads data an
+// earlier kernel wrote or writes global memory, and in at least one thread of
+// every CTA before it exits, so "predecessor complete" stays transitive along
+// the stream.
+//
+// On by default; CASCADIA_PDL=0 in the environment or set_pdl(false) turns
+// the attribute off (the kernels' griddepcontrol instructions are then
+// no-ops).  A CUDA graph keeps the setting it was captured with.
+inline int& pdl_flag() {
+  static int v = [] {
+    const char* e = std::getenv("CASCADIA_PDL");
+    return e != nullptr ? std::atoi(e) : 1;
+  }();
+  return v;
+}
+
+template <typename... KArgs, typename... Args>
+inline void launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_flag() ? 1 : 0;
+  CB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,

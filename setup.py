@@ -28,6 +28,7 @@ SOURCES = [
     "gemv_w4a16.cu",
     "ep.cu",
     "mla.cu",
+    "gdn.cu",
 ]
 
 NVCC_FLAGS = [

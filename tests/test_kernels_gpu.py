@@ -208,7 +208,8 @@ def _make_cache(seq_lens, hkv, d, layers, layer, g, nb_extra=3):
     return kc, vc, table, dense
 
 
-@pytest.mark.parametrize("d,hq,hkv", [(128, 32, 8), (64, 32, 8), (128, 16, 1)])
+@pytest.mark.parametrize("d,hq,hkv", [(128, 32, 8), (64, 32, 8), (128, 16, 1), (256, 16, 2),
+                                      (256, 4, 2)])
 @pytest.mark.parametrize("splits", [1, 3])
 def test_attn_decode(d, hq, hkv, splits):
     g = torch.Generator().manual_seed(d + hq + splits)
@@ -236,7 +237,7 @@ def test_attn_decode(d, hq, hkv, splits):
         _close(out[b].view(hq, d), e[0], rtol=2e-2, atol=2e-2)
 
 
-@pytest.mark.parametrize("d", [128, 64])
+@pytest.mark.parametrize("d", [128, 64, 256])
 def test_attn_prefill(d):
     g = torch.Generator().manual_seed(21 + d)
     hq, hkv = 8, 2
