@@ -429,6 +429,10 @@ class LLMBuilder(Builder):
             from ..models.qwen36 import HybridMoEModel
 
             return HybridMoEModel
+        if cfg.is_dsa:
+            from ..models.glm5 import GLM5Model
+
+            return GLM5Model
         if cfg.is_mla:
             from ..models.mla import MLAModel
 

@@ -17,13 +17,8 @@ class MoEBuilder(LLMBuilder):
     """LLMBuilder that always builds the MoE model (rejects dense presets)."""
 
     def model_class(self, cfg):
-        from ..models.moe import MoEModel
         from .base import InvalidConfig
 
         if not cfg.is_moe:
             raise InvalidConfig(f"{self.model_name}: not a sparse-MoE config")
-        if cfg.is_mla:
-            from ..models.mla import MLAModel
-
-            return MLAModel
-        return MoEModel
+        return super().model_class(cfg)

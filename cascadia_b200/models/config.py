@@ -48,6 +48,12 @@ class ModelConfig:
     qk_rope_head_dim: int = 0
     qk_nope_head_dim: int = 0
     v_head_dim: int = 0
+    # --- DSA sparse attention (GLM-5 / DeepSeek-V3.2 lightning indexer) ---
+    index_topk: int = 0                # 0: dense attention
+    index_n_heads: int = 0
+    index_head_dim: int = 128
+    indexer_types: Optional[tuple] = None  # per layer "full" | "shared" (None: all full)
+    mla_rope_interleaved: bool = True  # False: checkpoint rotates split halves (NeoX)
     # --- hybrid linear attention (Qwen3.5 / Qwen3.6: Gated DeltaNet layers,
     # every full_attention_interval-th layer full attention) ---
     full_attention_interval: int = 0   # 0: no linear-attention layers
@@ -59,6 +65,17 @@ class ModelConfig:
     attn_output_gate: bool = False     # full attention output * sigmoid(gate)
     shared_expert_gate: bool = False   # shared expert output * sigmoid(w . x)
     shared_expert_intermediate_size: int = 0
+
+    @property
+    def is_dsa(self) -> bool:
+        return self.index_topk > 0
+
+    def layer_has_indexer(self, li: int) -> bool:
+        """Layer li computes its own DSA top-k (IndexShare: "shared" layers
+        reuse the previous indexer layer's selection)."""
+        if not self.is_dsa:
+            return False
+        return self.indexer_types is None or self.indexer_types[li] == "full"
 
     @property
     def is_hybrid(self) -> bool:
@@ -132,6 +149,21 @@ class ModelConfig:
             c.qk_rope_head_dim = d["qk_rope_head_dim"]
             c.qk_nope_head_dim = d["qk_nope_head_dim"]
             c.v_head_dim = d["v_head_dim"]
+        if mt == "glm_moe_dsa" or d.get("index_topk"):
+            rp = d.get("rope_parameters") or {}
+            c.arch = "glm5"
+            c.rope_theta = float(rp.get("rope_theta", d.get("rope_theta", c.rope_theta)))
+            c.rope_scaling = None
+            c.index_topk = int(d["index_topk"])
+            c.index_n_heads = int(d.get("index_n_heads", 32))
+            c.index_head_dim = int(d.get("index_head_dim", 128))
+            if d.get("indexer_types"):
+                c.indexer_types = tuple(d["indexer_types"])
+            c.mla_rope_interleaved = False
+            c.router = "sigmoid"
+            types = d.get("mlp_layer_types")
+            c.first_k_dense_replace = types.index("sparse") if types and "sparse" in types else \
+                int(d.get("first_k_dense_replace", 3))
         if mt.startswith("qwen3"):
             c.qk_norm = True
         if mt.startswith("qwen3_5") or mt.startswith("qwen3_next"):
@@ -188,6 +220,18 @@ PRESETS = {
                                          "beta_slow": 1.0, "mscale": 1.0, "mscale_all_dim": 1.0,
                                          "original_max_position_embeddings": 4096},
                            eos_token_ids=(163586,)),
+    # GLM-5 (HF glm_moe_dsa): MLA + DSA lightning indexer (top-2048), 3 dense
+    # + 75 MoE layers (256 experts top-8, sigmoid + bias, 1 shared).
+    "glm-5": ModelConfig(arch="glm5", vocab_size=154880, hidden_size=6144, num_layers=78,
+                         num_heads=64, num_kv_heads=64, head_dim=256, intermediate_size=12288,
+                         rope_theta=8000000.0, rms_eps=1e-5, num_experts=256,
+                         num_experts_per_tok=8, moe_intermediate_size=2048, num_shared_experts=1,
+                         router="sigmoid", norm_topk_prob=True, routed_scaling_factor=2.5,
+                         first_k_dense_replace=3, q_lora_rank=2048, kv_lora_rank=512,
+                         qk_rope_head_dim=64, qk_nope_head_dim=192, v_head_dim=256,
+                         index_topk=2048, index_n_heads=32, index_head_dim=128,
+                         mla_rope_interleaved=False, group_size=32, max_position=202752,
+                         eos_token_ids=(1,)),
     # Qwen3.6-35B-A3B (HF qwen3_5_moe): 30 Gated DeltaNet + 10 gated
     # full-attention layers (head_dim 256, rotary on 64 dims), 256 experts
     # top-8 + a sigmoid-gated shared expert.
@@ -227,6 +271,19 @@ PRESETS = {
                                           "mscale_all_dim": 1.0,
                                           "original_max_position_embeddings": 4096},
                             eos_token_ids=(1,)),
+    # GLM-5 layer structure at small width: MLA (latent 512, rope 64; nope
+    # 192 / v 256 as in GLM-5), DSA indexer with top-8 (so selection matters
+    # at test lengths), IndexShare on layer 2, 1 dense + 2 MoE layers.
+    "tiny-glm5": ModelConfig(arch="glm5", vocab_size=512, hidden_size=256, num_layers=3,
+                             num_heads=8, num_kv_heads=8, head_dim=256, intermediate_size=512,
+                             rope_theta=8000000.0, rms_eps=1e-5, num_experts=8,
+                             num_experts_per_tok=2, moe_intermediate_size=128,
+                             num_shared_experts=1, router="sigmoid", norm_topk_prob=True,
+                             routed_scaling_factor=2.5, first_k_dense_replace=1, q_lora_rank=256,
+                             kv_lora_rank=512, qk_rope_head_dim=64, qk_nope_head_dim=192,
+                             v_head_dim=256, index_topk=8, index_n_heads=16, index_head_dim=128,
+                             indexer_types=("full", "full", "shared"), mla_rope_interleaved=False,
+                             eos_token_ids=(1,)),
     # Qwen3.6 layer structure at small width (linear head dims are the real
     # 128; full attention head_dim 256 as in the real model).
     "tiny-qwen36": ModelConfig(arch="qwen3_5_moe", vocab_size=512, hidden_size=256, num_layers=4,

@@ -86,10 +86,11 @@ class MLAModel(MoEModel):
         super().__init__(cfg, device, **kw)
         assert cfg.kv_lora_rank == LATENT and cfg.qk_rope_head_dim == ROPE, \
             "the MLA kernels are built for a 512-wide latent and a 64-wide rope key"
-        self.nope = cfg.qk_nope_head_dim
-        self.vd = cfg.v_head_dim
-        assert self.nope == 128 and self.vd == 128, "qk_nope_head_dim = v_head_dim = 128"
+        self.nope = cfg.qk_nope_head_dim   # 128 (Kimi-K2) or 192 (GLM-5)
+        self.vd = cfg.v_head_dim           # 128 or 256
         self.qk_dim = self.nope + ROPE
+        # The q_a / kv_a RMSNorms use eps 1e-6 (the published MLA norms).
+        self.lora_eps = 1e-6
         self.scale = 1.0 / math.sqrt(self.qk_dim)
         self.hq = cfg.num_heads
 
@@ -152,27 +153,43 @@ class MLAModel(MoEModel):
                 self._moe(lw, h, hidden)
         return hidden
 
+    def _norm_eps(self, x, w, out, eps):
+        if self.device.type == "cuda":
+            return ops.rmsnorm(x, w, out, eps)
+        out.copy_(ref.rmsnorm(x, w, eps).to(torch.bfloat16))
+        return out
+
     def _q_and_kv(self, a: MLAAttention, x: torch.Tensor):
+        """(q, normalised latent c, rope key, q_a residual or None)."""
+        qa_n = None
         if a.q_a is not None:
             qa = a.q_a(x)
             qa_n = torch.empty_like(qa)
-            self._norm(qa, a.q_a_norm, qa_n)
+            self._norm_eps(qa, a.q_a_norm, qa_n, self.lora_eps)
             q = a.q_b(qa_n)
         else:
             q = a.q_b(x)
         kva = a.kv_a(x)  # [T, 640]: latent | rope key | zero pad
         c = torch.empty(x.shape[0], LATENT, dtype=x.dtype, device=x.device)
-        self._norm(kva[:, :LATENT], a.kv_a_norm, c)
-        return q, c, kva[:, LATENT:ROW]
+        self._norm_eps(kva[:, :LATENT], a.kv_a_norm, c, self.lora_eps)
+        return q, c, kva[:, LATENT:ROW], qa_n
 
     def _mla(self, li: int, a: MLAAttention, x: torch.Tensor, batch: Batch) -> torch.Tensor:
-        q, c, kr = self._q_and_kv(a, x)
+        q, c, kr, _ = self._q_and_kv(a, x)
         if self.device.type == "cuda":
             return self._mla_gpu(li, a, q, c, kr, batch)
         return self._mla_cpu(li, a, q, c, kr, batch)
 
+    def _virtual_seqs(self, batch: Batch):
+        """Block tables and lengths with one row per query token (prefill:
+        each token is a sequence of its own context length)."""
+        if batch.is_decode:
+            return batch.block_tables, batch.seq_lens
+        return batch.block_tables.index_select(0, self._tok2seq(batch)), batch.positions + 1
+
     # ------------------------------------------------------------ GPU (absorbed)
-    def _mla_gpu(self, li, a, q, c, kr, batch):
+    def _mla_gpu(self, li, a, q, c, kr, batch, sel=None):
+        """sel: optional DSA selection (scores [T, ld] fp32, thresholds [T])."""
         T, H = q.shape[0], self.hq
         q3 = q.view(T, H, self.qk_dim)
         q_full = torch.empty(T, H, ROW, dtype=torch.bfloat16, device=q.device)
@@ -182,21 +199,18 @@ class MLAModel(MoEModel):
         ops.ext().mla_rope_write(c, kr, q3[:, 0, self.nope:], self.qk_dim, q_full,
                                  batch.positions, self.cos_sin, batch.slots, self.kv.k, li, H)
         o_lat = torch.empty(T, H, LATENT, dtype=torch.bfloat16, device=q.device)
-        if batch.is_decode:
-            bt, lens = batch.block_tables, batch.seq_lens
-        else:
-            # One virtual sequence per query token: its own context length.
-            bt = batch.block_tables.index_select(0, self._tok2seq(batch))
-            lens = batch.positions + 1
+        bt, lens = self._virtual_seqs(batch)
         splits, bps = mla_split_plan(T, H, bt.shape[1])
         part_o = part_ml = o_lat
         if splits > 1:
             part_o = torch.empty(T * H * splits * LATENT, dtype=torch.float32, device=q.device)
             part_ml = torch.empty(T * H * splits * 2, dtype=torch.float32, device=q.device)
         ops.ext().mla_decode(q_full, self.kv.k, bt, lens, o_lat, li, splits, bps, part_o, part_ml,
-                             self.scale, ops.status_buffer(q.device))
+                             self.scale, ops.status_buffer(q.device),
+                             sel[0] if sel is not None else None,
+                             sel[1] if sel is not None else None)
         ops.LAUNCHES.add(3 if splits > 1 else 2)
-        out = torch.bmm(o_lat.transpose(0, 1), a.w_uv.transpose(1, 2))  # [H, T, 128]
+        out = torch.bmm(o_lat.transpose(0, 1), a.w_uv.transpose(1, 2))  # [H, T, v]
         return out.transpose(0, 1).reshape(T, H * self.vd)
 
     def _tok2seq(self, batch: Batch) -> torch.Tensor:
@@ -208,7 +222,7 @@ class MLAModel(MoEModel):
         return batch._tok2seq[1]
 
     # ------------------------------------------------------------ CPU oracle
-    def _mla_cpu(self, li, a, q, c, kr, batch):
+    def _mla_cpu(self, li, a, q, c, kr, batch, sel=None):
         T, H = q.shape[0], self.hq
         pos = batch.positions.long()
         q3 = q.float().view(T, H, self.qk_dim)
@@ -224,13 +238,16 @@ class MLAModel(MoEModel):
             lat = self.kv.gather_latent(li, sid).float()
             ctx = int(batch.ctx_len_of(sid))
             cc, kk_r = lat[:ctx, :LATENT], lat[:ctx, LATENT:]
-            k_nope = torch.einsum("hdl,tl->thd", a.w_uk, cc)          # [ctx, H, 128]
-            v = torch.einsum("hdl,tl->thd", a.w_uv, cc)               # [ctx, H, 128]
+            k_nope = torch.einsum("hdl,tl->thd", a.w_uk, cc)          # [ctx, H, nope]
+            v = torch.einsum("hdl,tl->thd", a.w_uv, cc)               # [ctx, H, v]
             k = torch.cat([k_nope, kk_r[:, None, :].expand(ctx, H, ROPE)], dim=2)
             qq = torch.cat([q3[r:r + ql, :, :self.nope], q_rope[r:r + ql]], dim=2)
             s = torch.einsum("qhd,thd->hqt", qq, k) * self.scale
             qpos = pos[r:r + ql]
             mask = torch.arange(ctx)[None, :] > qpos[:, None]
+            if sel is not None:  # DSA: only the selected positions
+                sc, thr = sel
+                mask = mask | (sc[r:r + ql, :ctx] < thr[r:r + ql, None])
             s = s.masked_fill(mask[None], float("-inf"))
             p = torch.softmax(s, dim=-1)
             out[r:r + ql] = torch.einsum("hqt,thd->qhd", p, v)

@@ -236,6 +236,18 @@ class HybridMoEModel(MoEModel):
     def state_bytes_per_seq(self) -> int:
         return HybridKVCache.state_bytes(self.n_linear, self.conv_ch, self.hv, self.dk, self.dv)
 
+    def save_state(self, batch: Batch):
+        """Copies of the batch's recurrent and conv state (the CUDA-graph
+        warm-up runs the step several times; each run advances the state)."""
+        kv = self.kv
+        slots = kv.block_slot.index_select(0, batch.block_tables[:, 0].long()).long()
+        return slots, kv.conv.index_select(1, slots), kv.rec.index_select(1, slots)
+
+    def restore_state(self, saved):
+        slots, conv, rec = saved
+        self.kv.conv.index_copy_(1, slots, conv)
+        self.kv.rec.index_copy_(1, slots, rec)
+
     def _seq_start(self, batch: Batch) -> torch.Tensor:
         key = tuple(batch.q_lens)
         t = self._seq_start_cache.get(key)

@@ -86,6 +86,10 @@ class DecodeGraph:
         """Capture the step into a CUDA graph (inputs must hold valid data)."""
         if not self.use_graph:
             return
+        # Models with recurrent state (linear attention) advance it on every
+        # step: keep the batch's state as it was before the warm-up steps.
+        m = self.model
+        saved = m.save_state(self.batch_view) if hasattr(m, "save_state") else None
         s = torch.cuda.Stream(device=self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(s):
@@ -93,6 +97,9 @@ class DecodeGraph:
                 self._step()
         torch.cuda.current_stream(self.dev).wait_stream(s)
         torch.cuda.synchronize(self.dev)
+        if saved is not None:
+            m.restore_state(saved)
+            torch.cuda.synchronize(self.dev)
         self.graph = torch.cuda.CUDAGraph()
         ops.LAUNCHES.start()
         with torch.cuda.graph(self.graph, stream=s):

