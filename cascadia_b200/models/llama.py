@@ -74,6 +74,7 @@ class LayerWeights:
     o: QLinear
     gate_up: QLinear
     down: QLinear
+    sparse: Optional[object] = None  # ops.ffn_sparse.SparseFFN when enabled
 
 
 class TPGroup:
@@ -216,6 +217,20 @@ class LlamaModel:
             tensors["post_attention_layernorm"].to(torch.bfloat16)))
 
     # ------------------------------------------------------------ KV cache
+    def enable_ffn_sparsity(self, tau_all: float = 0.05, taus=None):
+        """Single-token steps (TP=1) run the activation-sparse FFN: lanes with
+        |silu(gate)| below tau (x the token's max) skip up and down.  Off by
+        default; needs the INT4 weights kept at build time (KEEP_INT4)."""
+        from ..ops.ffn_sparse import SparseFFN
+
+        for i, lw in enumerate(self.layers):
+            gu, dn = lw.gate_up.int4, lw.down.int4
+            if gu is None or dn is None:
+                raise RuntimeError("build the model with llama.KEEP_INT4 = True first")
+            inter = gu.n // 2
+            lw.sparse = SparseFFN(gu.rows(0, inter), gu.rows(inter, 2 * inter), dn, self.device,
+                                  tau_all, taus[i] if taus is not None else None)
+
     def allocate_kv(self, num_blocks: int) -> KVCache:
         self.kv = KVCache(self.num_local_layers, num_blocks, self.hkv, self.d, self.device)
         return self.kv
@@ -265,6 +280,10 @@ class LlamaModel:
             else:
                 part = self.tp.all_reduce(lw.o(attn))
                 self._norm(part, lw.post_norm, h, residual=hidden)
+            if tp1 and T == 1 and lw.sparse is not None:
+                lw.sparse(h, residual=hidden, out=hidden)  # activation-sparse FFN
+                pending = None
+                continue
             act = lw.gate_up(h, ops.EPI_SILU)
             if tp1:
                 lw.down(act, ops.EPI_RESID, residual=hidden, out=hidden)

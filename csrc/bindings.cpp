@@ -19,6 +19,14 @@ void gdn_recurrent(torch::Tensor qkv, torch::Tensor z, torch::Tensor ab, torch::
                    torch::Tensor seq_start, torch::Tensor block_tables, torch::Tensor block_slot,
                    torch::Tensor out, int64_t Hk, int64_t Hv, double eps);
 void sigmoid_gate(torch::Tensor x, torch::Tensor gate);
+// ffn_sparse.cu
+void ffn_sparse_forward(torch::Tensor x, torch::Tensor gate_packed, torch::Tensor gate_scales,
+                        torch::Tensor up_packed, torch::Tensor up_scales,
+                        torch::Tensor downT_packed, torch::Tensor downT_scales,
+                        c10::optional<torch::Tensor> tau, double tau_all,
+                        c10::optional<torch::Tensor> residual, torch::Tensor out,
+                        torch::Tensor iwork, torch::Tensor fwork, int64_t group_size,
+                        int64_t down_group_size);
 bool pdl_enabled();
 int64_t w4a16_counter_count(int64_t M, int64_t N);
 void w4a16_set_trace(c10::optional<torch::Tensor> buf);
@@ -120,6 +128,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_conv", &cb::gdn_conv);
   m.def("gdn_recurrent", &cb::gdn_recurrent);
   m.def("sigmoid_gate", &cb::sigmoid_gate);
+  m.def("ffn_sparse_forward", &cb::ffn_sparse_forward);
   m.def("pdl_enabled", &cb::pdl_enabled);
   m.def("attn_decode", &cb::attn_decode);
   m.def("attn_prefill", &cb::attn_prefill);

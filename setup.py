@@ -29,6 +29,7 @@ SOURCES = [
     "ep.cu",
     "mla.cu",
     "gdn.cu",
+    "ffn_sparse.cu",
 ]
 
 NVCC_FLAGS = [

@@ -184,11 +184,19 @@ def test_hybrid_engine_batched_solo_and_chunked(device):
     prompts = [torch.randint(3, 500, (n,), generator=g).tolist() for n in (5, 24, 11)]
     tasks = [GenerationTask(f"t{i}", "", max_tokens=4, prompt_ids=p) for i, p in enumerate(prompts)]
     batched = _run(e, tasks)
+    def same(a, b):
+        # CPU: bit-identical.  GPU: batch size changes the cuBLAS algorithm
+        # of the shared-expert gate and the attention split plan, so a late
+        # near-tie may flip; leaked state would change every token.
+        if device == "cpu":
+            return a == b
+        return a[:2] == b[:2] and sum(x == y for x, y in zip(a, b)) >= 3
+
     for i, t in enumerate(tasks):
         solo = _run(e, [GenerationTask(f"s{i}", "", max_tokens=4, prompt_ids=t.prompt_ids)])
-        assert solo[f"s{i}"] == batched[t.task_id]
+        assert same(solo[f"s{i}"], batched[t.task_id]), (solo, batched)
     # Prefill in chunks carries the conv and recurrent state across chunks.
     e.sched.max_prefill_tokens = 8
     chunked = _run(e, [GenerationTask("c", "", max_tokens=4, prompt_ids=prompts[1])])
-    assert chunked["c"] == batched["t1"]
+    assert same(chunked["c"], batched["t1"]), (chunked, batched)
     assert not e.model.kv.slot_of and len(e.model.kv.free_slots) == 8
