@@ -246,7 +246,8 @@ class LLMEngine(Engine):
             pos[i] = p
             slots[i] = st.blocks[p // BLOCK_SIZE] * BLOCK_SIZE + p % BLOCK_SIZE
             lens[i] = p + 1
-            table[i, :len(st.blocks)] = st.blocks
+            kv.slide(s.seq_id, self.model.cfg, p)
+            table[i, :len(st.blocks)] = np.maximum(st.blocks, 0)
         g.fill(ids, pos, slots, lens, table)
         g.upload()
         if g.use_graph and g.graph is None:

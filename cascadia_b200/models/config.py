@@ -31,6 +31,10 @@ class ModelConfig:
     partial_rotary_factor: float = 1.0
     max_position: int = 131072
     group_size: int = 128
+    # Sliding-window attention (0: full causal): keys within the last
+    # `sliding_window` positions plus the first `attention_sinks` ones.
+    sliding_window: int = 0
+    attention_sinks: int = 0
     eos_token_ids: tuple = (128001, 128009)
     # --- sparse MoE ---
     num_experts: int = 0
@@ -129,6 +133,9 @@ class ModelConfig:
             partial_rotary_factor=float(d.get("partial_rotary_factor", 1.0)),
             max_position=int(d.get("max_position_embeddings", 131072)),
         )
+        if d.get("sliding_window") and d.get("use_sliding_window", True) and \
+                d.get("model_type", "") in ("mistral", "mixtral", "qwen2", "starcoder2"):
+            c.sliding_window = int(d["sliding_window"])
         eos = d.get("eos_token_id")
         if eos is not None:
             c.eos_token_ids = tuple(eos) if isinstance(eos, list) else (eos,)

@@ -323,13 +323,14 @@ class LlamaModel:
                               hq, hkv, d, self.cfg.rot_dim)
             out = torch.empty(T, hq * d, dtype=torch.bfloat16, device=self.device)
             q = qkv[:, :hq * d]
+            win, sinks = self.cfg.sliding_window, self.cfg.attention_sinks
             if batch.is_decode:
                 ops.attn_decode(q, kv.k, kv.v, batch.block_tables, batch.seq_lens, out, li,
                                 batch.num_splits, batch.blocks_per_split, batch.part_o,
-                                batch.part_ml, self.scale)
+                                batch.part_ml, self.scale, win, sinks)
             else:
                 ops.attn_prefill(q, kv.k, kv.v, batch.block_tables, batch.tiles, out, li,
-                                 self.scale)
+                                 self.scale, win, sinks)
             return out
         # CPU oracle path.
         x = qkv.float().view(T, hq + 2 * hkv, d)
@@ -347,7 +348,8 @@ class LlamaModel:
         for sid, ql in zip(batch.seq_ids, batch.q_lens):
             kk, vv = kv.gather(li, sid)
             ctx = int(batch.ctx_len_of(sid))
-            o = ref.attention(q[row:row + ql], kk[:ctx], vv[:ctx], pos[row:row + ql], self.scale)
+            o = ref.attention(q[row:row + ql], kk[:ctx], vv[:ctx], pos[row:row + ql], self.scale,
+                              self.cfg.sliding_window, self.cfg.attention_sinks)
             out[row:row + ql] = o.reshape(ql, hq * d)
             row += ql
         return out.to(torch.bfloat16)
@@ -418,6 +420,7 @@ def build_batch(model: LlamaModel, seq_ids: Sequence[str], q_lens: Sequence[int]
     pos, slots, ctx = [], [], []
     for sid, ql, p0 in zip(seq_ids, q_lens, positions_start):
         kv.reserve(sid, p0 + ql)
+        kv.slide(sid, model.cfg, p0)
         s = kv.seqs[sid]
         s.length = max(s.length, p0 + ql)
         pos.extend(range(p0, p0 + ql))

@@ -166,18 +166,23 @@ def w4a16_plan(m: int, n: int, k: int, splits: int = 0):
 
 # ----------------------------------------------------------------- attention
 def attn_decode(q, k_cache, v_cache, block_tables, seq_lens, out, layer: int, num_splits: int,
-                blocks_per_split: int, part_o, part_ml, scale: float):
+                blocks_per_split: int, part_o, part_ml, scale: float, window: int = 0,
+                sinks: int = 0):
+    """Paged decode attention; ``window`` > 0: sliding window of that many
+    positions (plus the first ``sinks`` positions)."""
     if _dbg.ENABLED and not torch.cuda.is_current_stream_capturing():
         _dbg.check_paged(block_tables, seq_lens, k_cache.shape[1])
     ext().attn_decode(q, k_cache, v_cache, block_tables, seq_lens, out, layer, num_splits,
-                      blocks_per_split, part_o, part_ml, scale, status_buffer(q.device))
+                      blocks_per_split, part_o, part_ml, scale, status_buffer(q.device), window,
+                      sinks)
     LAUNCHES.add(2 if num_splits > 1 else 1)
     return out
 
 
-def attn_prefill(q, k_cache, v_cache, block_tables, tiles, out, layer: int, scale: float):
+def attn_prefill(q, k_cache, v_cache, block_tables, tiles, out, layer: int, scale: float,
+                 window: int = 0, sinks: int = 0):
     ext().attn_prefill(q, k_cache, v_cache, block_tables, tiles, out, layer, scale,
-                       status_buffer(q.device))
+                       status_buffer(q.device), window, sinks)
     LAUNCHES.add(1)
     return out
 

@@ -62,10 +62,11 @@ def apply_rope(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, 
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Tensor,
-              scale: float) -> torch.Tensor:
+              scale: float, window: int = 0, sinks: int = 0) -> torch.Tensor:
     """Causal GQA attention for one sequence.
 
     q: [Tq, Hq, D], k/v: [Tk, Hkv, D] (positions 0..Tk-1), q_pos: [Tq].
+    window > 0: a query at q sees keys q - window < k <= q and k < sinks.
     """
     tq, hq, d = q.shape
     tk, hkv, _ = k.shape
@@ -75,6 +76,9 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Te
     s = torch.einsum("qhd,khd->hqk", q.float(), kf) * scale
     kpos = torch.arange(tk)
     mask = kpos[None, :] > q_pos.long()[:, None]  # [Tq, Tk]
+    if window > 0:
+        far = kpos[None, :] <= q_pos.long()[:, None] - window
+        mask = mask | (far & (kpos[None, :] >= sinks))
     s = s.masked_fill(mask[None], float("-inf"))
     p = torch.softmax(s, dim=-1)
     return torch.einsum("hqk,khd->qhd", p, vf)

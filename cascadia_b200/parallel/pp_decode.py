@@ -66,7 +66,8 @@ class PipelinedDecoder:
             pos[i] = p
             slots[i] = s.blocks[p // BLOCK_SIZE] * BLOCK_SIZE + p % BLOCK_SIZE
             lens[i] = p + 1
-            table[i, :len(s.blocks)] = s.blocks
+            kv.slide(sid, self.m.cfg, p)
+            table[i, :len(s.blocks)] = np.maximum(s.blocks, 0)
         # ids arrive by p2p (stage 0) or are unused: keep what is in the buffer.
         g.fill(g.host.numpy()[:b].copy(), pos, slots, lens, table)
         # The CPU oracle attention looks sequences up by id.

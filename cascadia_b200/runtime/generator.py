@@ -178,7 +178,8 @@ class BatchGenerator:
             pos[i] = p
             slots[i] = s.blocks[p // BLOCK_SIZE] * BLOCK_SIZE + p % BLOCK_SIZE
             lens[i] = p + 1
-            table[i, :len(s.blocks)] = s.blocks
+            kv.slide(sid, self.model.cfg, p)
+            table[i, :len(s.blocks)] = np.maximum(s.blocks, 0)
         g.fill(np.asarray(last_tokens, dtype=np.int32), pos, slots, lens, table)
 
     def decode(self, seq_ids: Sequence[str], last_tokens, width: int) -> torch.Tensor:

@@ -115,25 +115,48 @@ class KVCache:
         s.length = min(s.length, new_length)
         keep = (s.length + BLOCK_SIZE - 1) // BLOCK_SIZE
         if keep < len(s.blocks):
-            self.allocator.free(s.blocks[keep:])
+            self.allocator.free([b for b in s.blocks[keep:] if b >= 0])
             s.blocks = s.blocks[:keep]
+
+    def evict_before(self, seq_id: str, first_needed: int, sinks: int = 0) -> int:
+        """Sliding-window attention: return the blocks whose positions all lie
+        before ``first_needed`` (and past the ``sinks`` first positions) to
+        the pool.  Their table entries become -1 (the kernels never read
+        them; the device tables carry block 0 there).  Returns blocks freed."""
+        s = self.seqs[seq_id]
+        lo = -(-sinks // BLOCK_SIZE)
+        hi = min(len(s.blocks), max(0, first_needed) // BLOCK_SIZE)
+        gone = [j for j in range(lo, hi) if s.blocks[j] >= 0]
+        if gone:
+            self.allocator.free([s.blocks[j] for j in gone])
+            for j in gone:
+                s.blocks[j] = -1
+        return len(gone)
+
+    def slide(self, seq_id: str, cfg, first_query_pos: int):
+        """Free what a sliding-window model no longer reads (no-op without
+        a window): blocks wholly before the earliest key the queries from
+        ``first_query_pos`` on can see."""
+        w = getattr(cfg, "sliding_window", 0)
+        if w > 0:
+            self.evict_before(seq_id, first_query_pos - w + 1, cfg.attention_sinks)
 
     def free_sequence(self, seq_id: str):
         s = self.seqs.pop(seq_id, None)
         if s is not None:
-            self.allocator.free(s.blocks)
+            self.allocator.free([b for b in s.blocks if b >= 0])
 
     def block_table(self, seq_ids: List[str], width: int, device) -> torch.Tensor:
         t = torch.zeros(len(seq_ids), width, dtype=torch.int32)
         for i, sid in enumerate(seq_ids):
             b = self.seqs[sid].blocks
-            t[i, :len(b)] = torch.tensor(b, dtype=torch.int32)
+            t[i, :len(b)] = torch.tensor(b, dtype=torch.int32).clamp_min(0)
         return t.to(device, non_blocking=True)
 
     def gather(self, layer: int, seq_id: str):
         """Dense [len, H, D] copies of one sequence's K/V (CPU oracle path)."""
         s = self.seqs[seq_id]
-        ids = torch.tensor(s.blocks, dtype=torch.long, device=self.k.device)
+        ids = torch.tensor(s.blocks, dtype=torch.long, device=self.k.device).clamp_min(0)
         k = self.k[layer, ids].permute(0, 2, 1, 3).reshape(-1, self.kv_heads, self.k.shape[-1])
         v = self.v[layer, ids].permute(0, 2, 1, 3).reshape(-1, self.kv_heads, self.v.shape[-1])
         return k, v

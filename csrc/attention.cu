@@ -43,7 +43,32 @@ struct DecodeArgs {
   int layer;
   int blocks_per_split, splits;
   float scale_log2;
+  // Sliding window (0: none): a query at position q sees keys k with
+  // q - window < k <= q, plus the first `sinks` positions (attention sinks).
+  int window, sinks;
 };
+
+// Visible 16-token blocks of a window: the sink blocks [0, nsb) then the
+// window blocks from wb0 on; virtual block v maps to block block_of(v).
+struct VisibleBlocks {
+  int nsb, wb0, n;
+  __device__ __forceinline__ int block_of(int v) const { return v < nsb ? v : wb0 + (v - nsb); }
+};
+
+__device__ __forceinline__ VisibleBlocks visible_blocks(int first_visible, int total_blocks,
+                                                        int window, int sinks) {
+  VisibleBlocks vb;
+  if (window <= 0) {
+    vb.nsb = total_blocks;
+    vb.wb0 = total_blocks;
+    vb.n = total_blocks;
+    return vb;
+  }
+  vb.wb0 = min(total_blocks, max(0, first_visible) >> 4);
+  vb.nsb = min((sinks + 15) >> 4, vb.wb0);
+  vb.n = vb.nsb + (total_blocks - vb.wb0);
+  return vb;
+}
 
 template <int D>
 __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant__ CUtensorMap tk,
@@ -71,7 +96,11 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
   grid_dep_wait();  // q, the cache rows and the lengths come from earlier kernels
 
   const int seq_len = a.seq_lens[b];
-  const int nblocks = (seq_len + 15) >> 4;
+  // The query is at position seq_len - 1: with a window it sees positions
+  // from seq_len - window on (and the sinks).
+  const VisibleBlocks vis =
+      visible_blocks(seq_len - a.window, (seq_len + 15) >> 4, a.window, a.sinks);
+  const int nblocks = vis.n;
   const int blk0 = sp * a.blocks_per_split;
   const int blk1 = min(nblocks, blk0 + a.blocks_per_split);
   // This warp handles blocks blk0 + warp, blk0 + warp + 4, ...
@@ -87,7 +116,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
   const int* bt = a.block_tables + (size_t)b * a.bt_stride;
   const int row_base_layer = a.layer * a.NB;
   auto issue = [&](int i, int st) {
-    const int j = blk0 + warp + 4 * i;
+    const int j = vis.block_of(blk0 + warp + 4 * i);
     const int phys = bt[j];
     const int row = ((row_base_layer + phys) * a.Hkv + h) * 16;
     uint8_t* kb = wbuf + st * STAGE;
@@ -167,7 +196,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
         mma_16816(s[1], qa[ks], b10, b11);
       }
     }
-    const int j = blk0 + warp + 4 * i;
+    const int j = vis.block_of(blk0 + warp + 4 * i);
     const int pos0 = j * 16;
     float p[2][4];
 #pragma unroll
@@ -179,7 +208,9 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
         for (int e = 0; e < 2; ++e) {
           const int pos = pos0 + nt * 8 + 2 * t4 + e;
           float v = s[nt][2 * r + e] * a.scale_log2;
-          v = pos < seq_len ? v : -INFINITY;
+          const bool seen =
+              pos < seq_len && (a.window <= 0 || pos >= seq_len - a.window || pos < a.sinks);
+          v = seen ? v : -INFINITY;
           s[nt][2 * r + e] = v;
           mx = fmaxf(mx, v);
         }
@@ -322,6 +353,7 @@ struct PrefillArgs {
   int* status;
   int Hq, Hkv, G, NB, layer;
   float scale_log2;
+  int window, sinks;  // as in DecodeArgs
 };
 
 // One CTA = 64 query rows (4 warps x 16) of one query head.  K/V tiles of 64
@@ -351,7 +383,16 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __grid_constant
   const int4 tinfo = a.tiles[blockIdx.x];
   const int b = tinfo.x, qrow0 = tinfo.y, pos0 = tinfo.z, nq = tinfo.w;
   const int kv_len = pos0 + nq;  // causal: the last query sees everything before it
-  const int ntiles = (kv_len + 63) / 64;
+  // 64-token tiles with something visible to this tile's queries (with a
+  // window, the first query pos0 sees from pos0 - window + 1 on).
+  const int all_tiles = (kv_len + 63) / 64;
+  int nst = all_tiles, wt0 = all_tiles;
+  if (a.window > 0) {
+    wt0 = min(all_tiles, max(0, pos0 - a.window + 1) / 64);
+    nst = min((a.sinks + 63) / 64, wt0);
+  }
+  const int ntiles = a.window > 0 ? nst + (all_tiles - wt0) : all_tiles;
+  auto tile_of = [&](int v) { return v < nst ? v : wt0 + (v - nst); };
   const int* bt = a.block_tables + (size_t)b * a.bt_stride;
 
   if (threadIdx.x == 0) {
@@ -362,7 +403,8 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __grid_constant
   }
   __syncthreads();
 
-  auto issue = [&](int ti, int st) {
+  auto issue = [&](int vt, int st) {
+    const int ti = tile_of(vt);
     uint8_t* base = smem + st * STAGE;
     const int nblk = min(4, ((kv_len - ti * 64) + 15) / 16);
     mbar_arrive_expect_tx(&full[st], nblk * 2 * BLK_BYTES);
@@ -425,7 +467,7 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __grid_constant
     if (!mbar_wait(&full[st], (ti >> 1) & 1, a.status, kStatusAttnTimeout, &s_abort)) break;
     const uint32_t kaddr = smem_u32(smem + st * STAGE);
     const uint32_t vaddr = kaddr + TILE_BYTES;
-    const int kpos0 = ti * 64;
+    const int kpos0 = tile_of(ti) * 64;
     if (kpos0 <= warp_last_pos) {
       float s[8][4];
 #pragma unroll
@@ -465,7 +507,9 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __grid_constant
           for (int e = 0; e < 2; ++e) {
             const int kp = kpos0 + nt * 8 + 2 * t4 + e;
             float v = s[nt][2 * r + e] * a.scale_log2;
-            v = (kp <= qpos[r] && kp < kv_len) ? v : -INFINITY;
+            const bool seen = kp <= qpos[r] && kp < kv_len &&
+                              (a.window <= 0 || kp > qpos[r] - a.window || kp < a.sinks);
+            v = seen ? v : -INFINITY;
             s[nt][2 * r + e] = v;
             mx = fmaxf(mx, v);
           }
@@ -554,7 +598,8 @@ static CUtensorMap kv_tmap(const torch::Tensor& cache) {
 void attn_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                  torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
                  int64_t layer, int64_t num_splits, int64_t blocks_per_split,
-                 torch::Tensor part_o, torch::Tensor part_ml, double scale, torch::Tensor status) {
+                 torch::Tensor part_o, torch::Tensor part_ml, double scale, torch::Tensor status,
+                 int64_t window, int64_t sinks) {
   TORCH_CHECK(k_cache.dim() == 5 && k_cache.is_contiguous() && v_cache.is_contiguous(),
               "kv cache must be [L, NB, Hkv, 16, D] contiguous");
   TORCH_CHECK(k_cache.size(3) == 16, "block size must be 16");
@@ -586,6 +631,8 @@ void attn_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
   a.blocks_per_split = (int)blocks_per_split;
   a.splits = (int)num_splits;
   a.scale_log2 = (float)scale * kLog2e;
+  a.window = (int)window;
+  a.sinks = (int)sinks;
   if (num_splits > 1) {
     TORCH_CHECK(part_o.numel() >= (int64_t)B * Hkv * num_splits * a.G * D, "part_o too small");
     TORCH_CHECK(part_ml.numel() >= (int64_t)B * Hkv * num_splits * a.G * 2, "part_ml too small");
@@ -643,7 +690,7 @@ void attn_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
 // q: [T, Hq*D]; tiles: int32 [n_tiles, 4] {seq, first row, first position, rows}
 void attn_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                   torch::Tensor block_tables, torch::Tensor tiles, torch::Tensor out, int64_t layer,
-                  double scale, torch::Tensor status) {
+                  double scale, torch::Tensor status, int64_t window, int64_t sinks) {
   const int D = (int)k_cache.size(4);
   const int Hkv = (int)k_cache.size(2);
   const int Hq = (int)(q.size(1) / D);
@@ -668,6 +715,8 @@ void attn_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
   a.NB = (int)k_cache.size(1);
   a.layer = (int)layer;
   a.scale_log2 = (float)scale * kLog2e;
+  a.window = (int)window;
+  a.sinks = (int)sinks;
   CUtensorMap tk = kv_tmap(k_cache), tv = kv_tmap(v_cache);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   dim3 grid(n_tiles, Hq);

@@ -91,10 +91,11 @@ void moe_combine(torch::Tensor y, torch::Tensor inv, torch::Tensor w,
 void attn_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                  torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
                  int64_t layer, int64_t num_splits, int64_t blocks_per_split,
-                 torch::Tensor part_o, torch::Tensor part_ml, double scale, torch::Tensor status);
+                 torch::Tensor part_o, torch::Tensor part_ml, double scale, torch::Tensor status,
+                 int64_t window, int64_t sinks);
 void attn_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                   torch::Tensor block_tables, torch::Tensor tiles, torch::Tensor out, int64_t layer,
-                  double scale, torch::Tensor status);
+                  double scale, torch::Tensor status, int64_t window, int64_t sinks);
 // elementwise.cu
 void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out, int64_t vocab_lo);
 void rmsnorm(torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tensor w,
@@ -130,8 +131,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sigmoid_gate", &cb::sigmoid_gate);
   m.def("ffn_sparse_forward", &cb::ffn_sparse_forward);
   m.def("pdl_enabled", &cb::pdl_enabled);
-  m.def("attn_decode", &cb::attn_decode);
-  m.def("attn_prefill", &cb::attn_prefill);
+  m.def("attn_decode", &cb::attn_decode, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("block_tables"), py::arg("seq_lens"), py::arg("out"), py::arg("layer"),
+        py::arg("num_splits"), py::arg("blocks_per_split"), py::arg("part_o"), py::arg("part_ml"),
+        py::arg("scale"), py::arg("status"), py::arg("window") = 0, py::arg("sinks") = 0);
+  m.def("attn_prefill", &cb::attn_prefill, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("block_tables"), py::arg("tiles"), py::arg("out"), py::arg("layer"),
+        py::arg("scale"), py::arg("status"), py::arg("window") = 0, py::arg("sinks") = 0);
   m.def("embedding", &cb::embedding);
   m.def("rmsnorm", &cb::rmsnorm);
   m.def("rope_kv_write", &cb::rope_kv_write);

@@ -108,3 +108,31 @@ def test_api_over_llm_engine():
             body = b"".join(resp.iter_bytes()).decode()
         assert body.rstrip().endswith("data: [DONE]")
     r.close()
+
+
+def test_sliding_window_generation_frees_old_blocks():
+    """A window model decodes past its window: CPU attention sees only the
+    window (+ sinks) and blocks wholly before it return to the pool."""
+    import dataclasses
+
+    cfg = dataclasses.replace(get_config("tiny-llama"), sliding_window=32, attention_sinks=4)
+    m = LlamaModel(cfg, "cpu").init_random(seed=3, gen_device="cpu")
+    m.allocate_kv(64)
+    gen = BatchGenerator(m, use_graph=False)
+    prompt = list(range(3, 60))
+    ids = ["w"]
+    gen.prefill(ids, [prompt])
+    held = [b for b in m.kv.seqs["w"].blocks if b >= 0]
+    assert all(b >= 0 for b in m.kv.seqs["w"].blocks)  # the prompt's queries need them all
+    last = [5]
+    for _ in range(20):
+        last = [int(t) for t in gen.decode(ids, last, 8)]
+    s = m.kv.seqs["w"]
+    assert s.length == 57 + 20
+    # At position 76 the window starts at 45: block 1 (16..31) went back to
+    # the pool, the sink block 0 stays.
+    assert s.blocks[0] >= 0 and s.blocks[1] < 0
+    assert sum(b >= 0 for b in s.blocks) <= 4  # sink block + 3 window blocks
+    assert len(held) >= sum(b >= 0 for b in s.blocks)
+    m.kv.free_sequence("w")
+    assert m.kv.allocator.num_free == m.kv.num_blocks

@@ -334,3 +334,50 @@ def test_spec_verify():
     for b in range(3):
         r = ref.spec_verify(target[b].tolist(), draft[b].tolist())
         assert o[b, :len(r)].tolist() == r
+
+
+@pytest.mark.parametrize("d", [128, 256])
+@pytest.mark.parametrize("window,sinks", [(40, 0), (70, 4), (16, 20)])
+def test_attn_sliding_window_decode_and_prefill(d, window, sinks):
+    g = torch.Generator().manual_seed(window + sinks + d)
+    hq, hkv = 8, 2
+    seq_lens = [1, 30, 100, 257]
+    layers, layer = 1, 0
+    kc, vc, table, dense = _make_cache(seq_lens, hkv, d, layers, layer, g)
+    bs = len(seq_lens)
+    scale = 1.0 / math.sqrt(d)
+    q = torch.randn(bs, hq * d, generator=g).to(torch.bfloat16)
+    maxb = table.shape[1]
+    for splits in (1, 3):
+        bps = max(1, math.ceil(maxb / splits))
+        sp = max(1, math.ceil(maxb / bps))
+        part_o = torch.empty(bs * hkv * sp * (hq // hkv) * d, dtype=torch.float32, device=DEV)
+        part_ml = torch.empty(bs * hkv * sp * (hq // hkv) * 2, dtype=torch.float32, device=DEV)
+        out = torch.empty(bs, hq * d, dtype=torch.bfloat16, device=DEV)
+        ops.attn_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), table.to(DEV),
+                        torch.tensor(seq_lens, dtype=torch.int32, device=DEV), out, layer, sp, bps,
+                        part_o, part_ml, scale, window=window, sinks=sinks)
+        torch.cuda.synchronize()
+        _status_ok()
+        for b in range(bs):
+            k, v = dense[b]
+            e = ref.attention(q[b].view(1, hq, d), k, v, torch.tensor([seq_lens[b] - 1]), scale,
+                              window, sinks)
+            _close(out[b].view(hq, d), e[0], rtol=2e-2, atol=2e-2)
+    # Prefill: whole prompts and a chunk with a cached prefix.
+    qlen = [1, 30, 60, 200]
+    t = sum(qlen)
+    qp = torch.randn(t, hq * d, generator=g).to(torch.bfloat16)
+    tiles = ops.prefill_tiles(qlen, seq_lens, DEV)
+    out = torch.zeros(t, hq * d, dtype=torch.bfloat16, device=DEV)
+    ops.attn_prefill(qp.to(DEV), kc.to(DEV), vc.to(DEV), table.to(DEV), tiles, out, layer, scale,
+                     window=window, sinks=sinks)
+    torch.cuda.synchronize()
+    _status_ok()
+    row = 0
+    for b in range(bs):
+        k, v = dense[b]
+        pos = torch.arange(seq_lens[b] - qlen[b], seq_lens[b])
+        e = ref.attention(qp[row:row + qlen[b]].view(-1, hq, d), k, v, pos, scale, window, sinks)
+        _close(out[row:row + qlen[b]].view(-1, hq, d), e, rtol=2e-2, atol=2e-2)
+        row += qlen[b]
