@@ -426,6 +426,10 @@ class LLMBuilder(Builder):
     def model_class(self, cfg):
         """Dense Llama-family model, or the sparse-MoE model for MoE configs
         (hybrid Gated-DeltaNet MoE, MLA MoE, plain MoE)."""
+        if cfg.is_gemma4:
+            from ..models.gemma4 import Gemma4Model
+
+            return Gemma4Model
         if cfg.is_hybrid:
             from ..models.qwen36 import HybridMoEModel
 

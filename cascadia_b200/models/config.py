@@ -58,6 +58,19 @@ class ModelConfig:
     index_head_dim: int = 128
     indexer_types: Optional[tuple] = None  # per layer "full" | "shared" (None: all full)
     mla_rope_interleaved: bool = True  # False: checkpoint rotates split halves (NeoX)
+    # --- Gemma-4 (per-layer attention types, PLE, shared KV) ---
+    layer_types: Optional[tuple] = None   # per layer "sliding_attention" | "full_attention"
+    local_window: int = 0                 # window of the sliding layers
+    global_head_dim: int = 0
+    num_global_kv_heads: int = 0
+    attention_k_eq_v: bool = False
+    num_kv_shared_layers: int = 0
+    use_double_wide_mlp: bool = False
+    hidden_size_per_layer_input: int = 0
+    vocab_size_per_layer_input: int = 0
+    final_logit_softcapping: float = 0.0
+    rope_theta_local: float = 10000.0
+    global_partial_rotary: float = 1.0
     # --- hybrid linear attention (Qwen3.5 / Qwen3.6: Gated DeltaNet layers,
     # every full_attention_interval-th layer full attention) ---
     full_attention_interval: int = 0   # 0: no linear-attention layers
@@ -69,6 +82,10 @@ class ModelConfig:
     attn_output_gate: bool = False     # full attention output * sigmoid(gate)
     shared_expert_gate: bool = False   # shared expert output * sigmoid(w . x)
     shared_expert_intermediate_size: int = 0
+
+    @property
+    def is_gemma4(self) -> bool:
+        return self.arch == "gemma4"
 
     @property
     def is_dsa(self) -> bool:
@@ -171,6 +188,25 @@ class ModelConfig:
             types = d.get("mlp_layer_types")
             c.first_k_dense_replace = types.index("sparse") if types and "sparse" in types else \
                 int(d.get("first_k_dense_replace", 3))
+        if mt.startswith("gemma4"):
+            rp = d.get("rope_parameters") or {}
+            c.arch = "gemma4"
+            c.layer_types = tuple(d["layer_types"])
+            c.local_window = int(d.get("sliding_window", 512))
+            c.global_head_dim = int(d.get("global_head_dim") or c.head_dim)
+            c.num_global_kv_heads = int(d.get("num_global_key_value_heads") or c.num_kv_heads)
+            c.attention_k_eq_v = bool(d.get("attention_k_eq_v", False))
+            c.num_kv_shared_layers = int(d.get("num_kv_shared_layers", 0))
+            c.use_double_wide_mlp = bool(d.get("use_double_wide_mlp", False))
+            c.hidden_size_per_layer_input = int(d.get("hidden_size_per_layer_input") or 0)
+            c.vocab_size_per_layer_input = int(d.get("vocab_size_per_layer_input") or 0)
+            c.final_logit_softcapping = float(d.get("final_logit_softcapping") or 0.0)
+            c.rope_theta_local = float(rp.get("sliding_attention", {}).get("rope_theta", 10000.0))
+            fa = rp.get("full_attention", {})
+            c.rope_theta = float(fa.get("rope_theta", 1e6))
+            c.global_partial_rotary = float(fa.get("partial_rotary_factor", 1.0))
+            c.rope_scaling = None
+            c.tie_word_embeddings = bool(d.get("tie_word_embeddings", True))
         if mt.startswith("qwen3"):
             c.qk_norm = True
         if mt.startswith("qwen3_5") or mt.startswith("qwen3_next"):
@@ -278,6 +314,21 @@ PRESETS = {
                                           "mscale_all_dim": 1.0,
                                           "original_max_position_embeddings": 4096},
                             eos_token_ids=(1,)),
+    # Gemma-4 layer structure at small width: sliding (head_dim 256, window
+    # 16) and full (head_dim 512, K = V, one KV head) layers, 2 shared-KV
+    # layers with double-wide MLPs, per-layer inputs, soft-capped logits.
+    "tiny-gemma4": ModelConfig(arch="gemma4", vocab_size=512, hidden_size=256, num_layers=6,
+                               num_heads=4, num_kv_heads=2, head_dim=256, intermediate_size=512,
+                               rms_eps=1e-6, tie_word_embeddings=True,
+                               layer_types=("sliding_attention", "sliding_attention",
+                                            "full_attention", "sliding_attention",
+                                            "sliding_attention", "full_attention"),
+                               local_window=16, global_head_dim=512, num_global_kv_heads=1,
+                               attention_k_eq_v=True, num_kv_shared_layers=2,
+                               use_double_wide_mlp=True, hidden_size_per_layer_input=128,
+                               vocab_size_per_layer_input=512, final_logit_softcapping=30.0,
+                               rope_theta=1000000.0, rope_theta_local=10000.0,
+                               global_partial_rotary=0.25, eos_token_ids=(1,)),
     # GLM-5 layer structure at small width: MLA (latent 512, rope 64; nope
     # 192 / v 256 as in GLM-5), DSA indexer with top-8 (so selection matters
     # at test lengths), IndexShare on layer 2, 1 dense + 2 MoE layers.

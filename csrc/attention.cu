@@ -70,14 +70,20 @@ __device__ __forceinline__ VisibleBlocks visible_blocks(int first_visible, int t
   return vb;
 }
 
-template <int D>
+// D: head dim (q.k and the cache rows).  DV: output dims one CTA produces;
+// DV < D splits the output of a head over D / DV CTAs (head_dim 512: two
+// CTAs each compute all scores and half of the output), blockIdx.z =
+// split * (D / DV) + half.
+template <int D, int DV = D>
 __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant__ CUtensorMap tk,
                                                           const __grid_constant__ CUtensorMap tv,
                                                           const DecodeArgs a) {
-  constexpr int KV_BYTES = 16 * D * 2;  // one block of K (or V)
-  constexpr int STAGE = 2 * KV_BYTES;
+  constexpr int KV_BYTES = 16 * D * 2;   // one block of K
+  constexpr int V_BYTES = 16 * DV * 2;   // this CTA's slice of one block of V
+  constexpr int STAGE = KV_BYTES + V_BYTES;
   constexpr int NKS = D / 16;
-  // head_dim 256: Q fragments come from shared memory per k-step (the
+  constexpr int HALVES = D / DV;
+  // head_dim >= 256: Q fragments come from shared memory per k-step (the
   // output accumulators alone take 128 registers).
   constexpr bool QS = D > 128;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -87,7 +93,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
   const int lane = threadIdx.x & 31;
   const int h = blockIdx.x;
   const int b = blockIdx.y;
-  const int sp = blockIdx.z;
+  const int sp = blockIdx.z / HALVES;
+  const int half = blockIdx.z % HALVES;
   uint8_t* wbuf = smem + warp * 2 * STAGE;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 4 * 2 * STAGE);
   uint64_t* full = bars + warp * 2;
@@ -122,10 +129,10 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     uint8_t* kb = wbuf + st * STAGE;
     mbar_arrive_expect_tx(&full[st], STAGE);
 #pragma unroll
-    for (int bx = 0; bx < D / 64; ++bx) {
-      tma_load_2d(kb + bx * 16 * 128, &tk, bx * 64, row, &full[st]);
-      tma_load_2d(kb + KV_BYTES + bx * 16 * 128, &tv, bx * 64, row, &full[st]);
-    }
+    for (int bx = 0; bx < D / 64; ++bx) tma_load_2d(kb + bx * 16 * 128, &tk, bx * 64, row, &full[st]);
+#pragma unroll
+    for (int bx = 0; bx < DV / 64; ++bx)
+      tma_load_2d(kb + KV_BYTES + bx * 16 * 128, &tv, half * DV + bx * 64, row, &full[st]);
   };
   if (lane == 0) {
     if (my_n > 0) issue(0, 0);
@@ -159,9 +166,9 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     }
   }
 
-  float o[D / 8][4];
+  float o[DV / 8][4];
 #pragma unroll
-  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  for (int i = 0; i < DV / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m[2] = {kNegBig, kNegBig};
   float l[2] = {0.f, 0.f};
   bool ok = true;
@@ -232,7 +239,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
       l[r] = l[r] * alpha + sum;
       m[r] = m_new;
 #pragma unroll
-      for (int nt = 0; nt < D / 8; ++nt) {
+      for (int nt = 0; nt < DV / 8; ++nt) {
         o[nt][2 * r] *= alpha;
         o[nt][2 * r + 1] *= alpha;
       }
@@ -243,7 +250,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     pa[2] = pack_bf16(p[1][0], p[1][1]);
     pa[3] = pack_bf16(p[1][2], p[1][3]);
 #pragma unroll
-    for (int np = 0; np < D / 16; ++np) {
+    for (int np = 0; np < DV / 16; ++np) {
       const int mi = lane >> 3;
       const int row = ((mi & 1) << 3) + (lane & 7);
       const int chunk = 2 * np + (mi >> 1);
@@ -270,15 +277,15 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
   }
   __syncthreads();
   // Cross-warp merge through shared memory (reuse the stage buffers).
-  float* sm_o = reinterpret_cast<float*>(smem);          // [4][16][D]
-  float* sm_ml = sm_o + 4 * 16 * D;                      // [4][16][2]
+  float* sm_o = reinterpret_cast<float*>(smem);          // [4][16][DV]
+  float* sm_ml = sm_o + 4 * 16 * DV;                     // [4][16][2]
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int row = g + 8 * r;
 #pragma unroll
-    for (int nt = 0; nt < D / 8; ++nt) {
-      sm_o[(warp * 16 + row) * D + nt * 8 + 2 * t4] = o[nt][2 * r];
-      sm_o[(warp * 16 + row) * D + nt * 8 + 2 * t4 + 1] = o[nt][2 * r + 1];
+    for (int nt = 0; nt < DV / 8; ++nt) {
+      sm_o[(warp * 16 + row) * DV + nt * 8 + 2 * t4] = o[nt][2 * r];
+      sm_o[(warp * 16 + row) * DV + nt * 8 + 2 * t4 + 1] = o[nt][2 * r + 1];
     }
     if (t4 == 0) {
       sm_ml[(warp * 16 + row) * 2] = m[r];
@@ -286,9 +293,9 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     }
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < a.G * D; idx += 128) {
-    const int gg = idx / D;
-    const int d = idx % D;
+  for (int idx = threadIdx.x; idx < a.G * DV; idx += 128) {
+    const int gg = idx / DV;
+    const int d = idx % DV;
     float M = kNegBig;
 #pragma unroll
     for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_ml[(w * 16 + gg) * 2]);
@@ -297,14 +304,15 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     for (int w = 0; w < 4; ++w) {
       const float wt = exp2f(sm_ml[(w * 16 + gg) * 2] - M);
       L += sm_ml[(w * 16 + gg) * 2 + 1] * wt;
-      O += sm_o[(w * 16 + gg) * D + d] * wt;
+      O += sm_o[(w * 16 + gg) * DV + d] * wt;
     }
     if (a.splits == 1) {
       const float y = L > 0.f ? O / L : 0.f;
-      a.out[(size_t)b * a.out_stride + (size_t)(h * a.G + gg) * D + d] = __float2bfloat16(y);
+      a.out[(size_t)b * a.out_stride + (size_t)(h * a.G + gg) * D + half * DV + d] =
+          __float2bfloat16(y);
     } else {
       const size_t base = (((size_t)b * a.Hkv + h) * a.splits + sp) * a.G + gg;
-      a.part_o[base * D + d] = O;
+      a.part_o[base * D + half * DV + d] = O;
       if (d == 0) {
         a.part_ml[base * 2] = M;
         a.part_ml[base * 2 + 1] = L;
@@ -667,6 +675,22 @@ void attn_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
       launch_kernel(attn_decode_combine_kernel<256>, dim3(B, Hq), dim3(256), 0, stream, a.part_o,
                     a.part_ml, a.out, a.out_stride, Hkv, a.G, (int)num_splits);
     }
+  } else if (D == 512) {
+    // Two CTAs per head (256 output dims each): stages hold a whole K block
+    // and half a V block; + barriers + the [16][512] Q tile + slack.
+    constexpr int smem = 4 * 2 * (16 * 512 * 2 + 16 * 256 * 2) + 128 + 16 * 512 * 2 + 1024;
+    static bool cfg = false;
+    if (!cfg) {
+      CB_CUDA_CHECK(cudaFuncSetAttribute(attn_decode_kernel<512, 256>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      cfg = true;
+    }
+    const dim3 grid2(Hkv, B, (unsigned)num_splits * 2);
+    launch_kernel(attn_decode_kernel<512, 256>, grid2, dim3(128), smem, stream, tk, tv, a);
+    if (num_splits > 1) {
+      launch_kernel(attn_decode_combine_kernel<512>, dim3(B, Hq), dim3(512), 0, stream, a.part_o,
+                    a.part_ml, a.out, a.out_stride, Hkv, a.G, (int)num_splits);
+    }
   } else if (D == 64) {
     constexpr int smem = 4 * 2 * 2 * 16 * 64 * 2 + 1024 + 128;
     // The merge buffer needs 4*16*64*4 + 4*16*2*4 bytes, which fits in smem.
@@ -682,7 +706,7 @@ void attn_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                     a.part_ml, a.out, a.out_stride, Hkv, a.G, (int)num_splits);
     }
   } else {
-    TORCH_CHECK(false, "head_dim must be 64, 128 or 256");
+    TORCH_CHECK(false, "head_dim must be 64, 128, 256 or 512");
   }
   CB_CUDA_CHECK(cudaGetLastError());
 }

@@ -255,7 +255,8 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos
 
 // ------------------------------------------------------------------ q/k norm
 // Per-head RMSNorm of the q and k heads of a fused qkv row, in place (Qwen3's
-// q_norm / k_norm, applied before RoPE).  One warp per head; D <= 256.
+// q_norm / k_norm, applied before RoPE).  One warp per head; D <= 1024 (each
+// lane holds up to four 8-element chunks).
 __global__ void head_rmsnorm_kernel(bf16* __restrict__ qkv, int ldq, const bf16* __restrict__ qw,
                                     const bf16* __restrict__ kw, int Hq, int Hkv, int D,
                                     float eps) {
@@ -267,23 +268,29 @@ __global__ void head_rmsnorm_kernel(bf16* __restrict__ qkv, int ldq, const bf16*
   for (int hh = warp; hh < Hq + Hkv; hh += nw) {
     bf16* hp = qkv + (size_t)t * ldq + (size_t)hh * D;
     const bf16* w = hh < Hq ? qw : kw;
-    float v[8];
-    const int d0 = lane * 8;
-    const bool act = d0 < D;
+    float v[4][8];
     float ss = 0.f;
-    if (act) {
-      load8(hp + d0, v);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) ss += v[k] * v[k];
+    for (int c = 0; c < 4; ++c) {
+      const int d0 = c * 256 + lane * 8;
+      if (d0 < D) {
+        load8(hp + d0, v[c]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss += v[c][k] * v[c][k];
+      }
     }
     ss = warp_sum(ss);
     const float inv = rsqrtf(ss / (float)D + eps);
-    if (act) {
-      float wv[8];
-      load8(w + d0, wv);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = v[k] * inv * wv[k];
-      store8(hp + d0, v);
+    for (int c = 0; c < 4; ++c) {
+      const int d0 = c * 256 + lane * 8;
+      if (d0 < D) {
+        float wv[8];
+        load8(w + d0, wv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[c][k] = v[c][k] * inv * wv[k];
+        store8(hp + d0, v[c]);
+      }
     }
   }
 }
@@ -293,7 +300,7 @@ void head_rmsnorm(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, int64
   const int T = (int)qkv.size(0);
   if (T == 0) return;
   TORCH_CHECK(qkv.stride(1) == 1 && (qkv.stride(0) * 2) % 16 == 0, "qkv rows must be aligned");
-  TORCH_CHECK(D % 8 == 0 && D <= 256, "head_rmsnorm: D must be a multiple of 8, <= 256");
+  TORCH_CHECK(D % 8 == 0 && D <= 1024, "head_rmsnorm: D must be a multiple of 8, <= 1024");
   const c10::cuda::CUDAGuard guard(qkv.device());
   launch_kernel(head_rmsnorm_kernel, dim3(T), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
                 reinterpret_cast<bf16*>(qkv.data_ptr()), (int)qkv.stride(0),

@@ -209,7 +209,7 @@ def _make_cache(seq_lens, hkv, d, layers, layer, g, nb_extra=3):
 
 
 @pytest.mark.parametrize("d,hq,hkv", [(128, 32, 8), (64, 32, 8), (128, 16, 1), (256, 16, 2),
-                                      (256, 4, 2)])
+                                      (256, 4, 2), (512, 8, 2), (512, 16, 1)])
 @pytest.mark.parametrize("splits", [1, 3])
 def test_attn_decode(d, hq, hkv, splits):
     g = torch.Generator().manual_seed(d + hq + splits)
