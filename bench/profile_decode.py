@@ -40,14 +40,17 @@ def main():
         cfg.num_layers = a.layers
     dev = torch.device("cuda", 0)
     t0 = time.time()
-    if cfg.is_moe:
-        from cascadia_b200.models.moe import MoEModel
+    if cfg.is_moe or cfg.is_gemma4:
+        from cascadia_b200.engine.llm import LLMBuilder
 
-        m = MoEModel(cfg, dev).init_random(seed=1)
+        m = LLMBuilder.model_class(None, cfg)(cfg, dev).init_random(seed=1)
     else:
         m = LlamaModel(cfg, dev).init_random(seed=1)
     width = -(-(a.prompt_len + a.steps + 8) // BLOCK_SIZE)
-    m.allocate_kv(a.batch * width + 8)
+    if cfg.is_hybrid:
+        m.allocate_kv(a.batch * width + 8, max_seqs=a.batch)
+    else:
+        m.allocate_kv(a.batch * width + 8)
     gen = BatchGenerator(m, use_graph=False)
     g = torch.Generator().manual_seed(0)
     prompts = torch.randint(0, cfg.vocab_size, (a.batch, a.prompt_len), generator=g).tolist()
