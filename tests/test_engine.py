@@ -136,3 +136,18 @@ def test_sliding_window_generation_frees_old_blocks():
     assert len(held) >= sum(b >= 0 for b in s.blocks)
     m.kv.free_sequence("w")
     assert m.kv.allocator.num_free == m.kv.num_blocks
+
+
+@pytest.mark.parametrize("preset", ["tiny-glm5", "tiny-gemma4", "tiny-mla", "tiny-moe"])
+def test_builder_serves_every_model_family(preset):
+    """The builder picks the model class from the config and the engine
+    serves a request end to end (CPU oracle path)."""
+    from cascadia_b200.types import GenerationTask
+
+    b = LLMBuilder(preset, device="cpu", kv_blocks=128, max_model_len=256, max_running=4)
+    n = get_config(preset).num_layers
+    for _ in b.load(ShardSpec(preset, 0, n, n, device="cpu")):
+        pass
+    e = b.build()
+    out = _run(e, [GenerationTask("t", "", max_tokens=3, prompt_ids=list(range(3, 23)))])
+    assert out["t"][-1].is_final and len(_ids(out["t"])) == 3
