@@ -207,18 +207,25 @@ class MoEModel(LlamaModel):
             x = part.float().view(T, nh, d)
             part.copy_(ref.rmsnorm(x, w, self.cfg.rms_eps).to(torch.bfloat16).view(T, nh * d))
 
-    def _shared_expert(self, lw: MoELayer, h: torch.Tensor) -> Optional[torch.Tensor]:
-        """Output of the layer's shared expert(s), or None."""
+    def _shared_expert(self, lw: MoELayer, h: torch.Tensor):
+        """(output of the layer's shared expert(s) or None, fp32 gate logits
+        [T] or None); the combine adds sigmoid(gate) * output."""
         if lw.shared is None:
-            return None
-        return lw.shared[1](lw.shared[0](h, ops.EPI_SILU))
+            return None, None
+        return lw.shared[1](lw.shared[0](h, ops.EPI_SILU)), None
+
+    @staticmethod
+    def _gated(shared_out, gate):
+        if shared_out is None or gate is None:
+            return shared_out
+        return (shared_out.float() * torch.sigmoid(gate.float()).view(-1, 1)).to(torch.bfloat16)
 
     def _moe(self, lw: MoELayer, h: torch.Tensor, hidden: torch.Tensor):
         cfg = self.cfg
         k = cfg.num_experts_per_tok
         scoring = 0 if cfg.router == "softmax" else 1
         bank = lw.experts
-        shared_out = self._shared_expert(lw, h)
+        shared_out, shared_gate = self._shared_expert(lw, h)
         if self.ep is not None:
             if self.device.type == "cuda":
                 ids, w = ops.moe_topk_gate(h, lw.router, k, scoring, cfg.norm_topk_prob,
@@ -226,8 +233,8 @@ class MoEModel(LlamaModel):
             else:
                 ids, w = ref_topk_gate(h, lw.router, lw.router_bias, k, scoring,
                                        cfg.norm_topk_prob, cfg.routed_scaling_factor)
-            add = hidden if shared_out is None else (hidden.float() + shared_out.float()).to(
-                torch.bfloat16)
+            so = self._gated(shared_out, shared_gate)
+            add = hidden if so is None else (hidden.float() + so.float()).to(torch.bfloat16)
             self.ep.moe(bank, h, ids, w.float(), add, hidden)
             return
         if self.device.type == "cuda":
@@ -251,9 +258,8 @@ class MoEModel(LlamaModel):
                                              ops.EPI_SILU, offsets, bank.E, T)
                 y = ops.w4a16_gemm_grouped(act, bank.dn_blob, bank.hidden, bank.gs,
                                            ops.EPI_STORE, offsets, bank.E, T)
-            add = hidden if shared_out is None else (hidden.float() + shared_out.float()).to(
-                torch.bfloat16)
-            ops.moe_combine(y, inv, w, add=add, out=hidden)
+            ops.moe_combine(y, inv, w, add=hidden, out=hidden, shared=shared_out,
+                            shared_gate=shared_gate)
             return
         # CPU oracle.
         ids, w = ref_topk_gate(h, lw.router, lw.router_bias, k, scoring, cfg.norm_topk_prob,
@@ -266,8 +272,9 @@ class MoEModel(LlamaModel):
                 a = ref.silu_mul(gu[:, :bank.inter], gu[:, bank.inter:]).to(torch.bfloat16)
                 y = (a.float() @ bank.dn_ref[e].t()).to(torch.bfloat16)
                 out[t] += float(w[t, j]) * y[0].float()
-        if shared_out is not None:
-            out += shared_out.float()
+        so = self._gated(shared_out, shared_gate)
+        if so is not None:
+            out += so.float()
         hidden.copy_((hidden.float() + out).to(torch.bfloat16))
 
 

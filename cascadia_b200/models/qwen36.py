@@ -285,14 +285,16 @@ class HybridMoEModel(MoEModel):
         return hidden
 
     def _shared_expert(self, lw, h):
-        out = super()._shared_expert(lw, h)
+        """Shared expert output and its gate logits w . x (the sigmoid is
+        applied by the combine)."""
+        out, _ = super()._shared_expert(lw, h)
         if out is None or lw.shared_gate is None:
-            return out
+            return out, None
         if self.device.type == "cuda":
-            s = torch.sigmoid(torch.matmul(h, lw.shared_gate.t()).float())
+            g = torch.matmul(h, lw.shared_gate.t()).float().view(-1)
         else:
-            s = torch.sigmoid(h.float() @ lw.shared_gate.float().t())
-        return (out.float() * s).to(torch.bfloat16)
+            g = (h.float() @ lw.shared_gate.float().t()).view(-1)
+        return out, g
 
     def _linear_attention(self, si: int, lin: LinearAttn, h: torch.Tensor, hidden: torch.Tensor,
                           batch: Batch):

@@ -385,10 +385,12 @@ def w4a16_gemv_grouped(x16, xs, blob, n: int, epilogue: int, offsets, num_groups
     return out
 
 
-def moe_combine(y, inv, w, add=None, out=None):
+def moe_combine(y, inv, w, add=None, out=None, shared=None, shared_gate=None):
+    """out[t] = add[t] + sum_j w[t, j] y[inv[t, j]] + g_t * shared[t], with
+    g_t = sigmoid(shared_gate[t]) when a gate is given (else 1)."""
     T = w.shape[0]
     if out is None:
         out = torch.empty(T, y.shape[1], dtype=torch.bfloat16, device=y.device)
-    ext().moe_combine(y, inv, w, add, out)
+    ext().moe_combine(y, inv, w, add, out, shared, shared_gate)
     LAUNCHES.add(1)
     return out

@@ -86,7 +86,8 @@ void moe_permute(torch::Tensor topk_ids, int64_t E, torch::Tensor offsets, torch
                  torch::Tensor inv, c10::optional<torch::Tensor> x,
                  c10::optional<torch::Tensor> xp);
 void moe_combine(torch::Tensor y, torch::Tensor inv, torch::Tensor w,
-                 c10::optional<torch::Tensor> add, torch::Tensor out);
+                 c10::optional<torch::Tensor> add, torch::Tensor out,
+                 c10::optional<torch::Tensor> shared, c10::optional<torch::Tensor> shared_gate);
 // attention.cu
 void attn_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                  torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
@@ -148,7 +149,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("w4a16_gemm_grouped", &cb::w4a16_gemm_grouped);
   m.def("moe_topk_gate", &cb::moe_topk_gate);
   m.def("moe_permute", &cb::moe_permute);
-  m.def("moe_combine", &cb::moe_combine);
+  m.def("moe_combine", &cb::moe_combine, py::arg("y"), py::arg("inv"), py::arg("w"),
+        py::arg("add"), py::arg("out"), py::arg("shared") = py::none(),
+        py::arg("shared_gate") = py::none());
   m.def("ep_dispatch", &cb::ep_dispatch);
   m.def("mla_rope_write", &cb::mla_rope_write);
   m.def("mla_decode", &cb::mla_decode, py::arg("q"), py::arg("cache"), py::arg("block_tables"),

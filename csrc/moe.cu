@@ -54,19 +54,34 @@ __global__ void __launch_bounds__(kGateThreads) moe_topk_gate_kernel(
   // 1. logits of this CTA's experts.
   const int e0 = blockIdx.y * kGateExpertsPerCta;
   const int e1 = min(E, e0 + kGateExpertsPerCta);
-  for (int e = e0 + warp; e < e1; e += nw) {
-    const bf16* wr = wg + (size_t)e * H;
-    float acc = 0.f;
-    for (int i = lane * 8; i < H; i += 32 * 8) {
-      const uint4 xu = *reinterpret_cast<const uint4*>(xr + i);
-      const uint4 wu = *reinterpret_cast<const uint4*>(wr + i);
-      const bf16* xv = reinterpret_cast<const bf16*>(&xu);
-      const bf16* wv = reinterpret_cast<const bf16*>(&wu);
+  // Each warp computes kGatePerWarp experts side by side: one load of x
+  // per step serves all of them and their weight loads are independent.
+  constexpr int kGatePerWarp = kGateExpertsPerCta / (kGateThreads / 32);
+  const int ew0 = e0 + warp * kGatePerWarp;
+  float acc[kGatePerWarp];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) acc += __bfloat162float(xv[q]) * __bfloat162float(wv[q]);
+  for (int j = 0; j < kGatePerWarp; ++j) acc[j] = 0.f;
+#pragma unroll 2
+  for (int i = lane * 8; i < H; i += 32 * 8) {
+    const uint4 xu = *reinterpret_cast<const uint4*>(xr + i);
+    const bf16* xv = reinterpret_cast<const bf16*>(&xu);
+    float xf[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) xf[q] = __bfloat162float(xv[q]);
+#pragma unroll
+    for (int j = 0; j < kGatePerWarp; ++j) {
+      if (ew0 + j < e1) {
+        const uint4 wu = *reinterpret_cast<const uint4*>(wg + (size_t)(ew0 + j) * H + i);
+        const bf16* wv = reinterpret_cast<const bf16*>(&wu);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[j] += xf[q] * __bfloat162float(wv[q]);
+      }
     }
-    acc = warp_sum(acc);
-    if (lane == 0) logits[(size_t)t * E + e] = acc;
+  }
+#pragma unroll
+  for (int j = 0; j < kGatePerWarp; ++j) {
+    const float v = warp_sum(acc[j]);
+    if (lane == 0 && ew0 + j < e1) logits[(size_t)t * E + ew0 + j] = v;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -273,11 +288,18 @@ void moe_permute(torch::Tensor topk_ids, int64_t E, torch::Tensor offsets, torch
 
 // ------------------------------------------------------------------ combine
 // out[t] = sum_j w[t, j] * y[inv[t*k + j]] (+ add[t]), fp32 accumulation.
+// out[t] = add[t] + sum_j w[t, j] * y[inv[t, j]]
+//          (+ shared[t], scaled by sigmoid(shared_gate[t]) when given)
 __global__ void moe_combine_kernel(const bf16* __restrict__ y, const int* __restrict__ inv,
                                    const float* __restrict__ w, int k, int H,
                                    const bf16* __restrict__ add, int ld_add,
+                                   const bf16* __restrict__ shared, int ld_shared,
+                                   const float* __restrict__ shared_gate,
                                    bf16* __restrict__ out, int ldo) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int t = blockIdx.x;
+  const float sg = shared_gate != nullptr ? 1.f / (1.f + __expf(-shared_gate[t])) : 1.f;
   for (int i = threadIdx.x; i < H / 8; i += blockDim.x) {
     float acc[8];
 #pragma unroll
@@ -289,6 +311,12 @@ __global__ void moe_combine_kernel(const bf16* __restrict__ y, const int* __rest
       const bf16* v = reinterpret_cast<const bf16*>(&u);
 #pragma unroll
       for (int q = 0; q < 8; ++q) acc[q] += wt * __bfloat162float(v[q]);
+    }
+    if (shared != nullptr) {
+      const uint4 u = *reinterpret_cast<const uint4*>(shared + (size_t)t * ld_shared + i * 8);
+      const bf16* v = reinterpret_cast<const bf16*>(&u);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] += sg * __bfloat162float(v[q]);
     }
     if (add != nullptr) {
       const uint4 u = *reinterpret_cast<const uint4*>(add + (size_t)t * ld_add + i * 8);
@@ -305,18 +333,28 @@ __global__ void moe_combine_kernel(const bf16* __restrict__ y, const int* __rest
 }
 
 void moe_combine(torch::Tensor y, torch::Tensor inv, torch::Tensor w, c10::optional<torch::Tensor> add,
-                 torch::Tensor out) {
+                 torch::Tensor out, c10::optional<torch::Tensor> shared,
+                 c10::optional<torch::Tensor> shared_gate) {
   const int T = (int)w.size(0);
   const int k = (int)w.size(1);
   const int H = (int)y.size(1);
+  TORCH_CHECK(H % 8 == 0 && y.is_contiguous(), "y must be contiguous [rows, H], H % 8 == 0");
+  TORCH_CHECK(!shared.has_value() || (shared->stride(1) == 1 && shared->size(0) >= T),
+              "shared: [T, H] rows");
+  TORCH_CHECK(!shared_gate.has_value() || (shared_gate->scalar_type() == at::kFloat &&
+                                           shared_gate->numel() >= T),
+              "shared_gate: fp32 [T]");
   if (T == 0) return;
   const c10::cuda::CUDAGuard guard(y.device());
-  moe_combine_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const bf16*>(y.data_ptr()), inv.data_ptr<int>(), w.data_ptr<float>(), k, H,
-      add.has_value() ? reinterpret_cast<const bf16*>(add->data_ptr()) : nullptr,
-      add.has_value() ? (int)add->stride(0) : 0, reinterpret_cast<bf16*>(out.data_ptr()),
-      (int)out.stride(0));
-  CB_CUDA_CHECK(cudaGetLastError());
+  launch_kernel(moe_combine_kernel, dim3(T), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+                reinterpret_cast<const bf16*>(y.data_ptr()), (const int*)inv.data_ptr<int>(),
+                (const float*)w.data_ptr<float>(), k, H,
+                add.has_value() ? reinterpret_cast<const bf16*>(add->data_ptr()) : (const bf16*)nullptr,
+                add.has_value() ? (int)add->stride(0) : 0,
+                shared.has_value() ? reinterpret_cast<const bf16*>(shared->data_ptr()) : (const bf16*)nullptr,
+                shared.has_value() ? (int)shared->stride(0) : 0,
+                shared_gate.has_value() ? (const float*)shared_gate->data_ptr<float>() : (const float*)nullptr,
+                reinterpret_cast<bf16*>(out.data_ptr()), (int)out.stride(0));
 }
 
 }  // namespace cb
