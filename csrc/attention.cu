@@ -74,7 +74,8 @@ __device__ __forceinline__ VisibleBlocks visible_blocks(int first_visible, int t
 // DV < D splits the output of a head over D / DV CTAs (head_dim 512: two
 // CTAs each compute all scores and half of the output), blockIdx.z =
 // split * (D / DV) + half.
-template <int D, int DV = D>
+// WIN: a sliding window / sinks may hide positions (compiled out otherwise).
+template <int D, int DV = D, bool WIN = false>
 __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant__ CUtensorMap tk,
                                                           const __grid_constant__ CUtensorMap tv,
                                                           const DecodeArgs a) {
@@ -105,8 +106,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
   const int seq_len = a.seq_lens[b];
   // The query is at position seq_len - 1: with a window it sees positions
   // from seq_len - window on (and the sinks).
-  const VisibleBlocks vis =
-      visible_blocks(seq_len - a.window, (seq_len + 15) >> 4, a.window, a.sinks);
+  const VisibleBlocks vis = visible_blocks(seq_len - a.window, (seq_len + 15) >> 4,
+                                           WIN ? a.window : 0, a.sinks);
   const int nblocks = vis.n;
   const int blk0 = sp * a.blocks_per_split;
   const int blk1 = min(nblocks, blk0 + a.blocks_per_split);
@@ -123,7 +124,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
   const int* bt = a.block_tables + (size_t)b * a.bt_stride;
   const int row_base_layer = a.layer * a.NB;
   auto issue = [&](int i, int st) {
-    const int j = vis.block_of(blk0 + warp + 4 * i);
+    const int j = WIN ? vis.block_of(blk0 + warp + 4 * i) : blk0 + warp + 4 * i;
     const int phys = bt[j];
     const int row = ((row_base_layer + phys) * a.Hkv + h) * 16;
     uint8_t* kb = wbuf + st * STAGE;
@@ -203,7 +204,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
         mma_16816(s[1], qa[ks], b10, b11);
       }
     }
-    const int j = vis.block_of(blk0 + warp + 4 * i);
+    const int j = WIN ? vis.block_of(blk0 + warp + 4 * i) : blk0 + warp + 4 * i;
     const int pos0 = j * 16;
     float p[2][4];
 #pragma unroll
@@ -216,7 +217,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
           const int pos = pos0 + nt * 8 + 2 * t4 + e;
           float v = s[nt][2 * r + e] * a.scale_log2;
           const bool seen =
-              pos < seq_len && (a.window <= 0 || pos >= seq_len - a.window || pos < a.sinks);
+              pos < seq_len && (!WIN || pos >= seq_len - a.window || pos < a.sinks);
           v = seen ? v : -INFINITY;
           s[nt][2 * r + e] = v;
           mx = fmaxf(mx, v);
@@ -366,7 +367,7 @@ struct PrefillArgs {
 
 // One CTA = 64 query rows (4 warps x 16) of one query head.  K/V tiles of 64
 // tokens (4 paged blocks) stream through a 2-stage TMA ring.
-template <int D>
+template <int D, bool WIN = false>
 __global__ void __launch_bounds__(128) attn_prefill_kernel(const __grid_constant__ CUtensorMap tk,
                                                            const __grid_constant__ CUtensorMap tv,
                                                            const PrefillArgs a) {
@@ -395,11 +396,11 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __grid_constant
   // window, the first query pos0 sees from pos0 - window + 1 on).
   const int all_tiles = (kv_len + 63) / 64;
   int nst = all_tiles, wt0 = all_tiles;
-  if (a.window > 0) {
+  if (WIN && a.window > 0) {
     wt0 = min(all_tiles, max(0, pos0 - a.window + 1) / 64);
     nst = min((a.sinks + 63) / 64, wt0);
   }
-  const int ntiles = a.window > 0 ? nst + (all_tiles - wt0) : all_tiles;
+  const int ntiles = (WIN && a.window > 0) ? nst + (all_tiles - wt0) : all_tiles;
   auto tile_of = [&](int v) { return v < nst ? v : wt0 + (v - nst); };
   const int* bt = a.block_tables + (size_t)b * a.bt_stride;
 
@@ -516,7 +517,7 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const __grid_constant
             const int kp = kpos0 + nt * 8 + 2 * t4 + e;
             float v = s[nt][2 * r + e] * a.scale_log2;
             const bool seen = kp <= qpos[r] && kp < kv_len &&
-                              (a.window <= 0 || kp > qpos[r] - a.window || kp < a.sinks);
+                              (!WIN || kp > qpos[r] - a.window || kp < a.sinks);
             v = seen ? v : -INFINITY;
             s[nt][2 * r + e] = v;
             mx = fmaxf(mx, v);
@@ -602,6 +603,41 @@ static CUtensorMap kv_tmap(const torch::Tensor& cache) {
                            CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Stages (a K block + this CTA's slice of a V block per warp and stage) +
+// barriers + the Q tile for head dims above 128 + alignment slack.
+template <int D, int DV, bool WIN>
+static void launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeArgs& a,
+                          dim3 grid, int B, int Hq, cudaStream_t stream) {
+  constexpr int kStage = 16 * D * 2 + 16 * DV * 2;
+  constexpr int smem = 4 * 2 * kStage + 128 + (D > 128 ? 16 * D * 2 : 0) + 1024;
+  static bool cfg = false;
+  if (!cfg) {
+    CB_CUDA_CHECK(cudaFuncSetAttribute(attn_decode_kernel<D, DV, WIN>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    cfg = true;
+  }
+  const dim3 g(grid.x, grid.y, grid.z * (D / DV));
+  launch_kernel(attn_decode_kernel<D, DV, WIN>, g, dim3(128), smem, stream, tk, tv, a);
+  if (a.splits > 1) {
+    launch_kernel(attn_decode_combine_kernel<D>, dim3(B, Hq), dim3(D), 0, stream, a.part_o,
+                  a.part_ml, a.out, a.out_stride, a.Hkv, a.G, a.splits);
+  }
+}
+
+// Two K/V stages of 64 tokens + barriers + the Q tile above head_dim 128.
+template <int D, bool WIN>
+static void launch_prefill(const CUtensorMap& tk, const CUtensorMap& tv, const PrefillArgs& a,
+                           dim3 grid, cudaStream_t stream) {
+  constexpr int smem = 2 * 2 * 4 * 16 * D * 2 + 128 + (D > 128 ? 64 * D * 2 : 0) + 1024;
+  static bool cfg = false;
+  if (!cfg) {
+    CB_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<D, WIN>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    cfg = true;
+  }
+  launch_kernel(attn_prefill_kernel<D, WIN>, grid, dim3(128), smem, stream, tk, tv, a);
+}
+
 // q: [B, Hq*D] view (row stride arbitrary); out: [B, Hq*D].
 void attn_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                  torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor out,
@@ -647,64 +683,21 @@ void attn_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
   }
   CUtensorMap tk = kv_tmap(k_cache), tv = kv_tmap(v_cache);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  dim3 grid(Hkv, B, (unsigned)num_splits);
+  const dim3 grid(Hkv, B, (unsigned)num_splits);
+  const bool win = window > 0;
   if (D == 128) {
-    constexpr int smem = 4 * 2 * 2 * 16 * 128 * 2 + 1024 + 128;
-    static bool cfg = false;
-    if (!cfg) {
-      CB_CUDA_CHECK(cudaFuncSetAttribute(attn_decode_kernel<128>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      cfg = true;
-    }
-    launch_kernel(attn_decode_kernel<128>, grid, dim3(128), smem, stream, tk, tv, a);
-    if (num_splits > 1) {
-      launch_kernel(attn_decode_combine_kernel<128>, dim3(B, Hq), dim3(128), 0, stream, a.part_o,
-                    a.part_ml, a.out, a.out_stride, Hkv, a.G, (int)num_splits);
-    }
-  } else if (D == 256) {
-    // Stages + barriers + the [16][256] Q tile + alignment slack.
-    constexpr int smem = 4 * 2 * 2 * 16 * 256 * 2 + 128 + 16 * 256 * 2 + 1024;
-    static bool cfg = false;
-    if (!cfg) {
-      CB_CUDA_CHECK(cudaFuncSetAttribute(attn_decode_kernel<256>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      cfg = true;
-    }
-    launch_kernel(attn_decode_kernel<256>, grid, dim3(128), smem, stream, tk, tv, a);
-    if (num_splits > 1) {
-      launch_kernel(attn_decode_combine_kernel<256>, dim3(B, Hq), dim3(256), 0, stream, a.part_o,
-                    a.part_ml, a.out, a.out_stride, Hkv, a.G, (int)num_splits);
-    }
-  } else if (D == 512) {
-    // Two CTAs per head (256 output dims each): stages hold a whole K block
-    // and half a V block; + barriers + the [16][512] Q tile + slack.
-    constexpr int smem = 4 * 2 * (16 * 512 * 2 + 16 * 256 * 2) + 128 + 16 * 512 * 2 + 1024;
-    static bool cfg = false;
-    if (!cfg) {
-      CB_CUDA_CHECK(cudaFuncSetAttribute(attn_decode_kernel<512, 256>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      cfg = true;
-    }
-    const dim3 grid2(Hkv, B, (unsigned)num_splits * 2);
-    launch_kernel(attn_decode_kernel<512, 256>, grid2, dim3(128), smem, stream, tk, tv, a);
-    if (num_splits > 1) {
-      launch_kernel(attn_decode_combine_kernel<512>, dim3(B, Hq), dim3(512), 0, stream, a.part_o,
-                    a.part_ml, a.out, a.out_stride, Hkv, a.G, (int)num_splits);
-    }
+    if (win) launch_decode<128, 128, true>(tk, tv, a, grid, B, Hq, stream);
+    else launch_decode<128, 128, false>(tk, tv, a, grid, B, Hq, stream);
   } else if (D == 64) {
-    constexpr int smem = 4 * 2 * 2 * 16 * 64 * 2 + 1024 + 128;
-    // The merge buffer needs 4*16*64*4 + 4*16*2*4 bytes, which fits in smem.
-    static bool cfg = false;
-    if (!cfg) {
-      CB_CUDA_CHECK(cudaFuncSetAttribute(attn_decode_kernel<64>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      cfg = true;
-    }
-    launch_kernel(attn_decode_kernel<64>, grid, dim3(128), smem, stream, tk, tv, a);
-    if (num_splits > 1) {
-      launch_kernel(attn_decode_combine_kernel<64>, dim3(B, Hq), dim3(64), 0, stream, a.part_o,
-                    a.part_ml, a.out, a.out_stride, Hkv, a.G, (int)num_splits);
-    }
+    if (win) launch_decode<64, 64, true>(tk, tv, a, grid, B, Hq, stream);
+    else launch_decode<64, 64, false>(tk, tv, a, grid, B, Hq, stream);
+  } else if (D == 256) {
+    if (win) launch_decode<256, 256, true>(tk, tv, a, grid, B, Hq, stream);
+    else launch_decode<256, 256, false>(tk, tv, a, grid, B, Hq, stream);
+  } else if (D == 512) {
+    // Two CTAs per head, 256 output dims each.
+    if (win) launch_decode<512, 256, true>(tk, tv, a, grid, B, Hq, stream);
+    else launch_decode<512, 256, false>(tk, tv, a, grid, B, Hq, stream);
   } else {
     TORCH_CHECK(false, "head_dim must be 64, 128, 256 or 512");
   }
@@ -743,35 +736,17 @@ void attn_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
   a.sinks = (int)sinks;
   CUtensorMap tk = kv_tmap(k_cache), tv = kv_tmap(v_cache);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  dim3 grid(n_tiles, Hq);
+  const dim3 grid(n_tiles, Hq);
+  const bool win = window > 0;
   if (D == 128) {
-    constexpr int smem = 2 * 2 * 4 * 16 * 128 * 2 + 1024 + 64;
-    static bool cfg = false;
-    if (!cfg) {
-      CB_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<128>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      cfg = true;
-    }
-    launch_kernel(attn_prefill_kernel<128>, grid, dim3(128), smem, stream, tk, tv, a);
-  } else if (D == 256) {
-    // Two K/V stages + barriers + the [64][256] Q tile + alignment slack.
-    constexpr int smem = 2 * 2 * 4 * 16 * 256 * 2 + 128 + 64 * 256 * 2 + 1024;
-    static bool cfg = false;
-    if (!cfg) {
-      CB_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<256>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      cfg = true;
-    }
-    launch_kernel(attn_prefill_kernel<256>, grid, dim3(128), smem, stream, tk, tv, a);
+    if (win) launch_prefill<128, true>(tk, tv, a, grid, stream);
+    else launch_prefill<128, false>(tk, tv, a, grid, stream);
   } else if (D == 64) {
-    constexpr int smem = 2 * 2 * 4 * 16 * 64 * 2 + 1024 + 64;
-    static bool cfg = false;
-    if (!cfg) {
-      CB_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<64>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      cfg = true;
-    }
-    launch_kernel(attn_prefill_kernel<64>, grid, dim3(128), smem, stream, tk, tv, a);
+    if (win) launch_prefill<64, true>(tk, tv, a, grid, stream);
+    else launch_prefill<64, false>(tk, tv, a, grid, stream);
+  } else if (D == 256) {
+    if (win) launch_prefill<256, true>(tk, tv, a, grid, stream);
+    else launch_prefill<256, false>(tk, tv, a, grid, stream);
   } else {
     TORCH_CHECK(false, "head_dim must be 64, 128 or 256");
   }
