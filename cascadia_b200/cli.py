@@ -54,7 +54,7 @@ def _common(p: argparse.ArgumentParser):
     p.add_argument("--tokenizer", default=None)
     p.add_argument("--log-level", default="info")
     p.add_argument("--max-concurrent", type=int, default=16)
-    p.add_argument("--spec", default=None, choices=["ngram", "draft"],
+    p.add_argument("--spec", default=None, choices=["ngram", "draft", "mtp"],
                    help="speculative decoding of greedy requests")
     p.add_argument("--spec-k", type=int, default=4, help="draft tokens per round")
     p.add_argument("--draft-model", default=None, help="draft model preset (--spec draft)")

@@ -53,7 +53,7 @@ class LLMEngine(Engine):
                  max_prefill_tokens: int = 8192, max_model_len: int = 8192,
                  use_graph: bool = True, prefix_cache_blocks: int = 0, model_id: str = "llm",
                  max_queue: int = 1024, spec: Optional[str] = None, draft_model=None,
-                 spec_k: int = 4):
+                 spec_k: int = 4, mtp_head=None):
         self.model = model
         self.dev = model.device
         self.cfg = model.cfg
@@ -76,12 +76,17 @@ class LLMEngine(Engine):
         # Set for the first stage of a pipeline (parallel.pp.PipelineHead):
         # the model forward then relays through the downstream stages.
         self.pipeline = None
-        # Speculative decoding of greedy sequences: "ngram" (prompt lookup)
-        # or "draft" (a small model with its own KV, ``draft_model``).
-        if spec not in (None, "ngram", "draft"):
+        # Speculative decoding of greedy sequences: "ngram" (prompt lookup),
+        # "draft" (a small model with its own KV, ``draft_model``) or "mtp"
+        # (a GLM-5 multi-token-prediction head, ``mtp_head``).
+        if spec not in (None, "ngram", "draft", "mtp"):
             raise InvalidConfig(f"unknown speculative mode {spec!r}")
         if spec == "draft" and draft_model is None:
             raise InvalidConfig("speculative mode 'draft' needs a draft model")
+        if spec == "mtp" and (mtp_head is None or pc is not None):
+            # The head reads the target's hidden row of every prompt token,
+            # which a prefix-cache hit skips.
+            raise InvalidConfig("speculative mode 'mtp' needs an MTP head and no prefix cache")
         self.spec = spec
         self.spec_k = spec_k
         self.drafter = None
@@ -89,6 +94,10 @@ class LLMEngine(Engine):
             from ..runtime.spec import ModelDrafter
 
             self.drafter = ModelDrafter(draft_model, use_graph)
+        elif spec == "mtp":
+            from ..runtime.spec import MTPDrafter
+
+            self.drafter = MTPDrafter(mtp_head)
         self.spec_stats = None
         if spec is not None:
             from ..runtime.spec import SpecStats
@@ -177,6 +186,14 @@ class LLMEngine(Engine):
             s.prefilled = st + n
         seqs = [s for s, _, _ in work]
         toks = self._run_model(batch, ids, seqs)
+        if self.spec == "mtp" and self.pipeline is None:
+            # Queue every prompt row for the MTP head with the token after it.
+            off = 0
+            for (s, st, n), t in zip(work, toks):
+                p = s.prompt_ids
+                nxt = list(p[st + 1:st + n]) + [p[st + n] if st + n < len(p) else int(t)]
+                self.drafter.observe(s.seq_id, st, nxt, self._last_hidden[off:off + n])
+                off += n
         for s, t in zip(seqs, toks):
             if not s.in_prefill:
                 self._emit(s, int(t), out)
@@ -187,6 +204,7 @@ class LLMEngine(Engine):
         hidden = m.embed_tokens(ids)
         if self.pipeline is None:
             m.forward(batch, hidden)
+            self._last_hidden = hidden
             rows = torch.tensor(batch.last_rows, dtype=torch.long, device=self.dev)
             logits = m.head(hidden.index_select(0, rows).contiguous())
             return self._pick(seqs, logits)
@@ -287,16 +305,19 @@ class LLMEngine(Engine):
                 drafts.append(s.ngram.propose(k))
         drafts = [d[:b] for d, b in zip(drafts, budget)]
         kv_lens = [s.total_len - 1 for s in seqs]
-        results = verify_batch(m, ids, [s.output_ids[-1] for s in seqs], drafts, kv_lens)
+        hid = [] if self.spec == "mtp" else None
+        results = verify_batch(m, ids, [s.output_ids[-1] for s in seqs], drafts, kv_lens, hid)
         st = self.spec_stats
         st.rounds += 1
-        for s, d, acc, kl in zip(seqs, drafts, results, kv_lens):
+        for i, (s, d, acc, kl) in enumerate(zip(seqs, drafts, results, kv_lens)):
             a = len(acc) - 1
             st.drafted += len(d)
             st.accepted += a
             st.emitted += len(acc)
             if not s.finished:
                 m.kv.truncate(s.seq_id, kl + 1 + a)
+                if hid is not None:
+                    self.drafter.observe(s.seq_id, kl, acc, hid[i])
                 if self.drafter is not None:
                     self.drafter.accept(s.seq_id, a, k)
             for t in acc:
@@ -381,6 +402,8 @@ class LLMEngine(Engine):
         if finish is None:
             out.append((tid, Chunk.token(tid, tok, text).with_n_tokens(1)))
             return
+        if self.drafter is not None:
+            self.drafter.release(s.seq_id)
         if tok not in self.eos:
             out.append((tid, Chunk.token(tid, tok, text).with_n_tokens(1)))
         fin = Chunk.final_marker(tid, "").with_finish_reason(finish).with_prompt_tokens(
@@ -406,6 +429,7 @@ class LLMBuilder(Builder):
         self.draft_name = draft_model
         self.draft_kv_blocks = draft_kv_blocks
         self.draft = None
+        self.mtp = None
         self.model_name = model
         self.device = device
         self.kv_blocks = kv_blocks
@@ -512,6 +536,16 @@ class LLMBuilder(Builder):
             self.draft = LlamaModel(dcfg, self.device).init_random(seed=self.seed + 1)
             self.draft.allocate_kv(self.draft_kv_blocks or blocks)
             yield LoadProgress.msg(f"draft model {self.draft_name} loaded")
+        if self.spec == "mtp":
+            if not cfg.num_nextn_predict_layers or not cfg.is_dsa:
+                raise InvalidConfig("--spec mtp needs a GLM-5 model with an MTP layer")
+            if self.prefix_cache_blocks:
+                raise InvalidConfig("--spec mtp does not combine with the prefix cache")
+            from ..models.glm5 import GLM5MTP
+
+            self.mtp = GLM5MTP(self.model).init_random(seed=self.seed + 2)
+            self.mtp.allocate_kv(blocks)
+            yield LoadProgress.msg("MTP draft head loaded")
         yield LoadProgress.done()
 
     def build(self) -> Engine:
@@ -521,4 +555,4 @@ class LLMBuilder(Builder):
                          max_model_len=self.max_model_len, use_graph=self.use_graph,
                          prefix_cache_blocks=self.prefix_cache_blocks,
                          model_id=self.model_name, spec=self.spec, draft_model=self.draft,
-                         spec_k=self.spec_k)
+                         spec_k=self.spec_k, mtp_head=self.mtp)

@@ -58,6 +58,7 @@ class ModelConfig:
     index_head_dim: int = 128
     indexer_types: Optional[tuple] = None  # per layer "full" | "shared" (None: all full)
     mla_rope_interleaved: bool = True  # False: checkpoint rotates split halves (NeoX)
+    num_nextn_predict_layers: int = 0  # MTP draft layers stored after the last layer
     # --- Gemma-4 (per-layer attention types, PLE, shared KV) ---
     layer_types: Optional[tuple] = None   # per layer "sliding_attention" | "full_attention"
     local_window: int = 0                 # window of the sliding layers
@@ -96,7 +97,10 @@ class ModelConfig:
         reuse the previous indexer layer's selection)."""
         if not self.is_dsa:
             return False
-        return self.indexer_types is None or self.indexer_types[li] == "full"
+        # The MTP layer (index num_layers) owns its indexer.
+        if self.indexer_types is None or li >= len(self.indexer_types):
+            return True
+        return self.indexer_types[li] == "full"
 
     @property
     def is_hybrid(self) -> bool:
@@ -184,6 +188,7 @@ class ModelConfig:
             if d.get("indexer_types"):
                 c.indexer_types = tuple(d["indexer_types"])
             c.mla_rope_interleaved = False
+            c.num_nextn_predict_layers = int(d.get("num_nextn_predict_layers", 0))
             c.router = "sigmoid"
             types = d.get("mlp_layer_types")
             c.first_k_dense_replace = types.index("sparse") if types and "sparse" in types else \
@@ -274,7 +279,7 @@ PRESETS = {
                          qk_rope_head_dim=64, qk_nope_head_dim=192, v_head_dim=256,
                          index_topk=2048, index_n_heads=32, index_head_dim=128,
                          mla_rope_interleaved=False, group_size=32, max_position=202752,
-                         eos_token_ids=(1,)),
+                         num_nextn_predict_layers=1, eos_token_ids=(1,)),
     # Qwen3.6-35B-A3B (HF qwen3_5_moe): 30 Gated DeltaNet + 10 gated
     # full-attention layers (head_dim 256, rotary on 64 dims), 256 experts
     # top-8 + a sigmoid-gated shared expert.
@@ -341,7 +346,7 @@ PRESETS = {
                              kv_lora_rank=512, qk_rope_head_dim=64, qk_nope_head_dim=192,
                              v_head_dim=256, index_topk=8, index_n_heads=16, index_head_dim=128,
                              indexer_types=("full", "full", "shared"), mla_rope_interleaved=False,
-                             eos_token_ids=(1,)),
+                             num_nextn_predict_layers=1, eos_token_ids=(1,)),
     # Qwen3.6 layer structure at small width (linear head dims are the real
     # 128; full attention head_dim 256 as in the real model).
     "tiny-qwen36": ModelConfig(arch="qwen3_5_moe", vocab_size=512, hidden_size=256, num_layers=4,

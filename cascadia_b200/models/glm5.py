@@ -251,3 +251,98 @@ def load_hf_weights(model: GLM5Model, sd: Dict[str, torch.Tensor],
         model.lm_head = QLinear(q4((head if head is not None else
                                     sd[prefix + "embed_tokens.weight"]).float()), dev)
     return model
+
+
+class GLM5MTP:
+    """GLM-5's multi-token-prediction head (``num_nextn_predict_layers`` = 1,
+    the DeepSeek-V3 MTP module stored as layer ``num_layers``), used as a
+    speculative-decoding drafter.  Row j of the head reads the target's
+    pre-norm hidden ``h_j`` at position j and the token at position j + 1, and
+    predicts the token at j + 2::
+
+        x  = rmsnorm(embed[t_{j+1}], enorm)
+        h  = rmsnorm(final_norm(h_j), hnorm)   (chain steps: rmsnorm(h', hnorm))
+        h' = block(eh_proj [x ; h])            one MLA + DSA + MoE decoder layer
+        t_{j+2} = argmax lm_head(rmsnorm(h', shared_head.norm))
+
+    (crates/cascadia-engine-sparse-moe/src/glm/mtp.rs:1-20 and :66-112 for
+    the chain; ``embed``, ``final_norm`` and ``lm_head`` are the target's.)
+
+    The reference clears the block's KV before each draft chain, so a draft
+    attends only to the chain before it.  Here the block keeps a paged latent
+    KV over the whole sequence: every verified position gets a row (its
+    target hidden and the verified next token, one ragged forward per round
+    for all sequences), and only the chain rows are rewound after the verify.
+    ``eh_proj`` stays bf16 (the reference's notes: INT4 there collapses the
+    acceptance rate); the block is INT4 like every other layer.
+    """
+
+    def __init__(self, target: GLM5Model):
+        cfg = target.cfg
+        assert cfg.num_nextn_predict_layers >= 1, "config has no MTP layer"
+        self.target = target
+        self.cfg = cfg
+        self.device = target.device
+        L = cfg.num_layers
+        self.block = GLM5Model(cfg, target.device, layer_start=L, layer_end=L + 1,
+                               has_embed=False, has_head=False)
+        h = cfg.hidden_size
+        ones = lambda: torch.ones(h, dtype=torch.bfloat16, device=self.device)  # noqa: E731
+        self.enorm, self.hnorm, self.head_norm = ones(), ones(), ones()
+        self.eh_proj = None
+
+    @property
+    def kv(self):
+        return self.block.kv
+
+    def init_random(self, seed: int = 0, std: float = 0.02, gen_device=None):
+        from .llama import _layer_generator
+        from .moe import BF16Linear
+
+        self.block.init_random(seed, std, gen_device)
+        h = self.cfg.hidden_size
+        dev = torch.device(gen_device) if gen_device is not None else self.device
+        g = _layer_generator(seed, 100002, dev)
+        self.eh_proj = BF16Linear(torch.randn(h, 2 * h, generator=g, device=dev) * std,
+                                  self.device)
+        return self
+
+    def allocate_kv(self, num_blocks: int):
+        return self.block.allocate_kv(num_blocks)
+
+    def step(self, batch: Batch, next_tokens: torch.Tensor, h_prev: torch.Tensor,
+             from_target: bool):
+        """One forward of the head over ``batch`` (rows at the positions of
+        ``h_prev``).  Returns (h' [T, H] bf16, greedy drafts [T] int32)."""
+        t = self.target
+        T, H = h_prev.shape
+        x = t.embed_tokens(next_tokens)
+        xn = torch.empty_like(x)
+        t._norm(x, self.enorm, xn)
+        hn = torch.empty_like(h_prev)
+        if from_target:
+            t._norm(h_prev, t.final_norm, hn)
+            h_prev = hn.clone()
+        t._norm(h_prev, self.hnorm, hn)
+        hx = self.eh_proj(torch.cat([xn, hn], dim=-1)).contiguous()
+        self.block.forward(batch, hx)
+        y = torch.empty_like(hx)
+        t._norm(hx, self.head_norm, y)
+        return hx, t.greedy(t.lm_head(y))
+
+
+def load_mtp_weights(mtp: GLM5MTP, sd: Dict[str, torch.Tensor],
+                     prefix: str = "model.") -> GLM5MTP:
+    """Fill the MTP head from a ``glm_moe_dsa`` state dict: the block is
+    ``layers.{num_layers}`` (loaded like any decoder layer), plus ``enorm``,
+    ``hnorm``, ``eh_proj`` and ``shared_head.norm`` of that layer."""
+    from .moe import BF16Linear
+
+    p = f"{prefix}layers.{mtp.cfg.num_layers}."
+    dev = mtp.device
+    bf = lambda n: sd[p + n].to(torch.bfloat16).to(dev)  # noqa: E731
+    load_hf_weights(mtp.block, sd, prefix)
+    mtp.enorm, mtp.hnorm = bf("enorm.weight"), bf("hnorm.weight")
+    mtp.head_norm = bf("shared_head.norm.weight")
+    mtp.eh_proj = BF16Linear(sd[p + "eh_proj.weight"].float(), dev)
+    return mtp

@@ -138,6 +138,7 @@ class BatchGenerator:
         self.model = model
         self.use_graph = use_graph
         self.graphs: Dict[tuple, DecodeGraph] = {}
+        self.last_hidden: Optional[torch.Tensor] = None
 
     def prefill(self, seq_ids: Sequence[str], prompts: Sequence[Sequence[int]],
                 start: Optional[Sequence[int]] = None) -> torch.Tensor:
@@ -151,6 +152,7 @@ class BatchGenerator:
         ids = torch.tensor([t for p in prompts for t in p], dtype=torch.int32).to(m.device)
         hidden = m.embed_tokens(ids)
         m.forward(batch, hidden)
+        self.last_hidden = hidden  # pre-norm rows of every prompt token (MTP drafting)
         last = torch.tensor(batch.last_rows, dtype=torch.long, device=m.device)
         logits = m.head(hidden.index_select(0, last).contiguous())
         return m.greedy(logits)

@@ -143,16 +143,22 @@ class SpecStats:
 
 
 def verify_batch(m, seq_ids: List[str], pending: List[int], drafts: List[List[int]],
-                 kv_lens: List[int]) -> List[List[int]]:
+                 kv_lens: List[int], hidden_out: Optional[list] = None) -> List[List[int]]:
     """One target forward over ``[pending, *drafts]`` per sequence (positions
     from ``kv_lens``), argmax of every row, device verify.  Returns, per
     sequence, the accepted drafts followed by the correction token.  The
-    caller rewinds the KV to ``kv_len + len(result)``."""
+    caller rewinds the KV to ``kv_len + len(result)``.  ``hidden_out``, when
+    given, receives the pre-norm hidden rows of each sequence's forward."""
     rows = [[p] + d for p, d in zip(pending, drafts)]
     batch = build_batch(m, seq_ids, [len(r) for r in rows], kv_lens, False)
     flat = torch.tensor([t for r in rows for t in r], dtype=torch.int32).to(m.device)
     hidden = m.embed_tokens(flat)
     m.forward(batch, hidden)
+    if hidden_out is not None:
+        o = 0
+        for r in rows:
+            hidden_out.append(hidden[o:o + len(r)])
+            o += len(r)
     picks = m.greedy(m.head(hidden)).to(torch.int32)  # argmax of every row
     kmax = max(len(d) for d in drafts)
     B = len(rows)
@@ -228,18 +234,90 @@ class ModelDrafter:
             self.model.kv.free_sequence(sid)
 
 
+class MTPDrafter:
+    """Drafts from a multi-token-prediction head (``models.glm5.GLM5MTP``).
+    The head's KV holds one row per verified position: after the prefill and
+    after every verify, ``observe`` queues the new verified rows (target
+    hidden, next token); ``propose`` runs them for all sequences in one
+    ragged forward, whose last row per sequence gives d1, then k-1 chain
+    steps (token d_i, hidden = the head's own output) give d2 .. dk.  The
+    chain rows are rewound in ``accept``.  (The reference's MTP spec loop:
+    crates/cascadia-engine-sparse-moe/src/glm/model.rs:404-470, one
+    sequence, block KV cleared per chain.)"""
+
+    def __init__(self, mtp):
+        self.mtp = mtp
+        self.kv_len: Dict[str, int] = {}
+        self.queue: Dict[str, Tuple[int, List[int], List[torch.Tensor]]] = {}
+
+    def observe(self, sid: str, start: int, next_tokens: Sequence[int], hidden: torch.Tensor):
+        """Target rows at positions ``start ..`` with their pre-norm hidden
+        and the verified token that follows each."""
+        n = len(next_tokens)
+        st, toks, hs = self.queue.get(sid, (start, [], []))
+        assert st + len(toks) == start, "observed rows must be contiguous"
+        self.queue[sid] = (st, toks + [int(t) for t in next_tokens], hs + [hidden[:n]])
+
+    def propose(self, seq_ids: List[str], histories: List[List[int]], k: int,
+                width: int) -> List[List[int]]:
+        mtp = self.mtp
+        kv = mtp.kv
+        dev = mtp.device
+        starts, qls, toks, hs = [], [], [], []
+        for sid in seq_ids:
+            if sid not in kv.seqs:
+                kv.add_sequence(sid)
+                self.kv_len[sid] = 0
+            st, t, h = self.queue.pop(sid)
+            assert st == self.kv_len[sid]
+            starts.append(st)
+            qls.append(len(t))
+            toks.extend(t)
+            hs.extend(h)
+        batch = build_batch(mtp.block, seq_ids, qls, starts, False)
+        ids = torch.tensor(toks, dtype=torch.int32).to(dev)
+        hout, picks = mtp.step(batch, ids, torch.cat(hs).contiguous(), from_target=True)
+        last = torch.tensor(batch.last_rows, dtype=torch.long, device=dev)
+        h = hout.index_select(0, last).contiguous()
+        d = picks.index_select(0, last)
+        for sid, st, q in zip(seq_ids, starts, qls):
+            self.kv_len[sid] = st + q
+        drafts = [[int(t)] for t in d.cpu()]
+        pos = [st + q - 1 for st, q in zip(starts, qls)]
+        for _ in range(k - 1):
+            pos = [p + 1 for p in pos]
+            batch = build_batch(mtp.block, seq_ids, [1] * len(seq_ids), pos, True)
+            h, d = mtp.step(batch, d.to(torch.int32), h, from_target=False)
+            for x, t in zip(drafts, d.cpu().tolist()):
+                x.append(int(t))
+        return drafts
+
+    def accept(self, sid: str, accepted: int, k: int):
+        self.mtp.kv.truncate(sid, self.kv_len[sid])
+
+    def release(self, sid: str):
+        self.kv_len.pop(sid, None)
+        self.queue.pop(sid, None)
+        if sid in self.mtp.kv.seqs:
+            self.mtp.kv.free_sequence(sid)
+
+
 class SpecDecoder:
     """Batched greedy speculative decoding of `target` with either a draft
     model (``draft``: a model with its own KV cache) or n-gram drafts."""
 
     def __init__(self, target, draft=None, k: int = 4, ngram_k: int = DEFAULT_NGRAM_K,
-                 use_graph: bool = True):
+                 use_graph: bool = True, mtp=None):
         from .generator import BatchGenerator
 
         self.target = target
-        self.k = k if draft is not None else ngram_k
+        self.k = k if (draft is not None or mtp is not None) else ngram_k
         self.tgen = BatchGenerator(target, use_graph=use_graph)
-        self.drafter = ModelDrafter(draft, use_graph) if draft is not None else None
+        if mtp is not None:
+            self.drafter = MTPDrafter(mtp)
+        else:
+            self.drafter = ModelDrafter(draft, use_graph) if draft is not None else None
+        self.mtp = self.drafter if mtp is not None else None
         self.stats = SpecStats()
 
     def generate(self, prompts: Sequence[Sequence[int]], max_new_tokens: int,
@@ -249,9 +327,14 @@ class SpecDecoder:
         longest = max(len(p) for p in prompts) + max_new_tokens + self.k + 2
         width = -(-longest // BLOCK_SIZE)
         first = self.tgen.prefill(ids, prompts)
+        if self.mtp is not None:
+            hid, o = self.tgen.last_hidden, 0
         states = []
         for sid, p, t in zip(ids, prompts, first.cpu().tolist()):
             s = SpecState(sid, list(p) + [int(t)], kv_len=len(p), generated=1)
+            if self.mtp is not None:
+                self.mtp.observe(sid, 0, list(p[1:]) + [int(t)], hid[o:o + len(p)])
+                o += len(p)
             if self.drafter is None:
                 s.ngram = NGramDraft(self.k)
                 s.ngram.extend(s.tokens)
@@ -268,11 +351,16 @@ class SpecDecoder:
                 drafts = [s.ngram.propose(self.k) for s in live]
             # Never draft past the token budget.
             drafts = [d[:max(0, max_new_tokens - s.generated - 1)] for s, d in zip(live, drafts)]
+            hid = [] if self.mtp is not None else None
             accepted = verify_batch(m, [s.sid for s in live], [s.tokens[-1] for s in live],
-                                    drafts, [s.kv_len for s in live])
+                                    drafts, [s.kv_len for s in live], hid)
             self.stats.rounds += 1
-            for s, d, acc in zip(live, drafts, accepted):
+            for i, (s, d, acc) in enumerate(zip(live, drafts, accepted)):
                 a = len(acc) - 1
+                if self.mtp is not None:
+                    # Rows kv_len .. kv_len + a are verified; each is followed
+                    # by the next accepted token (the last by the correction).
+                    self.mtp.observe(s.sid, s.kv_len, acc, hid[i])
                 self.stats.drafted += len(d)
                 self.stats.accepted += a
                 new = acc[:max_new_tokens - s.generated]
