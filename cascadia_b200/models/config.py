@@ -72,6 +72,7 @@ class ModelConfig:
     final_logit_softcapping: float = 0.0
     rope_theta_local: float = 10000.0
     global_partial_rotary: float = 1.0
+    gemma_moe: bool = False               # MoE block beside every layer's MLP (enable_moe_block)
     # --- hybrid linear attention (Qwen3.5 / Qwen3.6: Gated DeltaNet layers,
     # every full_attention_interval-th layer full attention) ---
     full_attention_interval: int = 0   # 0: no linear-attention layers
@@ -163,7 +164,7 @@ class ModelConfig:
         mt = d.get("model_type", "")
         if d.get("num_experts") or d.get("n_routed_experts"):
             c.num_experts = d.get("num_experts") or d.get("n_routed_experts")
-            c.num_experts_per_tok = d["num_experts_per_tok"]
+            c.num_experts_per_tok = d.get("num_experts_per_tok") or d.get("top_k_experts")
             c.moe_intermediate_size = d["moe_intermediate_size"]
             c.num_shared_experts = d.get("n_shared_experts", 0) or 0
             c.norm_topk_prob = bool(d.get("norm_topk_prob", True))
@@ -212,6 +213,13 @@ class ModelConfig:
             c.global_partial_rotary = float(fa.get("partial_rotary_factor", 1.0))
             c.rope_scaling = None
             c.tie_word_embeddings = bool(d.get("tie_word_embeddings", True))
+            if d.get("enable_moe_block"):
+                c.gemma_moe = True
+                c.num_experts = int(d["num_experts"])
+                c.num_experts_per_tok = int(d["top_k_experts"])
+                c.moe_intermediate_size = int(d["moe_intermediate_size"])
+                c.router = "softmax"
+                c.norm_topk_prob = True
         if mt.startswith("qwen3"):
             c.qk_norm = True
         if mt.startswith("qwen3_5") or mt.startswith("qwen3_next"):
@@ -334,6 +342,18 @@ PRESETS = {
                                vocab_size_per_layer_input=512, final_logit_softcapping=30.0,
                                rope_theta=1000000.0, rope_theta_local=10000.0,
                                global_partial_rotary=0.25, eos_token_ids=(1,)),
+    # The MoE-block variant (dense MLP + routed experts in every layer).
+    "tiny-gemma4-moe": ModelConfig(arch="gemma4", vocab_size=512, hidden_size=256, num_layers=4,
+                                   num_heads=4, num_kv_heads=2, head_dim=256,
+                                   intermediate_size=256, rms_eps=1e-6, tie_word_embeddings=True,
+                                   layer_types=("sliding_attention", "sliding_attention",
+                                                "sliding_attention", "full_attention"),
+                                   local_window=16, global_head_dim=512, num_global_kv_heads=1,
+                                   attention_k_eq_v=True, final_logit_softcapping=30.0,
+                                   rope_theta=1000000.0, rope_theta_local=10000.0,
+                                   global_partial_rotary=0.25, gemma_moe=True, num_experts=8,
+                                   num_experts_per_tok=2, moe_intermediate_size=128,
+                                   router="softmax", norm_topk_prob=True, eos_token_ids=(1,)),
     # GLM-5 layer structure at small width: MLA (latent 512, rope 64; nope
     # 192 / v 256 as in GLM-5), DSA indexer with top-8 (so selection matters
     # at test lengths), IndexShare on layer 2, 1 dense + 2 MoE layers.

@@ -20,7 +20,15 @@ gemma4-support.md).  Here one model object runs it on our kernels:
 * proportional RoPE on full layers (rotation on the first quarter of the
   frequency pairs, identity on the rest), logits soft-capped.
 
-The mixture-of-experts block of some Gemma-4 variants is not supported.
+The mixture-of-experts variant (``enable_moe_block``) adds, beside each
+layer's MLP, routed experts fed from the pre-MLP residual: the router
+RMS-normalises it (no weight), scales by a learned vector and H^-1/2
+(folded into the router rows), softmax top-k, renormalised, times a
+per-expert scale; the experts (GeLU-tanh) read their own pre-norm of the
+residual, and the two branches are normed separately and summed before the
+MLP's post-norm (transformers ``Gemma4TextDecoderLayer``).  On the GPU the
+router is the fused top-k gate kernel and the experts run the grouped
+small-M / grouped tcgen05 kernels with a store epilogue (GeLU in between).
 Caches: one paged pool per head size (256 / 512) over the same block
 tables.  The CPU path is the fp32 oracle.
 """
@@ -97,6 +105,17 @@ class G4Layer:
     ple_proj: Optional[QLinear]
     ple_norm: Optional[torch.Tensor]
     scalar: float
+    moe: Optional["G4MoE"] = None
+
+
+@dataclass
+class G4MoE:
+    router: torch.Tensor          # [E, H] bf16, scale * H^-1/2 folded into the columns
+    expert_scale: torch.Tensor    # [E] fp32
+    experts: object               # moe.ExpertBank (gate | up rows, not interleaved)
+    post_ff_norm_1: torch.Tensor  # after the MLP branch
+    pre_ff_norm_2: torch.Tensor   # expert input
+    post_ff_norm_2: torch.Tensor  # after the expert branch
 
 
 class Gemma4Model(LlamaModel):
@@ -175,6 +194,17 @@ class Gemma4Model(LlamaModel):
             for n in ("input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
                       "post_feedforward_layernorm"):
                 sd[p + n + ".weight"] = torch.ones(H, device=dev)
+            if cfg.gemma_moe:
+                E, Im = cfg.num_experts, cfg.moe_intermediate_size
+                sd[p + "router.proj.weight"] = r(E, H)
+                sd[p + "router.scale"] = torch.ones(H, device=dev)
+                sd[p + "router.per_expert_scale"] = torch.ones(E, device=dev)
+                sd[p + "experts.gate_up_proj"] = torch.randn(E, 2 * Im, H, generator=g,
+                                                             device=dev) * std
+                sd[p + "experts.down_proj"] = torch.randn(E, H, Im, generator=g, device=dev) * std
+                for n in ("post_feedforward_layernorm_1", "pre_feedforward_layernorm_2",
+                          "post_feedforward_layernorm_2"):
+                    sd[p + n + ".weight"] = torch.ones(H, device=dev)
             if P:
                 sd[p + "per_layer_input_gate.weight"] = r(P, H)
                 sd[p + "per_layer_projection.weight"] = r(H, P)
@@ -252,6 +282,8 @@ class Gemma4Model(LlamaModel):
             act = (F.gelu(gu[:, :I].float(), approximate="tanh") * gu[:, I:].float()).to(
                 torch.bfloat16)
             m = lw.down(act)
+            if lw.moe is not None:
+                m = self._moe_branch(lw.moe, m, hidden)
             self._norm_to(m, lw.post_ff_norm, t2)
             hidden.copy_((hidden.float() + t2.float()).to(torch.bfloat16))
             if lw.ple_gate is not None:
@@ -264,6 +296,62 @@ class Gemma4Model(LlamaModel):
             if lw.scalar != 1.0:
                 hidden.copy_((hidden.float() * lw.scalar).to(torch.bfloat16))
         return hidden
+
+    def _moe_branch(self, mo: G4MoE, mlp_out: torch.Tensor, resid: torch.Tensor) -> torch.Tensor:
+        """norm1(MLP output) + norm2(routed experts of the residual)."""
+        cfg = self.cfg
+        k = cfg.num_experts_per_tok
+        T = resid.shape[0]
+        h1 = torch.empty_like(mlp_out)
+        self._norm_to(mlp_out, mo.post_ff_norm_1, h1)
+        xe = torch.empty_like(resid)
+        self._norm_to(resid, mo.pre_ff_norm_2, xe)
+        bank = mo.experts
+        if self.device.type == "cuda":
+            rn = torch.empty_like(resid)
+            ops.rmsnorm(resid, self._ones_h, rn, cfg.rms_eps)
+            ids, w = ops.moe_topk_gate(rn, mo.router, k, 0, True, 1.0)
+            w = w * mo.expert_scale.index_select(0, ids.view(-1).long()).view(T, k)
+            n = T * k
+            I = bank.inter
+            if T <= 8 and bank.gs == 128:
+                offsets, perm, inv, _ = ops.moe_permute(ids, bank.E)
+                x16, xs = ops.moe_prep_fp16(xe, n, perm, k)
+                gu = ops.w4a16_gemv_grouped(x16, xs, bank.gu_blob, 2 * I, ops.EPI_STORE,
+                                            offsets, bank.E, sched=bank.sched[0])
+                act = (F.gelu(gu[:n, :I].float(), approximate="tanh") *
+                       gu[:n, I:].float()).to(torch.bfloat16)
+                a16, a_s = ops.moe_prep_fp16(act, n)
+                y = ops.w4a16_gemv_grouped(a16, a_s, bank.dn_blob, bank.hidden, ops.EPI_STORE,
+                                           offsets, bank.E, sched=bank.sched[1])
+            else:
+                offsets, perm, inv, xp = ops.moe_permute(ids, bank.E, xe)
+                gu = ops.w4a16_gemm_grouped(xp, bank.gu_blob, 2 * I, bank.gs, ops.EPI_STORE,
+                                            offsets, bank.E, T)
+                act = (F.gelu(gu[:, :I].float(), approximate="tanh") *
+                       gu[:, I:].float()).to(torch.bfloat16)
+                y = ops.w4a16_gemm_grouped(act, bank.dn_blob, bank.hidden, bank.gs,
+                                           ops.EPI_STORE, offsets, bank.E, T)
+            h2 = torch.empty_like(resid)
+            ops.moe_combine(y, inv, w, out=h2)
+        else:
+            rn = self._rms(resid, None).float()
+            probs = torch.softmax(rn @ mo.router.float().t(), dim=-1)
+            wt, ids = torch.topk(probs, k, dim=-1)
+            wt = wt / wt.sum(-1, keepdim=True) * mo.expert_scale[ids]
+            acc = torch.zeros(T, cfg.hidden_size)
+            I = bank.inter
+            for t in range(T):
+                for j in range(k):
+                    e = int(ids[t, j])
+                    gu = xe[t:t + 1].float() @ bank.gu_ref[e].t()
+                    a = (F.gelu(gu[:, :I], approximate="tanh") * gu[:, I:]).to(torch.bfloat16)
+                    y = (a.float() @ bank.dn_ref[e].t()).to(torch.bfloat16)
+                    acc[t] += float(wt[t, j]) * y[0].float()
+            h2 = acc.to(torch.bfloat16)
+        t2 = torch.empty_like(resid)
+        self._norm_to(h2, mo.post_ff_norm_2, t2)
+        return (h1.float() + t2.float()).to(torch.bfloat16)
 
     def _attention_g4(self, i: int, lw: G4Layer, h: torch.Tensor, batch: Batch) -> torch.Tensor:
         cfg = self.cfg
@@ -379,9 +467,24 @@ def load_hf_weights(model: Gemma4Model, sd: Dict[str, torch.Tensor],
         model.ple_model_proj = QLinear(q4(W("per_layer_model_projection.weight")), dev)
         model.ple_proj_norm = bf(W("per_layer_projection_norm.weight"))
     model.layers = []
+    model._ones_h = torch.ones(cfg.hidden_size, dtype=torch.bfloat16, device=dev)
     for li in range(cfg.num_layers):
         p = f"layers.{li}."
         sp = model.spec[li]
+        moe = None
+        if cfg.gemma_moe:
+            from .moe import ExpertBank
+
+            gu, dn = W(p + "experts.gate_up_proj"), W(p + "experts.down_proj")
+            fold = W(p + "router.scale") * cfg.hidden_size ** -0.5
+            moe = G4MoE(router=bf(W(p + "router.proj.weight") * fold[None, :]),
+                        expert_scale=W(p + "router.per_expert_scale").to(dev),
+                        experts=ExpertBank([q4(gu[e]) for e in range(cfg.num_experts)],
+                                           [q4(dn[e]) for e in range(cfg.num_experts)], dev,
+                                           interleave=False),
+                        post_ff_norm_1=bf(W(p + "post_feedforward_layernorm_1.weight")),
+                        pre_ff_norm_2=bf(W(p + "pre_feedforward_layernorm_2.weight")),
+                        post_ff_norm_2=bf(W(p + "post_feedforward_layernorm_2.weight")))
         full = sp["full"]
         d = cfg.global_head_dim if full else cfg.head_dim
         k_eq_v = full and cfg.attention_k_eq_v
@@ -408,7 +511,7 @@ def load_hf_weights(model: Gemma4Model, sd: Dict[str, torch.Tensor],
             ple_gate=QLinear(q4(W(p + "per_layer_input_gate.weight")), dev) if model.P else None,
             ple_proj=QLinear(q4(W(p + "per_layer_projection.weight")), dev) if model.P else None,
             ple_norm=bf(W(p + "post_per_layer_input_norm.weight")) if model.P else None,
-            scalar=float(W(p + "layer_scalar").reshape(-1)[0])))
+            scalar=float(W(p + "layer_scalar").reshape(-1)[0]), moe=moe))
     model.final_norm = bf(W("norm.weight"))
     head = sd.get("lm_head.weight")
     if head is None or cfg.tie_word_embeddings:

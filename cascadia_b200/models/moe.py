@@ -59,7 +59,8 @@ class ExpertBank:
     """All routed experts of one layer: blobs back to back (GPU) or dequantised
     fp32 weights (CPU oracle)."""
 
-    def __init__(self, gate_up: List[Int4Weight], down: List[Int4Weight], device):
+    def __init__(self, gate_up: List[Int4Weight], down: List[Int4Weight], device,
+                 interleave: bool = True):
         from . import llama
 
         self.int4 = (list(gate_up), list(down)) if llama.KEEP_INT4 else None
@@ -69,9 +70,15 @@ class ExpertBank:
         self.gs = gate_up[0].group_size
         dev = torch.device(device)
         if dev.type == "cuda":
-            self.gu_blob = torch.cat([w.to(dev).blob(interleave_gate_up=True) for w in gate_up])
+            # Interleaved gate/up rows feed the fused SiLU epilogue; without
+            # it the store epilogue gives [gate | up] columns.
+            self.gu_blob = torch.cat([w.to(dev).blob(interleave_gate_up=interleave)
+                                      for w in gate_up])
             self.dn_blob = torch.cat([w.to(dev).blob() for w in down])
             self.gu_ref = self.dn_ref = None
+            # Unit counters of the grouped small-M kernel (dynamic
+            # scheduling), one pair per projection of this layer.
+            self.sched = torch.zeros(2, 2, dtype=torch.int32, device=dev)
         else:
             self.gu_blob = self.dn_blob = None
             self.gu_ref = [w.dequant_bf16().float() for w in gate_up]
@@ -248,10 +255,10 @@ class MoEModel(LlamaModel):
                 n = T * k
                 x16, xs = ops.moe_prep_fp16(h, n, perm, k)
                 act = ops.w4a16_gemv_grouped(x16, xs, bank.gu_blob, 2 * bank.inter,
-                                             ops.EPI_SILU, offsets, bank.E)
+                                             ops.EPI_SILU, offsets, bank.E, sched=bank.sched[0])
                 a16, a_s = ops.moe_prep_fp16(act, n)
                 y = ops.w4a16_gemv_grouped(a16, a_s, bank.dn_blob, bank.hidden, ops.EPI_STORE,
-                                           offsets, bank.E)
+                                           offsets, bank.E, sched=bank.sched[1])
             else:
                 offsets, perm, inv, xp = ops.moe_permute(ids, bank.E, h)
                 act = ops.w4a16_gemm_grouped(xp, bank.gu_blob, 2 * bank.inter, bank.gs,

@@ -28,14 +28,26 @@ def _hf_model(ours: ModelConfig, seed=0):
         hidden_size_per_layer_input=ours.hidden_size_per_layer_input,
         vocab_size_per_layer_input=ours.vocab_size_per_layer_input,
         final_logit_softcapping=ours.final_logit_softcapping, rms_norm_eps=ours.rms_eps,
-        layer_types=list(ours.layer_types), tie_word_embeddings=True)
+        layer_types=list(ours.layer_types), tie_word_embeddings=True,
+        **(dict(enable_moe_block=True, num_experts=ours.num_experts,
+                top_k_experts=ours.num_experts_per_tok,
+                moe_intermediate_size=ours.moe_intermediate_size) if ours.gemma_moe else {}))
     cfg._attn_implementation = "eager"
     torch.manual_seed(seed)
     m = hf.Gemma4ForCausalLM(cfg).eval()
     g = torch.Generator().manual_seed(seed + 1)
     with torch.no_grad():
         for name, p in m.named_parameters():
-            if p.dim() == 1 and ("q_norm" in name or "k_norm" in name):
+            if "router.scale" in name:
+                # Ones (HF's init): the scale * H^-1/2 fold into the router
+                # rows is then exact.
+                p.fill_(1.0)
+            elif "router.proj" in name:
+                # A spread-out router: random near-ties between the k-th and
+                # (k+1)-th expert would flip with bf16 rounding of the input.
+                p.normal_(0, 1.0, generator=g)
+                p.copy_(p.to(torch.bfloat16).float())
+            elif p.dim() == 1 and ("q_norm" in name or "k_norm" in name):
                 # Attention is unscaled (scale 1 on RMS-normalised q and k):
                 # small norm weights keep the random model's softmax from
                 # being near one-hot, where bf16 rounding alone (HF's own
@@ -49,9 +61,10 @@ def _hf_model(ours: ModelConfig, seed=0):
             elif "embed" in name:  # also the tied LM head: INT4-representable
                 p.normal_(0, 0.05, generator=g)
                 p.copy_(Int4Weight.quantize(p.float(), 128).dequant_bf16().float())
-            else:
+            else:  # 3-D expert tensors: groups along the last (input) dim
                 p.normal_(0, 0.05, generator=g)
-                p.copy_(Int4Weight.quantize(p.float(), 128).dequant_bf16().float())
+                flat = p.reshape(-1, p.shape[-1]).float()
+                p.copy_(Int4Weight.quantize(flat, 128).dequant_bf16().float().view_as(p))
         for name, b in m.named_buffers():
             if name.endswith("layer_scalar"):
                 b.copy_(torch.tensor([0.75]))
@@ -90,8 +103,9 @@ def test_hf_config_maps_to_gemma4():
     assert cfg.num_kv_shared_layers == 18 and cfg.attention_k_eq_v
 
 
-def test_prefill_and_decode_match_hf():
-    cfg = get_config("tiny-gemma4")
+@pytest.mark.parametrize("preset", ["tiny-gemma4", "tiny-gemma4-moe"])
+def test_prefill_and_decode_match_hf(preset):
+    cfg = get_config(preset)
     hfm = _hf_model(cfg)
     ours = _ours(cfg, hfm.state_dict())
     n = 27  # longer than the 16-token window
@@ -115,3 +129,15 @@ def test_prefill_and_decode_match_hf():
         ours.forward(b, hid)
         _close(ours.head(hid), want)
         pos += 1
+
+
+def test_hf_config_maps_moe_block():
+    cfg = ModelConfig.from_hf({
+        "model_type": "gemma4_text", "vocab_size": 262144, "hidden_size": 2816,
+        "num_hidden_layers": 30, "num_attention_heads": 16, "num_key_value_heads": 8,
+        "head_dim": 256, "global_head_dim": 512, "sliding_window": 1024,
+        "intermediate_size": 2112, "enable_moe_block": True, "num_experts": 128,
+        "top_k_experts": 8, "moe_intermediate_size": 704,
+        "layer_types": (["sliding_attention"] * 5 + ["full_attention"]) * 5})
+    assert cfg.gemma_moe and cfg.num_experts == 128 and cfg.num_experts_per_tok == 8
+    assert cfg.moe_intermediate_size == 704 and cfg.router == "softmax"

@@ -14,15 +14,21 @@ from cascadia_b200.runtime.generator import BatchGenerator
 pytestmark = pytest.mark.gpu
 
 
-def _pair(seed=3):
-    cfg = get_config("tiny-gemma4")
+def _pair(seed=3, preset="tiny-gemma4"):
+    cfg = get_config(preset)
     cpu = Gemma4Model(cfg, "cpu").init_random(seed=seed, gen_device="cpu")
     gpu = Gemma4Model(cfg, "cuda").init_random(seed=seed, gen_device="cpu")
     for m in (cpu, gpu):
         m.allocate_kv(64)
+        g = torch.Generator().manual_seed(seed + 100)
         for lw in m.layers:  # moderate attention sharpness (see test_gemma4_cpu)
             lw.q_norm.fill_(0.2)
             lw.k_norm.fill_(0.2)
+            if lw.moe is not None:
+                # Router logits of std ~1 (the random init is near uniform,
+                # where CPU/GPU rounding would swap near-tied experts).
+                r = (torch.randn(lw.moe.router.shape, generator=g) / 16).to(torch.bfloat16)
+                lw.moe.router.copy_(r.to(lw.moe.router.device))
     return cfg, cpu, gpu
 
 
@@ -33,8 +39,9 @@ def _close(a, b, frac=0.05):
     assert err <= frac * scale + 1e-3, (err, scale)
 
 
-def test_prefill_beyond_window_then_decode_matches_cpu():
-    cfg, cpu, gpu = _pair()
+@pytest.mark.parametrize("preset", ["tiny-gemma4", "tiny-gemma4-moe"])
+def test_prefill_beyond_window_then_decode_matches_cpu(preset):
+    cfg, cpu, gpu = _pair(preset=preset)
     g = torch.Generator().manual_seed(1)
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g) for n in (5, 40)]
     ids = ["a", "b"]
@@ -60,8 +67,9 @@ def test_prefill_beyond_window_then_decode_matches_cpu():
         _close(gg, c)
 
 
-def test_graph_generation_matches_eager():
-    cfg, _, gpu = _pair(seed=5)
+@pytest.mark.parametrize("preset", ["tiny-gemma4", "tiny-gemma4-moe"])
+def test_graph_generation_matches_eager(preset):
+    cfg, _, gpu = _pair(seed=5, preset=preset)
     g = torch.Generator().manual_seed(2)
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (6, 30)]
     eager = BatchGenerator(gpu, use_graph=False).generate(prompts, 6, prefix="e")
