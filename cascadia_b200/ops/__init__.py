@@ -372,15 +372,17 @@ def moe_prep_fp16(x, rows: int, perm=None, topk: int = 1, rows_dev=None, out=Non
 
 
 def w4a16_gemv_grouped(x16, xs, blob, n: int, epilogue: int, offsets, num_groups: int,
-                       out=None, out_rows=None):
+                       out=None, out_rows=None, sched=None):
     """Grouped small-M W4A16 GEMM (group 128) on prepared activations; the
-    decode path of the MoE experts (few rows per expert)."""
+    decode path of the MoE experts (few rows per expert).  ``sched`` (int32
+    [2] zeros, owned by the call site and never used by two launches at
+    once) switches the kernel to dynamic unit scheduling."""
     rows = x16.shape[0]
     n_out = n // 2 if epilogue == EPI_SILU else n
     if out is None:
         out = torch.empty(rows, n_out, dtype=torch.bfloat16, device=x16.device)
     ext().w4a16_gemv_grouped(x16, xs, blob, out, n, epilogue, offsets, num_groups,
-                             status_buffer(x16.device), out_rows)
+                             status_buffer(x16.device), out_rows, sched)
     LAUNCHES.add(1)
     return out
 

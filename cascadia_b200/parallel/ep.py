@@ -121,11 +121,11 @@ class ExpertParallel:
             rows = min(self.world * self.row_bound * self.k, self.xp.shape[0])
             x16, xs = ops.moe_prep_fp16(self.xp, rows, rows_dev=self.total)
             act = ops.w4a16_gemv_grouped(x16, xs, bank.gu_blob, 2 * bank.inter, ops.EPI_SILU,
-                                         self.offsets, self.e_local)
+                                         self.offsets, self.e_local, sched=bank.sched[0])
             a16, a_s = ops.moe_prep_fp16(act, rows, rows_dev=self.total)
             ops.w4a16_gemv_grouped(a16, a_s, bank.dn_blob, bank.hidden, ops.EPI_STORE,
                                    self.offsets, self.e_local, out=act[:1, :0],
-                                   out_rows=self.out_rows)
+                                   out_rows=self.out_rows, sched=bank.sched[1])
         else:
             act = ops.w4a16_gemm_grouped(self.xp, bank.gu_blob, 2 * bank.inter, bank.gs,
                                          ops.EPI_SILU, self.offsets, self.e_local, max_rows)

@@ -76,7 +76,8 @@ std::vector<int64_t> moe_prep_shape(int64_t K);
 void w4a16_gemv_grouped(torch::Tensor x16, torch::Tensor xsum, torch::Tensor wblob,
                         torch::Tensor out, int64_t N, int64_t epilogue, torch::Tensor offsets,
                         int64_t num_groups, torch::Tensor status,
-                        c10::optional<torch::Tensor> out_rows);
+                        c10::optional<torch::Tensor> out_rows,
+                        c10::optional<torch::Tensor> sched);
 // moe.cu
 void moe_topk_gate(torch::Tensor x, torch::Tensor wg, c10::optional<torch::Tensor> bias,
                    int64_t k, int64_t scoring, bool norm_topk, double routed_scale,
@@ -166,5 +167,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_workspace_floats", &cb::gemv_workspace_floats);
   m.def("moe_prep_fp16", &cb::moe_prep_fp16);
   m.def("moe_prep_shape", &cb::moe_prep_shape);
-  m.def("w4a16_gemv_grouped", &cb::w4a16_gemv_grouped);
+  m.def("w4a16_gemv_grouped", &cb::w4a16_gemv_grouped, py::arg("x16"), py::arg("xsum"),
+        py::arg("wblob"), py::arg("out"), py::arg("N"), py::arg("epilogue"), py::arg("offsets"),
+        py::arg("num_groups"), py::arg("status"), py::arg("out_rows") = py::none(),
+        py::arg("sched") = py::none());
 }

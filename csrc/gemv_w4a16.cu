@@ -546,6 +546,15 @@ void gv_launch_nt(int NT, const GvArgs& a, dim3 grid, int smem, cudaStream_t s) 
 // per row, with the per-k-block offset corrections and the row exponent in
 // `xsum`), so a unit only copies its rows in: one bulk copy for the X rows,
 // one for their corrections, into a double-buffered X tile.
+//
+// Unit order: with `sched` (int[2], zero before the first launch) each CTA's
+// producer takes the next unit from an atomic counter, so CTAs that drew
+// many-row or many-tile experts do not hold up the grid; units of experts
+// without rows are skipped as they are drawn.  The producer hands each
+// sub-unit (expert, tile, first row, rows) to the consumers in shared memory
+// beside its X buffer, and a sentinel (expert -1) ends the loop.  The last
+// producer to finish resets the counter for the next launch.  Without
+// `sched` CTA b takes units b, b + grid, ... in order.
 struct GvgArgs {
   const uint8_t* wblob;
   long long blob_stride;     // bytes per expert
@@ -556,6 +565,7 @@ struct GvgArgs {
   __nv_bfloat16* out;        // [R, ldo]
   const long long* out_rows; // optional per-row destination addresses
   int* status;
+  int* sched;                // optional [next unit, CTAs done]
   int E, N, K, ldx16, ldxs, ldo, stages;
 };
 
@@ -584,6 +594,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_grouped_kernel(const
   uint64_t* xempty = bars + 2 * S + 2;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * S + 4);
   volatile int* s_abort = reinterpret_cast<volatile int*>(bars + 2 * S + 5);
+  int* info = reinterpret_cast<int*>(bars + 2 * S + 6);  // [2][4]: e, rt, row0, rows
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -604,7 +615,9 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_grouped_kernel(const
       int slot = 0, sub = 0, issued = 0;
       uint32_t phase = 0;
       bool go = true;
-      for (int u = blockIdx.x; u < a.E * RT && go; u += gridDim.x) {
+      const int total = a.E * RT;
+      int u = a.sched != nullptr ? atomicAdd(a.sched, 1) : (int)blockIdx.x;
+      while (go && u < total) {
         const int e = u / RT, rt = u % RT;
         const int r0 = a.offsets[e], n = min(a.offsets[e + 1], a.R) - r0;
         const uint8_t* wsrc = a.wblob + (size_t)e * a.blob_stride + (size_t)rt * KB * Blob::kBytes;
@@ -616,6 +629,10 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_grouped_kernel(const
             go = false;
             break;
           }
+          info[4 * xb + 0] = e;
+          info[4 * xb + 1] = rt;
+          info[4 * xb + 2] = r0 + c0;
+          info[4 * xb + 3] = rows;
           mbar_arrive_expect_tx(&xfull[xb], (uint32_t)(rows * (a.ldx16 * 2 + a.ldxs * 4)));
           bulk_g2s(xs + xb * xbytes, a.x16 + (size_t)(r0 + c0) * a.ldx16,
                    (uint32_t)(rows * a.ldx16 * 2), &xfull[xb]);
@@ -639,12 +656,32 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_grouped_kernel(const
             }
           }
         }
+        if (go) u = a.sched != nullptr ? atomicAdd(a.sched, 1) : u + (int)gridDim.x;
+      }
+      // Sentinel sub-unit: the consumers leave their loop on expert -1.
+      if (go) {
+        const int xb = sub & 1;
+        if (sub < 2 || mbar_wait(&xempty[xb], ((sub >> 1) - 1) & 1, a.status,
+                                 kStatusGemmLoadTimeout, abort_flag)) {
+          info[4 * xb] = -1;
+          mbar_arrive(&xfull[xb]);
+          ++sub;
+        }
       }
       // Wait (bounded) for the copies still in flight before leaving.
       for (int g = max(0, issued - S); g < issued; ++g)
         mbar_wait(&full[g % S], (g / S) & 1, nullptr, 0, nullptr);
       for (int sb = max(0, sub - 2); sb < sub; ++sb)
         mbar_wait(&xfull[sb & 1], (sb >> 1) & 1, nullptr, 0, nullptr);
+      if (a.sched != nullptr) {
+        // Every producer has drawn its last unit before it counts itself
+        // done, so the last one may reset the counter for the next launch.
+        __threadfence();
+        if (atomicAdd(a.sched + 1, 1) == (int)gridDim.x - 1) {
+          atomicExch(a.sched, 0);
+          atomicExch(a.sched + 1, 0);
+        }
+      }
     }
     return;
   }
@@ -657,22 +694,25 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_grouped_kernel(const
   const int sw0 = ((c ^ ((r0w >> 1) & 3)) << 4), sw1 = ((c ^ ((r1w >> 1) & 3)) << 4);
   const uint32_t ring_u = smem_u32(ring);
   const uint32_t xs_u = smem_u32(xs);
-  int slot = 0, sub = 0;
+  int slot = 0;
   uint32_t phase = 0;
   bool ok = true;
-  for (int u = blockIdx.x; u < a.E * RT && ok; u += gridDim.x) {
-    const int e = u / RT, rt = u % RT;
-    const int r0 = a.offsets[e], n = min(a.offsets[e + 1], a.R) - r0;
-    for (int c0 = 0; c0 < n && ok; c0 += MP, ++sub) {
-      const int rows = min(MP, n - c0);
+  for (int sub = 0; ok; ++sub) {
+    {
       const int xb = sub & 1;
-      if (ok && !mbar_wait(&xfull[xb], (sub >> 1) & 1, a.status, kStatusGemmMmaTimeout,
-                           abort_flag))
+      if (!mbar_wait(&xfull[xb], (sub >> 1) & 1, a.status, kStatusGemmMmaTimeout, abort_flag))
         ok = false;
+      // A failed wait leaves the info unread: the barrier section below
+      // then ends the loop for every warp (abort flag set).
+      const int e = ok ? info[4 * xb] : -1;
+      const int rt = ok ? info[4 * xb + 1] : 0;
+      const int row0 = ok ? info[4 * xb + 2] : 0;
+      const int rows = (ok && e >= 0) ? info[4 * xb + 3] : 0;
+      const bool work = ok && e >= 0;
       const uint32_t xbase = xs_u + xb * xbytes;
       const float* cs = xsm + xb * (sbytes / 4);
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int st = 0; st < spt && ok; ++st) {
+      for (int st = 0; st < spt && work && ok; ++st) {
         const int cur = slot;
         const uint32_t ph = phase;
         if (++slot == S) {
@@ -745,7 +785,8 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_grouped_kernel(const
       // Every consumer warp reaches these barriers for every sub-unit, also
       // after a failed wait; the abort decision is uniform (snapshot).
       named_bar_sync(1, kCons);  // previous epilogue done with red / tile
-      if (tid == 0) *s_abort = *abort_flag;
+      // 1: abort, 2: sentinel (no more units); the same for every warp.
+      if (tid == 0) *s_abort = *abort_flag ? 1 : (e < 0 ? 2 : 0);
       if (par == 1) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) red[(rg * 32 + lane) * 4 + q] = acc[q];
@@ -770,7 +811,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_grouped_kernel(const
           const int jj = idx & 63, m = idx >> 6;
           const float gt = tile[(2 * jj) * (MP + 1) + m];
           const float up = tile[(2 * jj + 1) * (MP + 1) + m];
-          const int row = r0 + c0 + m;
+          const int row = row0 + m;
           __nv_bfloat16* orow = a.out_rows != nullptr
                                     ? reinterpret_cast<__nv_bfloat16*>(a.out_rows[row])
                                     : a.out + (size_t)row * a.ldo;
@@ -779,7 +820,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) w4a16_gemv_grouped_kernel(const
       } else {
         for (int idx = tid; idx < 16 * rows; idx += kCons) {
           const int r8 = (idx & 15) * 8, m = idx >> 4;
-          const int row = r0 + c0 + m;
+          const int row = row0 + m;
           __nv_bfloat16* orow = a.out_rows != nullptr
                                     ? reinterpret_cast<__nv_bfloat16*>(a.out_rows[row])
                                     : a.out + (size_t)row * a.ldo;
@@ -951,7 +992,8 @@ static void gvg_launch(const GvgArgs& a, int grid, int smem, cudaStream_t stream
 void w4a16_gemv_grouped(torch::Tensor x16, torch::Tensor xsum, torch::Tensor wblob,
                         torch::Tensor out, int64_t N, int64_t epilogue, torch::Tensor offsets,
                         int64_t num_groups, torch::Tensor status,
-                        c10::optional<torch::Tensor> out_rows) {
+                        c10::optional<torch::Tensor> out_rows,
+                        c10::optional<torch::Tensor> sched) {
   const int K = (int)(x16.size(1) - 8);
   TORCH_CHECK(K % 128 == 0 && N % 128 == 0, "K and N must be multiples of 128");
   TORCH_CHECK(epilogue == kGvEpiStore || epilogue == kGvEpiSilu, "store or SiLU epilogue");
@@ -974,6 +1016,11 @@ void w4a16_gemv_grouped(torch::Tensor x16, torch::Tensor xsum, torch::Tensor wbl
                    ? reinterpret_cast<const long long*>(out_rows->data_ptr<int64_t>())
                    : nullptr;
   a.status = status.data_ptr<int>();
+  if (sched.has_value()) {
+    TORCH_CHECK(sched->is_cuda() && sched->scalar_type() == at::kInt && sched->numel() >= 2,
+                "sched must be a cuda int32 tensor of 2 zeros");
+    a.sched = sched->data_ptr<int>();
+  }
   a.E = (int)num_groups;
   a.N = (int)N;
   a.K = K;

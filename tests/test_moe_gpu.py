@@ -97,11 +97,14 @@ def test_grouped_gemm_large_groups():
     _grouped_case(len(rows), rows, 256, 512, 128, ops.EPI_STORE, seed=3)
 
 
+@pytest.mark.parametrize("dynamic", [False, True])
 @pytest.mark.parametrize("rows", [[3, 0, 1, 7, 0, 0, 12, 2], [1, 1, 1, 1], [0, 0, 20, 0]])
 @pytest.mark.parametrize("epi", [ops.EPI_STORE, ops.EPI_SILU])
-def test_grouped_small_m(rows, epi):
+def test_grouped_small_m(rows, epi, dynamic):
     """Grouped small-M kernel on prepared activations (fp16, scaled, with
-    offset corrections), including experts with more than 8 rows."""
+    offset corrections), including experts with more than 8 rows; static
+    and dynamic (atomic counter) unit order.  The dynamic counter is run
+    twice to check that it resets itself."""
     g = torch.Generator().manual_seed(sum(rows) + epi)
     G, N, K = len(rows), 512, 768
     ws = [Int4Weight.random(N, K, 0.05, 128, generator=g) for _ in range(G)]
@@ -114,9 +117,14 @@ def test_grouped_small_m(rows, epi):
     inter = epi == ops.EPI_SILU
     blob = torch.cat([w.to(DEV).blob(interleave_gate_up=inter) for w in ws])
     x16, xs = ops.moe_prep_fp16(x.to(DEV), M)
-    out = ops.w4a16_gemv_grouped(x16, xs, blob, N, epi,
-                                 torch.tensor(offs, dtype=torch.int32, device=DEV), G)
+    sched = torch.zeros(2, dtype=torch.int32, device=DEV) if dynamic else None
+    for _ in range(2 if dynamic else 1):
+        out = ops.w4a16_gemv_grouped(x16, xs, blob, N, epi,
+                                     torch.tensor(offs, dtype=torch.int32, device=DEV), G,
+                                     sched=sched)
     torch.cuda.synchronize()
+    if dynamic:
+        assert sched.tolist() == [0, 0]
     assert ops.read_status(DEV) == 0
     out = out.float().cpu()
     for e in range(G):
