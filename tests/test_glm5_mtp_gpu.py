@@ -1,7 +1,12 @@
 """GLM-5 MTP drafting on the GPU kernels: the head's ragged catch-up
 forward and chain steps run the MLA / DSA / MoE kernels on its own paged
 KV; speculative decoding with it reproduces greedy decoding (up to
-near-tied argmaxes between the verify and decode kernels)."""
+near-tied argmaxes between the verify and decode kernels).  The index top-k
+covers the whole context here: near-tied indexer scores would otherwise
+select different positions in the verify and decode kernels and the two
+greedy runs would part for that reason alone."""
+import dataclasses
+
 import pytest
 import torch
 
@@ -24,7 +29,7 @@ def _agree(a, b):
 
 
 def test_mtp_spec_matches_greedy_on_gpu():
-    cfg = get_config("tiny-glm5")
+    cfg = dataclasses.replace(get_config("tiny-glm5"), index_topk=2048)
     target = GLM5Model(cfg, "cuda").init_random(4, std=0.05, gen_device="cpu")
     target.allocate_kv(128)
     mtp = GLM5MTP(target).init_random(11, std=0.05, gen_device="cpu")
