@@ -66,6 +66,11 @@ class GLM5Model(MLAModel):
     def __init__(self, cfg, device, **kw):
         super().__init__(cfg, device, **kw)
         assert cfg.is_dsa and cfg.index_head_dim == 128
+        if not cfg.layer_has_indexer(self.layer_start):
+            # An IndexShare layer reuses the selection of the indexer layer
+            # before it, which a stage that starts with it does not have.
+            raise ValueError(f"a GLM-5 stage must start at an indexer layer, not layer "
+                             f"{self.layer_start} (indexer_types 'shared')")
         self.hi = cfg.index_n_heads
         # local layer -> slot in the index-key cache (-1: IndexShare layer)
         self.idx_slot = []
