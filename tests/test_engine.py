@@ -138,7 +138,8 @@ def test_sliding_window_generation_frees_old_blocks():
     assert m.kv.allocator.num_free == m.kv.num_blocks
 
 
-@pytest.mark.parametrize("preset", ["tiny-glm5", "tiny-gemma4", "tiny-mla", "tiny-moe"])
+@pytest.mark.parametrize("preset", ["tiny-glm5", "tiny-gemma4", "tiny-gemma4-moe", "tiny-mla",
+                                    "tiny-moe"])
 def test_builder_serves_every_model_family(preset):
     """The builder picks the model class from the config and the engine
     serves a request end to end (CPU oracle path)."""
@@ -151,3 +152,21 @@ def test_builder_serves_every_model_family(preset):
     e = b.build()
     out = _run(e, [GenerationTask("t", "", max_tokens=3, prompt_ids=list(range(3, 23)))])
     assert out["t"][-1].is_final and len(_ids(out["t"])) == 3
+
+
+def test_builder_spec_mtp_equals_plain():
+    """``--spec mtp`` through the builder: GLM-5 with its MTP head drafting
+    gives the same greedy tokens as plain decoding."""
+    from cascadia_b200.types import GenerationTask
+
+    outs = []
+    for spec in (None, "mtp"):
+        b = LLMBuilder("tiny-glm5", device="cpu", kv_blocks=128, max_model_len=256,
+                       max_running=4, spec=spec, spec_k=2)
+        n = get_config("tiny-glm5").num_layers
+        for _ in b.load(ShardSpec("tiny-glm5", 0, n, n, device="cpu")):
+            pass
+        e = b.build()
+        out = _run(e, [GenerationTask("t", "", max_tokens=6, prompt_ids=list(range(3, 23)))])
+        outs.append(_ids(out["t"]))
+    assert outs[0] == outs[1] and len(outs[0]) == 6
