@@ -187,12 +187,14 @@ class LLMEngine(Engine):
         seqs = [s for s, _, _ in work]
         toks = self._run_model(batch, ids, seqs)
         if self.spec == "mtp" and self.pipeline is None:
-            # Queue every prompt row for the MTP head with the token after it.
+            # Queue every prompt row of a greedy sequence (the ones that
+            # decode speculatively) for the MTP head, with the token after it.
             off = 0
             for (s, st, n), t in zip(work, toks):
-                p = s.prompt_ids
-                nxt = list(p[st + 1:st + n]) + [p[st + n] if st + n < len(p) else int(t)]
-                self.drafter.observe(s.seq_id, st, nxt, self._last_hidden[off:off + n])
+                if s.task.temperature <= 0 and not self._has_penalty(s):
+                    p = s.prompt_ids
+                    nxt = list(p[st + 1:st + n]) + [p[st + n] if st + n < len(p) else int(t)]
+                    self.drafter.observe(s.seq_id, st, nxt, self._last_hidden[off:off + n])
                 off += n
         for s, t in zip(seqs, toks):
             if not s.in_prefill:

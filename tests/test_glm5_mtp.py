@@ -171,6 +171,29 @@ def test_engine_mtp_mode_equals_plain_greedy():
     assert mtp.kv.allocator.num_free == mtp.kv.allocator.num_blocks
 
 
+def test_engine_mtp_with_a_sampled_request():
+    """A sampled request beside greedy ones decodes normally; the head never
+    holds rows for it."""
+    from cascadia_b200.engine.llm import LLMEngine
+    from cascadia_b200.types import GenerationTask
+
+    cfg, target, mtp = _pair(seed=4)
+    prompts = _prompts(cfg, 2, [8, 15])
+    e = LLMEngine(target, max_model_len=128, spec="mtp", spec_k=2, mtp_head=mtp)
+    e.submit(GenerationTask("g", "", max_tokens=6, prompt_ids=prompts[0]))
+    e.submit(GenerationTask("s", "", max_tokens=6, prompt_ids=prompts[1], temperature=0.8))
+    fin = set()
+    for _ in range(60):
+        for tid, c in e.step():
+            if c.is_final:
+                fin.add(tid)
+        assert "s" not in e.drafter.queue
+        if len(fin) == 2:
+            break
+    assert fin == {"g", "s"}
+    assert not e.drafter.queue and mtp.kv.allocator.num_free == mtp.kv.allocator.num_blocks
+
+
 def test_engine_mtp_refuses_prefix_cache():
     from cascadia_b200.engine.llm import LLMEngine
     from cascadia_b200.engine.base import InvalidConfig
