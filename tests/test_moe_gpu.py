@@ -139,6 +139,41 @@ def test_grouped_small_m(rows, epi, dynamic):
         assert err <= 0.01 * y.abs().max().item() + 1e-2, (e, err)
 
 
+@pytest.mark.parametrize("epi", [ops.EPI_STORE, ops.EPI_SILU])
+def test_grouped_small_m_many_units(epi):
+    """The decode down-projection shape (K 512: four X buffers in flight)
+    with many experts of 0 to 3 rows, so every CTA runs through several
+    units and the X ring wraps; dynamic unit order."""
+    g = torch.Generator().manual_seed(11 + epi)
+    G, N, K = 64, 2048, 512
+    rows = torch.randint(0, 4, (G,), generator=g).tolist()
+    ws = [Int4Weight.random(N, K, 0.05, 128, generator=g) for _ in range(G)]
+    offs = [0]
+    for r in rows:
+        offs.append(offs[-1] + r)
+    M = offs[-1]
+    x = (torch.randn(M, K, generator=g) * 0.5).to(torch.bfloat16)
+    inter = epi == ops.EPI_SILU
+    blob = torch.cat([w.to(DEV).blob(interleave_gate_up=inter) for w in ws])
+    x16, xs = ops.moe_prep_fp16(x.to(DEV), M)
+    sched = torch.zeros(2, dtype=torch.int32, device=DEV)
+    out = ops.w4a16_gemv_grouped(x16, xs, blob, N, epi,
+                                 torch.tensor(offs, dtype=torch.int32, device=DEV), G,
+                                 sched=sched)
+    torch.cuda.synchronize()
+    assert ops.read_status(DEV) == 0 and sched.tolist() == [0, 0]
+    out = out.float().cpu()
+    for e in range(G):
+        if rows[e] == 0:
+            continue
+        wq = (ws[e].unpack().float() - 8.0) * ws[e].scales.float().repeat_interleave(128, dim=1)
+        y = x[offs[e]:offs[e + 1]].float() @ wq.t()
+        if inter:
+            y = ref.silu_mul(y[:, :N // 2], y[:, N // 2:])
+        err = (out[offs[e]:offs[e + 1]] - y).abs().max().item()
+        assert err <= 0.01 * y.abs().max().item() + 1e-2, (e, err)
+
+
 def test_combine():
     g = torch.Generator().manual_seed(4)
     T, k, H = 33, 4, 384
