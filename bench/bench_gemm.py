@@ -35,13 +35,15 @@ def main():
     p.add_argument("--shapes", default="qkv,o,gate_up,down,lm_head")
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--copies", type=int, default=4, help="weight copies rotated per shape")
-    p.add_argument("--splits", type=int, default=0)
+    p.add_argument("--splits", type=int, default=0,
+                   help="0 auto; > 0 split-K kernel with that split; -1 stream kernel; "
+                        "-2 small-M kernel")
     p.add_argument("--graph", type=int, default=1, help="time a CUDA graph of the reps launches")
     p.add_argument("--trace", action="store_true",
                    help="tcgen05 path: print per-CTA phase times of one launch")
     a = p.parse_args()
     dev = torch.device("cuda", 0)
-    peak = 6543.4
+    peak = 6432.4
     pk = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
                       "MEASURED_PEAKS.json")
     if os.path.exists(pk):
@@ -99,33 +101,53 @@ def main():
         plan = ops.w4a16_plan(a.m, n, k, a.splits)
         res[name] = {"us": round(med, 2), "GBps": round(nbytes / med / 1e3, 1),
                      "frac_of_measured_hbm": round(nbytes / med / 1e3 / peak, 3),
-                     "plan[MT,splits,kbps,tt,rt]": plan,
-                     "path": "small-M" if (a.splits <= 0 and a.m <= int(os.environ.get(
-                         "CASCADIA_GEMV_MAX_M", "8"))) else "tcgen05"}
+                     "plan": plan,
+                     "path": {0: "split-K tcgen05", 1: "stream tcgen05",
+                              2: "small-M"}[plan[0]]}
         print(name, json.dumps(res[name]), flush=True)
-        if a.trace:
+        if a.trace and plan[0] in (0, 1):
             buf = torch.zeros(1 << 20, dtype=torch.int64, device=dev)
             ops.ext().w4a16_set_trace(buf)
             run(0)
             torch.cuda.synchronize()
             ops.ext().w4a16_set_trace(None)
-            mt, sp, _, tt, rt = plan
-            n = rt * max(sp, 1) * tt
-            tr = buf[:n * 8].view(n, 8).double().cpu()
+            if plan[0] == 0:
+                _, mt, sp, _, tt, rt = plan
+                n = rt * max(sp, 1) * tt
+                names = ["setup", "first_w", "issued", "last_mma", "acc_ready", "partials",
+                         "end"]
+            else:
+                n = plan[2]
+                names = ["tmem", "first_stage", "first_mma", "last_mma", "unit0_out",
+                         "last_unit_out", "end"]
+            width = 8 if plan[0] == 0 else 24
+            tr = buf[:n * width].view(n, width).double().cpu()
             t0 = tr[:, 0].min()
             rel = tr - tr[:, :1]
-            names = ["setup", "first_w", "issued", "last_mma", "acc_ready", "partials", "end"]
-            med = {nm: round(float(rel[:, i + 1].median()) / 1000, 2) for i, nm in enumerate(names)}
-            print("  trace (us from CTA start, median over CTAs):", json.dumps(med))
             print("  CTA start skew us: max", round(float(tr[:, 0].max() - t0) / 1000, 2),
                   "kernel span us", round(float(tr[:, 7].max() - t0) / 1000, 2), flush=True)
             for i, nm in enumerate(names):
                 col = rel[:, i + 1] / 1000
                 q = torch.quantile(col, torch.tensor([0.1, 0.5, 0.9, 1.0], dtype=col.dtype))
-                print(f"    {nm:10s} p10/p50/p90/max us:", [round(float(v), 2) for v in q])
-            slow = int(torch.argmax(rel[:, 7]))
-            print("    slowest CTA", slow, "(rt, split, tt) =", (slow % rt, (slow // rt) % max(sp, 1),
-                  slow // (rt * max(sp, 1))), [round(float(v) / 1000, 2) for v in rel[slow, 1:]])
+                print(f"    {nm:14s} p10/p50/p90/max us:", [round(float(v), 2) for v in q])
+            if width == 24:  # time spent waiting, per role (medians over CTAs, us)
+                waits = ["mma_wait_stage", "mma_wait_a", "mma_wait_acc", "deq_wait_stage",
+                         "deq_wait_aempty", "deq_work", "prod_wait_empty"]
+                print("    waits (kcycles p50/max):", {w: (round(float(tr[:, 8 + i].median()) / 1000, 1),
+                                                             round(float(tr[:, 8 + i].max()) / 1000, 1))
+                                                          for i, w in enumerate(waits)})
+                jt = buf[4096:4096 + 256].view(64, 4).double().cpu()
+                base = jt[:, 0].min()
+                print("    CTA 0 per job (clock cycles from first A ready): A ready | issue start | "
+                      "issue end | buffer seen free by job+4's group")
+                for jj in range(0, 40):
+                    r = (jt[jj] - base).tolist()
+                    nxt = (jt[jj + 4, 3] - base).item() if jj + 4 < 64 else float('nan')
+                    print(f"      job {jj:2d}: {r[0]:8.0f} {r[1]:8.0f} {r[2]:8.0f}   free seen {nxt:8.0f}")
+                print("    issuer 0 clock cycles (p50): 8-MMA issue", float(tr[:, 16].median()),
+                      "job commit", float(tr[:, 17].median()), "step commits",
+                      float(tr[:, 18].median()), "loop total", float(tr[:, 19].median()),
+                      "fence", float(tr[:, 20].median()), "step_info", float(tr[:, 21].median()))
     print("status", ops.read_status(dev))
 
 

@@ -103,6 +103,14 @@ class TPGroup:
         return out.view((self.size,) + tuple(x.shape))
 
 
+def vocab_shard_rows(vocab_size: int, tp: int) -> int:
+    """LM-head rows per rank at TP=`tp`: ceil(V / tp) rounded up to the
+    GEMM's 128-row tile (e.g. 128256 -> 64128 / 32128 / 16128 at TP 2/4/8)."""
+    if tp == 1:
+        return vocab_size
+    return -(-vocab_size // (tp * 128)) * 128
+
+
 def _layer_generator(seed: int, layer: int, device) -> torch.Generator:
     g = torch.Generator(device=device)
     g.manual_seed(seed * 1000003 + layer * 7919 + 17)
@@ -132,7 +140,12 @@ class LlamaModel:
         self.hkv = cfg.num_kv_heads // t
         self.d = cfg.head_dim
         self.inter = cfg.intermediate_size // t
-        self.vocab_shard = cfg.vocab_size // t if cfg.vocab_size % t == 0 else cfg.vocab_size
+        # Vocab-parallel LM head: every rank holds `vocab_shard` rows, a
+        # multiple of 128 (the GEMM's row tile); rows at or past the true
+        # vocabulary are zero padding that argmax and full_logits skip.
+        self.vocab_shard = vocab_shard_rows(cfg.vocab_size, t)
+        self.vocab_valid = max(0, min(self.vocab_shard,
+                                      cfg.vocab_size - self.tp.rank * self.vocab_shard))
         self.layers: List[LayerWeights] = []
         self.embed: Optional[torch.Tensor] = None
         self.final_norm: Optional[torch.Tensor] = None
@@ -186,11 +199,23 @@ class LlamaModel:
         return self
 
     def _vocab_shard(self, w: Int4Weight) -> Int4Weight:
+        """This rank's `vocab_shard` LM-head rows; rows past the vocabulary
+        are zero (nibble 8 with scale 0), so their logits are exactly 0 and
+        the argmax never looks at them."""
         t, r = self.tp.size, self.tp.rank
-        if t == 1 or self.cfg.vocab_size % t:
+        if t == 1:
             return w
-        vs = self.cfg.vocab_size // t
-        return w.rows(r * vs, (r + 1) * vs)
+        vs, valid = self.vocab_shard, self.vocab_valid
+        part = w.rows(r * vs, r * vs + valid)
+        if valid == vs:
+            return part
+        pad = vs - valid
+        dev = w.packed.device
+        zeros = Int4Weight(torch.full((pad, w.packed.shape[1]), -2004318072, dtype=torch.int32,
+                                      device=dev),  # 0x88888888: eight nibbles of value 0
+                           torch.zeros((pad, w.scales.shape[1]), dtype=w.scales.dtype, device=dev),
+                           w.group_size)
+        return Int4Weight.cat_rows([part, zeros]) if valid else zeros
 
     def _shard_layer(self, q, k, v, o, gate, up, down, in_norm, post_norm) -> LayerWeights:
         t, r, d = self.tp.size, self.tp.rank, self.cfg.head_dim
@@ -364,22 +389,27 @@ class LlamaModel:
         """Argmax over the full vocabulary (merging vocab shards)."""
         B = logits.shape[0]
         if self.device.type != "cuda":
-            return ref.argmax(logits)
+            return ref.argmax(self.full_logits(logits))
         idx = torch.empty(B, dtype=torch.int32, device=self.device)
-        if self.tp.size == 1 or self.vocab_shard == self.cfg.vocab_size:
+        if self.tp.size == 1:
             return ops.argmax(logits, idx)
         val = torch.empty(B, dtype=torch.float32, device=self.device)
-        ops.argmax(logits, idx, val, idx_offset=self.tp.rank * self.vocab_shard)
+        # Only the real vocabulary rows of this shard (a view with the same
+        # row stride): padded rows are never candidates.
+        ops.argmax(logits[:, :self.vocab_valid], idx, val,
+                   idx_offset=self.tp.rank * self.vocab_shard)
         pair = torch.stack([val, idx.float()], dim=1)  # exact for idx < 2^24
         allp = self.tp.all_gather_rows(pair)  # [tp, B, 2]
         best = torch.argmax(allp[:, :, 0], dim=0)  # first (lowest rank) wins ties
         return allp[best, torch.arange(B, device=self.device), 1].to(torch.int32)
 
     def full_logits(self, logits: torch.Tensor) -> torch.Tensor:
-        if self.tp.size == 1 or self.vocab_shard == self.cfg.vocab_size:
+        """[B, vocab_size] logits from every rank's (padded) shard."""
+        if self.tp.size == 1:
             return logits
-        allp = self.tp.all_gather_rows(logits)  # [tp, B, V/tp]
-        return allp.permute(1, 0, 2).reshape(logits.shape[0], -1)
+        allp = self.tp.all_gather_rows(logits.contiguous())  # [tp, B, vocab_shard]
+        full = allp.permute(1, 0, 2).reshape(logits.shape[0], -1)
+        return full[:, :self.cfg.vocab_size]
 
 
 @dataclass

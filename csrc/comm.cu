@@ -20,8 +20,13 @@
 // finished reading b.
 //
 // Waits are bounded (kWaitTimeoutNs); on expiry the kernel records
-// kStatusPeerTimeout in the status word and returns without touching its
-// outputs' correctness guarantees (the host aborts the batch).
+// kStatusPeerTimeout in the status word and leaves its outputs unwritten.
+// The engine reads the status word after every step and fails the batch
+// (engine.base.BatchAborted) when it is non-zero.
+//
+// Launched with programmatic dependent launch: the CTAs become resident
+// while the GEMM that writes the partials drains, and wait for it
+// (griddepcontrol.wait) before signalling the peers.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -72,6 +77,8 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_kernel(const ArArgs a) 
   __shared__ int s_epoch;
   __shared__ int s_ok;
   __shared__ float red[32];
+  grid_dep_launch();
+  grid_dep_wait();  // the partials, the residual and the epoch of the previous launch
   if (threadIdx.x == 0) {
     s_epoch = *reinterpret_cast<volatile int*>(a.epoch) + 1;
     s_ok = 1;
@@ -213,8 +220,8 @@ void ar_rmsnorm(torch::Tensor buf_ptrs, int64_t buf_offset_bytes, torch::Tensor 
   a.eps = (float)eps;
   // Every CTA must be resident at once (they wait on peers): at most one per SM.
   const int grid = (int)std::min<int64_t>(M, std::min(num_sms(), 128));
-  ar_rmsnorm_kernel<<<grid, kArThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
-  CB_CUDA_CHECK(cudaGetLastError());
+  launch_kernel(ar_rmsnorm_kernel, dim3(grid), dim3(kArThreads), 0,
+                at::cuda::getCurrentCUDAStream(), a);
 }
 
 }  // namespace cb

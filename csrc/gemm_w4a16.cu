@@ -37,8 +37,8 @@
 #include <cstdlib>
 #include <mutex>
 
+#include "gemm_stream.h"
 #include "gemv_w4a16.h"
-#include <unordered_map>
 
 #include "common.cuh"
 #include "host_utils.h"
@@ -106,13 +106,6 @@ struct GemmArgs {
   int M, N, K;
   int ldo, ldr;
   int kb_per_split, splits;
-  // Diagnostics only (CASCADIA_GEMM_DIAG): bit 0 skips the dequant math,
-  // bit 1 skips issuing the MMAs, bit 2 skips the activation loads and bit 3
-  // the dequant warps' shared-memory reads (persistent kernel).  Results are wrong in those modes; the
-  // pipeline, barriers and memory traffic are unchanged.
-  int diag;
-  // Persistent (stream-K) kernel only.
-  int row_tiles, units, ub, ur, max_contrib;
   // Grouped mode (MoE experts): blockIdx.z = expert * group_tiles + tile; the
   // expert's token rows are [group_offsets[e], group_offsets[e + 1]) of X and
   // Y, its weights start at wblob + e * group_blob_stride.
@@ -294,7 +287,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d_tm = tmem_acc + who * MT;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          if (args.diag & 2) break;
           const uint64_t db = umma_desc_sw128(x_addr + (kk >> 2) * (MT * 128) + (kk & 3) * 32);
           mma_bf16_ts(d_tm, a_tm + kk * 8, db, kIdesc, (it < NI && kk == 0) ? 0u : 1u);
         }
@@ -351,7 +343,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        if (args.diag & 1) break;
         const uint32_t words[4] = {p[c].x, p[c].y, p[c].z, p[c].w};
         uint32_t o[16];
 #pragma unroll
@@ -572,377 +563,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// ------------------------------------------------------------------------
-// Persistent stream-K variant (decode, MT <= 64).
-//
-// Measured on B200: a single SM streams bulk copies at a rate set by the
-// number of copies, not by bytes in flight (8.4 KiB copies top out near
-// 3.5 TB/s over 148 SMs at any ring depth, >= 16.9 KiB copies reach the HBM
-// peak).  The producer therefore fetches the weight blobs of two consecutive
-// k-blocks (contiguous in the blob layout) with ONE bulk copy into a stage
-// pair; dequantisation and MMA still work per k-block.
-//
-// One CTA per SM; the (tile, k-block) units of the whole GEMM are split into
-// equal contiguous ranges, one per CTA, so there is no wave quantisation and
-// the TMA ring streams across tile boundaries without refilling.  The MMA
-// warp alternates between two TMEM accumulators (one per tile segment), four
-// dedicated epilogue warps drain the previous segment while the next one
-// streams.  A tile split across CTAs reduces through the fp32 workspace in
-// contributor order (deterministic); the last contributor applies the fused
-// epilogue.  Gate/up rows alternate (gate_j, up_j), so SiLU(gate) * up is one
-// lane shuffle.
-constexpr int kEpiWarps = 4;
-constexpr int kPThreads = 64 + kDequantThreads + kEpiWarps * 32;
-
-template <int MT, int GS>
-struct PairPlan {
-  static constexpr int kBlob = BlobInfo<GS>::kBytes;
-  static constexpr int kUnitX = 2 * MT * 128;                      // X of one k-block
-  static constexpr int kXOff = (2 * kBlob + 1023) / 1024 * 1024;  // X after both blobs
-  static constexpr int kPair = kXOff + 2 * kUnitX;
-  static constexpr int kNPraw = (210 * 1024) / kPair / 2 * 2;      // even
-  static constexpr int kNP = kNPraw > 8 ? 8 : kNPraw;
-  static constexpr int kSL = 2 * kNP;                              // k-block slots (mult. of 4)
-  static constexpr int kBarOff = kNP * kPair;
-  static constexpr int kTotal = kBarOff + 1024 + 1024;
-  static_assert(kNP >= 2 && kSL % 4 == 0, "need an even number of stage pairs");
-};
-
-__device__ __forceinline__ int unit_begin(int c, int ub, int ur) { return c * ub + min(c, ur); }
-__device__ __forceinline__ int unit_owner(int u, int ub, int ur) {
-  const int t = ur * (ub + 1);
-  return u < t ? u / (ub + 1) : ur + (u - t) / ub;
-}
-
-template <int MT, int GS, int EPI>
-__device__ __forceinline__ void persist_final(const GemmArgs& args, const float (&v)[MT], int rt,
-                                              int row, int m_base, int lane) {
-  const int n = rt * 128 + row;
-  if constexpr (EPI == kEpiSilu) {
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      const float up = __shfl_xor_sync(0xffffffffu, v[m], 1);
-      const int gm = m_base + m;
-      if ((lane & 1) == 0 && gm < args.M) {
-        const float g = v[m];
-        args.out[(size_t)gm * args.ldo + rt * 64 + (row >> 1)] =
-            __float2bfloat16(g / (1.f + __expf(-g)) * up);
-      }
-    }
-  } else {
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      const int gm = m_base + m;
-      if (gm < args.M) {
-        float y = v[m];
-        if constexpr (EPI == kEpiResid)
-          y += __bfloat162float(args.residual[(size_t)gm * args.ldr + n]);
-        args.out[(size_t)gm * args.ldo + n] = __float2bfloat16(y);
-      }
-    }
-  }
-}
-
-template <int MT, int GS, int EPI>
-__global__ void __launch_bounds__(kPThreads, 1)
-    w4a16_persistent_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs args) {
-  using Plan = PairPlan<MT, GS>;
-  constexpr int NP = Plan::kNP;     // stage pairs (one bulk copy each)
-  constexpr int SL = Plan::kSL;     // k-block slots
-  constexpr int R = SL / kGroups;   // rounds resident in the ring
-  constexpr int BLOB = BlobInfo<GS>::kBytes;
-  constexpr uint32_t kTmemCols = 512;
-  constexpr uint32_t kIdesc = umma_idesc_bf16(128, MT);
-  static_assert(MT <= 64, "persistent kernel is for decode token tiles");
-
-  // Synchronisation (per "round" of 4 units, one per dequant group):
-  //   full_l[p]        TMA landed W + X of the two units of stage pair p
-  //   full_a[g]        group g wrote its unit's A tile into TMEM (4 warps)
-  //   round_done[r%R]  one tcgen05.commit after the round's MMAs: the round's
-  //                    4 stages and 4 A buffers are free again (MMA completion
-  //                    implies the dequant warps finished reading them).
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
-  uint8_t* l_smem = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Plan::kBarOff);
-  uint64_t* full_l = bars;
-  uint64_t* round_done = bars + NP;
-  uint64_t* full_a = round_done + R;
-  uint64_t* acc_full = full_a + kGroups;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* epi_bar = acc_empty + 2;  // bounded sync of the 4 epilogue warps
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(epi_bar + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* is_last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
-
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
-  const int KB = args.K / 128;
-  const int cta = blockIdx.x;
-  const int u_begin = unit_begin(cta, args.ub, args.ur);
-  const int n_units = unit_begin(cta + 1, args.ub, args.ur) - u_begin;
-
-  if (tid == 0) {
-    for (int p = 0; p < NP; ++p) mbar_init(&full_l[p], 1);
-    for (int r = 0; r < R; ++r) mbar_init(&round_done[r], 1);
-    for (int g = 0; g < kGroups; ++g) mbar_init(&full_a[g], 4);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kEpiWarps);
-    }
-    mbar_init(epi_bar, kEpiWarps * 32);
-    *abort_flag = 0;
-    *is_last_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tmem_acc = tmem_base + kAccCol;  // two buffers of MT columns
-
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      prefetch_tmap(&tmap_x);
-      const bool skip_x = (args.diag & 4) != 0;
-      int issued = 0;
-      for (int j = 0; 2 * j < n_units; ++j) {
-        const int i0 = 2 * j;
-        const int nu = min(2, n_units - i0);  // units in this pair
-        const int p = j % NP;
-        const int rho = i0 / kGroups;
-        // A round (4 units = 2 pairs) frees both of its pairs at once.
-        if ((j & 1) == 0 && !mbar_wait(&round_done[rho % R], ((rho / R) & 1) ^ 1, args.status,
-                                       kStatusGemmLoadTimeout, abort_flag))
-          break;
-        uint8_t* st = l_smem + p * Plan::kPair;
-        const int u0 = u_begin + i0;
-        const int tile0 = u0 / KB, kb0 = u0 % KB;
-        const int rt0 = tile0 % args.row_tiles, tt0 = tile0 / args.row_tiles;
-        int tt1 = tt0, rt1 = rt0, kb1 = kb0;
-        if (nu == 2) {
-          const int u1 = u0 + 1;
-          const int tile1 = u1 / KB;
-          kb1 = u1 % KB;
-          rt1 = tile1 % args.row_tiles;
-          tt1 = tile1 / args.row_tiles;
-        }
-        const uint32_t xbytes = skip_x ? 0u : (uint32_t)(nu * Plan::kUnitX);
-        mbar_arrive_expect_tx(&full_l[p], nu * BLOB + xbytes);
-        const uint8_t* w0 = args.wblob + ((size_t)rt0 * KB + kb0) * BLOB;
-        if (nu == 2 && tt1 == tt0) {
-          bulk_g2s(st, w0, 2 * BLOB, &full_l[p]);  // both k-blocks, one copy
-        } else {
-          bulk_g2s(st, w0, BLOB, &full_l[p]);
-          if (nu == 2)
-            bulk_g2s(st + BLOB, args.wblob + ((size_t)rt1 * KB + kb1) * BLOB, BLOB, &full_l[p]);
-        }
-        if (!skip_x) {
-          uint8_t* x0 = st + Plan::kXOff;
-          tma_load_2d(x0, &tmap_x, kb0 * 128, tt0 * MT, &full_l[p]);
-          tma_load_2d(x0 + MT * 128, &tmap_x, kb0 * 128 + 64, tt0 * MT, &full_l[p]);
-          if (nu == 2) {
-            uint8_t* x1 = x0 + Plan::kUnitX;
-            tma_load_2d(x1, &tmap_x, kb1 * 128, tt1 * MT, &full_l[p]);
-            tma_load_2d(x1 + MT * 128, &tmap_x, kb1 * 128 + 64, tt1 * MT, &full_l[p]);
-          }
-        }
-        ++issued;
-      }
-      for (int jj = max(0, issued - NP); jj < issued; ++jj)
-        mbar_wait(&full_l[jj % NP], (jj / NP) & 1, nullptr, 0, nullptr);
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      int seg = 0;
-      bool ok = true;
-      for (int i = 0; i < n_units && ok; ++i) {
-        const int u = u_begin + i;
-        const int kb = u % KB;
-        const bool first = (i == 0) || (kb == 0);
-        const bool last = (i == n_units - 1) || (kb == KB - 1);
-        const int buf = seg & 1;
-        if (first) {
-          ok = mbar_wait(&acc_empty[buf], ((seg >> 1) & 1) ^ 1, args.status,
-                         kStatusGemmMmaTimeout, abort_flag);
-          if (!ok) break;
-        }
-        const int p = (i >> 1) % NP;
-        const int g = i % kGroups;
-        const int rho = i / kGroups;
-        if (!mbar_wait(&full_a[g], rho & 1, args.status, kStatusGemmMmaTimeout, abort_flag) ||
-            !mbar_wait(&full_l[p], ((i >> 1) / NP) & 1, args.status, kStatusGemmMmaTimeout,
-                       abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t a_tm = tmem_base + g * kACols;
-        const uint32_t x_addr =
-            smem_u32(l_smem + p * Plan::kPair + Plan::kXOff + (i & 1) * Plan::kUnitX);
-        const uint32_t d_tm = tmem_acc + buf * MT;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          if (args.diag & 2) break;
-          const uint64_t db = umma_desc_sw128(x_addr + (kk >> 2) * (MT * 128) + (kk & 3) * 32);
-          mma_bf16_ts(d_tm, a_tm + kk * 8, db, kIdesc, (first && kk == 0) ? 0u : 1u);
-        }
-        if (last) {
-          mma_commit(&acc_full[buf]);
-          ++seg;
-        }
-        if (g == kGroups - 1 || i == n_units - 1) mma_commit(&round_done[rho % R]);
-      }
-    }
-  } else if (warp < 2 + kDequantWarps) {
-    // ------------------------------------------------------------ dequant
-    const int t = tid - 64;
-    const int grp = t >> 7;
-    const int q = warp & 3;
-    const int r = q * 32 + lane;
-    const __nv_bfloat162 k136 = __floats2bfloat162_rn(136.0f, 136.0f);
-    const uint32_t l_base = smem_u32(l_smem);
-    const uint32_t a_tm = tmem_base + grp * kACols + ((uint32_t)(q * 32) << 16);
-    for (int it = grp; it < n_units; it += kGroups) {
-      const int pr = (it >> 1) % NP;
-      const int rho = it / kGroups;
-      if (!mbar_wait(&full_l[pr], ((it >> 1) / NP) & 1, args.status, kStatusGemmDequantTimeout,
-                     abort_flag))
-        break;
-      const uint32_t wb = l_base + pr * Plan::kPair + (it & 1) * BLOB;
-      uint4 p[4] = {};
-      __nv_bfloat162 s2[4] = {};
-      if (!(args.diag & 8)) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) p[c] = lds128(wb + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int si = GS == 128 ? r : r * (128 / GS) + (c * 32) / GS;
-          const uint16_t sraw = lds16(wb + BlobInfo<GS>::kPacked + si * 2);
-          s2[c] = __halves2bfloat162(__ushort_as_bfloat16(sraw), __ushort_as_bfloat16(sraw));
-        }
-      }
-      // The previous round's MMAs must be done with this group's A buffer.
-      if (rho >= 1 && !mbar_wait(&round_done[(rho - 1) % R], ((rho - 1) / R) & 1, args.status,
-                                 kStatusGemmDequantTimeout, abort_flag))
-        break;
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (args.diag & 1) break;
-        const uint32_t words[4] = {p[c].x, p[c].y, p[c].z, p[c].w};
-        uint32_t o[16];
-#pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-          const uint32_t w = words[wi];
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            uint32_t v = ((w >> (4 * h)) & 0x000F000Fu) | 0x43004300u;  // bf16 (128 + q)
-            __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
-            b = __hmul2(__hsub2(b, k136), s2[c]);                      // (q - 8) * scale
-            o[wi * 4 + h] = *reinterpret_cast<uint32_t*>(&b);
-          }
-        }
-        tmem_st16(a_tm + c * 16, o);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&full_a[grp]);
-    }
-  } else {
-    // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
-    const int et = tid - (64 + kDequantThreads);  // 0..127
-    int seg = 0;
-    uint32_t epi_phase = 0;
-    bool epi_ok = true;
-    // All 128 epilogue threads arrive, then wait (bounded) for the phase.
-    auto epi_sync = [&]() {
-      mbar_arrive(epi_bar);
-      if (!mbar_wait(epi_bar, epi_phase & 1, args.status, kStatusGemmEpiTimeout, abort_flag))
-        epi_ok = false;
-      ++epi_phase;
-    };
-    for (int i = 0; i < n_units;) {
-      const int u = u_begin + i;
-      const int tile = u / KB;
-      const int kb0 = u % KB;
-      const int len = min(KB - kb0, n_units - i);
-      const int buf = seg & 1;
-      const int rt = tile % args.row_tiles, tt = tile / args.row_tiles;
-      if (!mbar_wait(&acc_full[buf], (seg >> 1) & 1, args.status, kStatusGemmEpiTimeout,
-                     abort_flag))
-        break;
-      tc_fence_after();
-      float v[MT];
-      const uint32_t lane_addr = tmem_acc + buf * MT + ((uint32_t)(q * 32) << 16);
-#pragma unroll
-      for (int c0 = 0; c0 < MT; c0 += 16) {
-        float u16[16];
-        tmem_ld16(lane_addr + c0, u16);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) v[c0 + k] = u16[k];
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
-      const bool whole = (kb0 == 0 && len == KB);
-      if (whole) {
-        persist_final<MT, GS, EPI>(args, v, rt, row, tt * MT, lane);
-      } else {
-        const int c_first = unit_owner(tile * KB, args.ub, args.ur);
-        const int c_last = unit_owner(tile * KB + KB - 1, args.ub, args.ur);
-        const int slot = cta - c_first;
-        const int ncontrib = c_last - c_first + 1;
-        float* wsp = args.ws + ((size_t)tile * args.max_contrib) * MT * 128;
-#pragma unroll
-        for (int m = 0; m < MT; ++m) wsp[((size_t)slot * MT + m) * 128 + row] = v[m];
-        __threadfence();
-        epi_sync();
-        if (et == 0) {
-          const int old = atomicAdd(&args.counters[tile], 1);
-          const int lst = (old == ncontrib - 1) ? 1 : 0;
-          if (lst) args.counters[tile] = 0;
-          *is_last_flag = lst;
-        }
-        epi_sync();
-        const bool lst = *is_last_flag != 0;
-        epi_sync();  // flag read before the next segment rewrites it
-        if (!epi_ok) break;
-        if (lst) {
-          __threadfence();
-#pragma unroll
-          for (int m = 0; m < MT; ++m) {
-            float acc = 0.f;
-            for (int j = 0; j < ncontrib; ++j) acc += __ldcg(&wsp[((size_t)j * MT + m) * 128 + row]);
-            v[m] = acc;
-          }
-          persist_final<MT, GS, EPI>(args, v, rt, row, tt * MT, lane);
-        }
-      }
-      ++seg;
-      i += len;
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
-  }
-}
-
 // ---------------------------------------------------------------- host side
 
 template <int MT, int GS, int EPI>
@@ -961,29 +581,6 @@ void launch_w4a16(const CUtensorMap& tmap, const GemmArgs& a, dim3 grid, cudaStr
   }
   w4a16_gemm_kernel<MT, GS, EPI><<<grid, kThreads, Plan::kTotal, stream>>>(tmap, a);
   CB_CUDA_CHECK(cudaGetLastError());
-}
-
-template <int MT, int GS, int EPI>
-void launch_persistent(const CUtensorMap& tmap, const GemmArgs& a, int ctas, cudaStream_t stream) {
-  using Plan = PairPlan<MT, GS>;
-  static bool configured = false;
-  if (!configured) {
-    CB_CUDA_CHECK(cudaFuncSetAttribute(w4a16_persistent_kernel<MT, GS, EPI>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, Plan::kTotal));
-    configured = true;
-  }
-  w4a16_persistent_kernel<MT, GS, EPI><<<ctas, kPThreads, Plan::kTotal, stream>>>(tmap, a);
-  CB_CUDA_CHECK(cudaGetLastError());
-}
-
-template <int GS, int EPI>
-void dispatch_persistent(int MT, const CUtensorMap& tmap, const GemmArgs& a, int ctas,
-                         cudaStream_t s) {
-  switch (MT) {
-    case 16: launch_persistent<16, GS, EPI>(tmap, a, ctas, s); break;
-    case 32: launch_persistent<32, GS, EPI>(tmap, a, ctas, s); break;
-    default: launch_persistent<64, GS, EPI>(tmap, a, ctas, s); break;
-  }
 }
 
 template <int GS, int EPI>
@@ -1028,8 +625,6 @@ static int pick_splits(int tiles, int KB, int num_sms) {
 
 struct GemmPlanInfo {
   int MT, splits, kbps, token_tiles, row_tiles;
-  bool persistent;
-  int ctas, units, ub, ur, max_contrib;
 };
 
 static GemmPlanInfo plan_gemm(int M, int N, int K, int forced_splits) {
@@ -1043,18 +638,6 @@ static GemmPlanInfo plan_gemm(int M, int N, int K, int forced_splits) {
   splits = std::max(1, std::min(splits, KB));
   p.kbps = (KB + splits - 1) / splits;
   p.splits = (KB + p.kbps - 1) / p.kbps;
-  // The persistent stream-K kernel is opt-in (CASCADIA_GEMM_PERSIST=1): on
-  // B200 the per-k-block split-K kernel measured faster for every decode shape.
-  static const bool persist = [] {
-    const char* e = std::getenv("CASCADIA_GEMM_PERSIST");
-    return e != nullptr && std::atoi(e) != 0;
-  }();
-  p.persistent = p.MT <= 64 && forced_splits <= 0 && persist;
-  p.units = p.row_tiles * p.token_tiles * KB;
-  p.ctas = std::min(num_sms(), p.units);
-  p.ub = p.units / p.ctas;
-  p.ur = p.units % p.ctas;
-  p.max_contrib = (KB + p.ub - 1) / p.ub + 1;
   return p;
 }
 
@@ -1090,22 +673,40 @@ static int gemv_max_m() {
 void set_pdl(bool on) { pdl_flag() = on ? 1 : 0; }
 bool pdl_enabled() { return pdl_flag() != 0; }
 
-static bool use_gemv(int64_t M, int64_t forced_splits) {
-  return forced_splits <= 0 && M <= gemv_max_m() && gemv_eligible(M);
+// Which kernel runs a GEMM.  `forced`: 0 chooses; > 0 the split-K kernel
+// with that many k-splits; -1 the persistent stream kernel; -2 the small-M
+// kernel (tests and microbenchmarks compare the kernels on one shape).
+enum GemmPath : int { kPathSplitK = 0, kPathStream = 1, kPathSmallM = 2 };
+
+static GemmPath choose_path(int64_t M, int64_t N, int64_t K, int64_t forced) {
+  if (forced > 0) return kPathSplitK;
+  const bool stream_ok = stream_eligible((int)M, (int)N, (int)K);
+  if (forced == -1) return stream_ok ? kPathStream : kPathSplitK;
+  if (forced == -2) return gemv_eligible(M) ? kPathSmallM : kPathSplitK;
+  if (M <= gemv_max_m() && gemv_eligible(M)) return kPathSmallM;
+  // The stream kernel is selected explicitly for now: measured on B200 at
+  // M = 64 its main loop runs ~0.6 us per 128x128 k-block per SM, like the
+  // split-K kernel, and the split-K grid balances the large shapes better.
+  return kPathSplitK;
 }
 
 int64_t w4a16_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t forced_splits) {
-  if (use_gemv(M, forced_splits)) return gemv_workspace_floats(M, N, K, 0);
+  switch (choose_path(M, N, K, forced_splits)) {
+    case kPathSmallM: return gemv_workspace_floats(M, N, K, 0);
+    case kPathStream: return stream_plan((int)M, (int)N, (int)K, num_sms()).ws_floats;
+    default: break;
+  }
   GemmPlanInfo p = plan_gemm((int)M, (int)N, (int)K, (int)forced_splits);
-  if (p.persistent)
-    return (int64_t)p.row_tiles * p.token_tiles * p.max_contrib * p.MT * 128;
   if (p.splits == 1) return 0;
   return (int64_t)p.splits * p.token_tiles * p.MT * N;
 }
 
+// Counters any path may use for an [M, N] output (zero between launches):
+// split-K one per (token tile, row tile), the stream kernel four per row
+// tile, the small-M kernel one per row tile.
 int64_t w4a16_counter_count(int64_t M, int64_t N) {
   const int MT = pick_mt((int)M);
-  return (int64_t)((M + MT - 1) / MT) * (N / 128);
+  return (int64_t)std::max<int64_t>((M + MT - 1) / MT, 4) * (N / 128);
 }
 
 // x: [M, K] bf16 (row stride K).  wblob: uint8 blob.  out: [M, ldo] bf16.
@@ -1129,7 +730,8 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
   if (M == 0) return;
   const c10::cuda::CUDAGuard guard(x.device());
   TORCH_CHECK(epilogue != kEpiResid || residual.has_value(), "residual epilogue needs residual");
-  if (use_gemv(M, forced_splits)) {
+  const GemmPath path = choose_path(M, N, K, forced_splits);
+  if (path == kPathSmallM) {
     const int64_t need = gemv_workspace_floats(M, N, K, 0);
     TORCH_CHECK(ws.numel() >= need, "workspace too small");
     TORCH_CHECK(need == 0 || counters.numel() >= N / 128, "counters too small");
@@ -1140,12 +742,19 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
                 status.data_ptr<int>(), 0, at::cuda::getCurrentCUDAStream());
     return;
   }
+  if (path == kPathStream) {
+    const StreamPlan sp = stream_plan(M, (int)N, K, num_sms());
+    TORCH_CHECK(ws.numel() >= sp.ws_floats, "workspace too small");
+    TORCH_CHECK(counters.numel() >= sp.counters, "counters too small");
+    stream_launch(x.data_ptr(), x.stride(0), wblob.data_ptr<uint8_t>(), out.data_ptr(),
+                  out.stride(0), residual.has_value() ? residual->data_ptr() : nullptr,
+                  residual.has_value() ? residual->stride(0) : 0, M, (int)N, K, (int)group_size,
+                  (int)epilogue, ws.data_ptr<float>(), counters.data_ptr<int>(),
+                  status.data_ptr<int>(), at::cuda::getCurrentCUDAStream(), g_gemm_trace);
+    return;
+  }
   GemmPlanInfo p = plan_gemm(M, (int)N, K, (int)forced_splits);
-  if (p.persistent) {
-    TORCH_CHECK(ws.numel() >= (int64_t)p.row_tiles * p.token_tiles * p.max_contrib * p.MT * 128,
-                "workspace too small");
-    TORCH_CHECK(counters.numel() >= (int64_t)p.token_tiles * p.row_tiles, "counters too small");
-  } else if (p.splits > 1) {
+  if (p.splits > 1) {
     TORCH_CHECK(ws.numel() >= (int64_t)p.splits * p.token_tiles * p.MT * N, "workspace too small");
     TORCH_CHECK(counters.numel() >= (int64_t)p.token_tiles * p.row_tiles, "counters too small");
   }
@@ -1156,13 +765,8 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
                    ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr())
                    : nullptr;
   a.ldr = residual.has_value() ? (int)residual->stride(0) : 0;
-  a.ws = (p.splits > 1 || p.persistent) ? ws.data_ptr<float>() : nullptr;
-  a.counters = (p.splits > 1 || p.persistent) ? counters.data_ptr<int>() : nullptr;
-  a.row_tiles = p.row_tiles;
-  a.units = p.units;
-  a.ub = p.ub;
-  a.ur = p.ur;
-  a.max_contrib = p.max_contrib;
+  a.ws = p.splits > 1 ? ws.data_ptr<float>() : nullptr;
+  a.counters = p.splits > 1 ? counters.data_ptr<int>() : nullptr;
   a.status = status.data_ptr<int>();
   a.M = M;
   a.N = (int)N;
@@ -1170,33 +774,15 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
   a.ldo = (int)out.stride(0);
   a.kb_per_split = p.kbps;
   a.splits = p.splits;
-  static const int diag = [] {
-    const char* e = std::getenv("CASCADIA_GEMM_DIAG");
-    return e ? std::atoi(e) : 0;
-  }();
-  a.diag = diag;
   a.trace = g_gemm_trace;
   a.vec_out = vec_rows_ok(out, residual);
   a.pdl = pdl_flag();
-  TORCH_CHECK(epilogue != kEpiResid || residual.has_value(), "residual epilogue needs residual");
 
   CUtensorMap tmap = make_tmap_2d_bf16(x.data_ptr(), (uint64_t)K, (uint64_t)M,
                                        (uint64_t)x.stride(0) * 2, 64, (uint32_t)p.MT,
                                        CU_TENSOR_MAP_SWIZZLE_128B);
   dim3 grid(p.row_tiles, p.splits, p.token_tiles);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  if (p.persistent) {
-    if (group_size == 128) {
-      if (epilogue == kEpiStore) dispatch_persistent<128, kEpiStore>(p.MT, tmap, a, p.ctas, stream);
-      else if (epilogue == kEpiSilu) dispatch_persistent<128, kEpiSilu>(p.MT, tmap, a, p.ctas, stream);
-      else dispatch_persistent<128, kEpiResid>(p.MT, tmap, a, p.ctas, stream);
-    } else {
-      if (epilogue == kEpiStore) dispatch_persistent<32, kEpiStore>(p.MT, tmap, a, p.ctas, stream);
-      else if (epilogue == kEpiSilu) dispatch_persistent<32, kEpiSilu>(p.MT, tmap, a, p.ctas, stream);
-      else dispatch_persistent<32, kEpiResid>(p.MT, tmap, a, p.ctas, stream);
-    }
-    return;
-  }
   if (group_size == 128) {
     if (epilogue == kEpiStore) dispatch_mt<128, kEpiStore>(p.MT, tmap, a, grid, stream);
     else if (epilogue == kEpiSilu) dispatch_mt<128, kEpiSilu>(p.MT, tmap, a, grid, stream);
@@ -1264,18 +850,27 @@ void w4a16_gemm_grouped(torch::Tensor x, torch::Tensor wblob, torch::Tensor out,
   }
 }
 
+// [path, MT, a, b, c, d]: split-K (0): splits, k-blocks per split, token
+// tiles, row tiles; stream (1): CTAs, tiles per pair, k-blocks per step,
+// steps; small-M (2): zeros.
 std::vector<int64_t> w4a16_plan(int64_t M, int64_t N, int64_t K, int64_t forced_splits) {
+  const GemmPath path = choose_path(M, N, K, forced_splits);
+  if (path == kPathStream) {
+    const StreamPlan p = stream_plan((int)M, (int)N, (int)K, num_sms());
+    return {1, p.MT, p.ctas, p.tpp, p.kstep, (int64_t)p.pairs * p.ksteps};
+  }
+  if (path == kPathSmallM) return {2, 0, 0, 0, 0, 0};
   GemmPlanInfo p = plan_gemm((int)M, (int)N, (int)K, (int)forced_splits);
-  return {p.MT, p.persistent ? -p.ctas : p.splits, p.persistent ? p.ub : p.kbps, p.token_tiles,
-          p.row_tiles};
+  return {0, p.MT, p.splits, p.kbps, p.token_tiles, p.row_tiles};
 }
 
 }  // namespace cb
 
 // ------------------------------------------------------------------ no-alloc entry point
-// The C entry point declared in gemm_w4a16_noalloc.h: the same kernels as
-// w4a16_gemm, with the split-K scratch (fp32 partials, per-tile counters and
-// a status word) in a fixed file-scope device array instead of caller tensors.
+// The C entry point declared in gemm_w4a16_noalloc.h: the kernel that
+// w4a16_gemm picks for the shape (small-M, persistent stream or split-K),
+// with its scratch (fp32 partials, counters and a status word) in a fixed
+// file-scope device array instead of caller tensors.
 #include "gemm_w4a16_noalloc.h"
 
 #include <cstring>
@@ -1316,14 +911,11 @@ cudaError_t na_set_attrs() {
   set((const void*)cb::w4a16_gemm_kernel<32, GS, EPI>, cb::SmemPlan<32, GS>::kTotal);
   set((const void*)cb::w4a16_gemm_kernel<64, GS, EPI>, cb::SmemPlan<64, GS>::kTotal);
   set((const void*)cb::w4a16_gemm_kernel<128, GS, EPI>, cb::SmemPlan<128, GS>::kTotal);
-  set((const void*)cb::w4a16_persistent_kernel<16, GS, EPI>, cb::PairPlan<16, GS>::kTotal);
-  set((const void*)cb::w4a16_persistent_kernel<32, GS, EPI>, cb::PairPlan<32, GS>::kTotal);
-  set((const void*)cb::w4a16_persistent_kernel<64, GS, EPI>, cb::PairPlan<64, GS>::kTotal);
   return e;
 }
 
-// Set-up for the current device (once): scratch address, kernel attributes
-// (they are per device) and the tensor-map encoder.
+// Set-up for the current device (once): scratch address, the kernels'
+// shared-memory attributes (they are per device) and the tensor-map encoder.
 cudaError_t na_setup(int dev, unsigned char** base, std::string* why) {
   std::lock_guard<std::mutex> lk(g_na_mu);
   if (g_na_base[dev] != nullptr) {
@@ -1339,7 +931,8 @@ cudaError_t na_setup(int dev, unsigned char** base, std::string* why) {
   const cudaError_t attrs[] = {
       na_set_attrs<128, cb::kEpiStore>(), na_set_attrs<128, cb::kEpiSilu>(),
       na_set_attrs<128, cb::kEpiResid>(), na_set_attrs<32, cb::kEpiStore>(),
-      na_set_attrs<32, cb::kEpiSilu>(),  na_set_attrs<32, cb::kEpiResid>()};
+      na_set_attrs<32, cb::kEpiSilu>(),  na_set_attrs<32, cb::kEpiResid>(),
+      cb::stream_set_attrs()};
   for (cudaError_t a : attrs)
     if (a != cudaSuccess) {
       *why = "cudaFuncSetAttribute";
@@ -1354,6 +947,10 @@ cudaError_t na_setup(int dev, unsigned char** base, std::string* why) {
   g_na_base[dev] = static_cast<unsigned char*>(p);
   *base = g_na_base[dev];
   return cudaSuccess;
+}
+
+bool na_aligned16(const void* p, long long ld) {
+  return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && ld % 8 == 0;
 }
 
 }  // namespace
@@ -1375,13 +972,22 @@ extern "C" __attribute__((visibility("default"))) int cb_w4a16_gemm_noalloc(
     return CB_NOALLOC_EINVAL;
   }
   if (M == 0) return CB_NOALLOC_OK;
-  // The plan (tile size, k-splits) and its scratch need, exactly as w4a16_gemm.
-  const GemmPlanInfo p = plan_gemm(M, N, K, 0);
-  const bool split = p.splits > 1 || p.persistent;
-  const long long ws_floats =
-      p.persistent ? (long long)p.row_tiles * p.token_tiles * p.max_contrib * p.MT * 128
-                   : (p.splits > 1 ? (long long)p.splits * p.token_tiles * p.MT * N : 0);
-  const long long counters = split ? (long long)p.token_tiles * p.row_tiles : 0;
+  // The kernel and its scratch need, exactly as w4a16_gemm chooses them.
+  const GemmPath path = choose_path(M, N, K, 0);
+  long long ws_floats = 0, counters = 0;
+  GemmPlanInfo p{};
+  if (path == kPathSmallM) {
+    ws_floats = gemv_workspace_floats(M, N, K, 0);
+    counters = ws_floats > 0 ? N / 128 : 0;
+  } else if (path == kPathStream) {
+    const StreamPlan sp = stream_plan(M, N, K, num_sms());
+    ws_floats = sp.ws_floats;
+    counters = sp.counters;
+  } else {
+    p = plan_gemm(M, N, K, 0);
+    ws_floats = p.splits > 1 ? (long long)p.splits * p.token_tiles * p.MT * N : 0;
+    counters = p.splits > 1 ? (long long)p.token_tiles * p.row_tiles : 0;
+  }
   if (ws_floats > (long long)CB_NOALLOC_MAX_WS_FLOATS ||
       counters > (long long)CB_NOALLOC_MAX_COUNTERS) {
     na_error(err, err_len,
@@ -1411,8 +1017,10 @@ extern "C" __attribute__((visibility("default"))) int cb_w4a16_gemm_noalloc(
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   float* ws = reinterpret_cast<float*>(base);
   int* ctr = reinterpret_cast<int*>(base + kNaWsBytes);
+  // With status == NULL the kernel's error code goes to a scratch word that
+  // the next call clears: the code is discarded (the header says so).
   int* st = status != nullptr ? status : reinterpret_cast<int*>(base + kNaStatusOff);
-  // What must start at zero: the tile counters this plan uses and (when the
+  // What must start at zero: the counters this call uses and (when the
   // scratch word is used) the status.  The partials are written before read.
   if (counters > 0) e = cudaMemsetAsync(ctr, 0, (size_t)counters * 4, s);
   if (e == cudaSuccess && status == nullptr) e = cudaMemsetAsync(st, 0, 4, s);
@@ -1421,50 +1029,49 @@ extern "C" __attribute__((visibility("default"))) int cb_w4a16_gemm_noalloc(
                                cudaGetErrorString(e));
     return CB_NOALLOC_ECUDA;
   }
-  GemmArgs a{};
-  a.wblob = static_cast<const uint8_t*>(wblob);
-  a.out = static_cast<__nv_bfloat16*>(out);
-  a.residual = epilogue == kEpiResid ? static_cast<const __nv_bfloat16*>(residual) : nullptr;
-  a.ldr = epilogue == kEpiResid ? (int)ldr : 0;
-  a.ws = split ? ws : nullptr;
-  a.counters = split ? ctr : nullptr;
-  a.row_tiles = p.row_tiles;
-  a.units = p.units;
-  a.ub = p.ub;
-  a.ur = p.ur;
-  a.max_contrib = p.max_contrib;
-  a.status = st;
-  a.M = M;
-  a.N = N;
-  a.K = K;
-  a.ldo = (int)ldo;
-  a.kb_per_split = p.kbps;
-  a.splits = p.splits;
   try {
+    if (path == kPathSmallM) {
+      gemv_launch(x, ldx, static_cast<const uint8_t*>(wblob), out, ldo,
+                  epilogue == kEpiResid ? residual : nullptr, epilogue == kEpiResid ? ldr : 0, M,
+                  N, K, group_size, epilogue, ws, ctr, st, 0, s);
+      return CB_NOALLOC_OK;
+    }
+    if (path == kPathStream) {
+      stream_launch(x, ldx, static_cast<const uint8_t*>(wblob), out, ldo,
+                    epilogue == kEpiResid ? residual : nullptr, epilogue == kEpiResid ? ldr : 0,
+                    M, N, K, group_size, epilogue, ws, ctr, st, s);
+      return CB_NOALLOC_OK;
+    }
+    GemmArgs a{};
+    a.wblob = static_cast<const uint8_t*>(wblob);
+    a.out = static_cast<__nv_bfloat16*>(out);
+    a.residual = epilogue == kEpiResid ? static_cast<const __nv_bfloat16*>(residual) : nullptr;
+    a.ldr = epilogue == kEpiResid ? (int)ldr : 0;
+    a.ws = p.splits > 1 ? ws : nullptr;
+    a.counters = p.splits > 1 ? ctr : nullptr;
+    a.status = st;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.ldo = (int)ldo;
+    a.kb_per_split = p.kbps;
+    a.splits = p.splits;
+    // The vectorised epilogue needs 16-byte aligned rows (as w4a16_gemm checks).
+    a.vec_out = na_aligned16(out, ldo) &&
+                (epilogue != kEpiResid || na_aligned16(residual, ldr)) ? 1 : 0;
+    a.pdl = pdl_flag();
     CUtensorMap tmap = make_tmap_2d_bf16(const_cast<void*>(x), (uint64_t)K, (uint64_t)M,
                                          (uint64_t)ldx * 2, 64, (uint32_t)p.MT,
                                          CU_TENSOR_MAP_SWIZZLE_128B);
-    if (p.persistent) {
-      if (group_size == 128) {
-        if (epilogue == kEpiStore) dispatch_persistent<128, kEpiStore>(p.MT, tmap, a, p.ctas, s);
-        else if (epilogue == kEpiSilu) dispatch_persistent<128, kEpiSilu>(p.MT, tmap, a, p.ctas, s);
-        else dispatch_persistent<128, kEpiResid>(p.MT, tmap, a, p.ctas, s);
-      } else {
-        if (epilogue == kEpiStore) dispatch_persistent<32, kEpiStore>(p.MT, tmap, a, p.ctas, s);
-        else if (epilogue == kEpiSilu) dispatch_persistent<32, kEpiSilu>(p.MT, tmap, a, p.ctas, s);
-        else dispatch_persistent<32, kEpiResid>(p.MT, tmap, a, p.ctas, s);
-      }
+    const dim3 grid(p.row_tiles, p.splits, p.token_tiles);
+    if (group_size == 128) {
+      if (epilogue == kEpiStore) dispatch_mt<128, kEpiStore>(p.MT, tmap, a, grid, s);
+      else if (epilogue == kEpiSilu) dispatch_mt<128, kEpiSilu>(p.MT, tmap, a, grid, s);
+      else dispatch_mt<128, kEpiResid>(p.MT, tmap, a, grid, s);
     } else {
-      const dim3 grid(p.row_tiles, p.splits, p.token_tiles);
-      if (group_size == 128) {
-        if (epilogue == kEpiStore) dispatch_mt<128, kEpiStore>(p.MT, tmap, a, grid, s);
-        else if (epilogue == kEpiSilu) dispatch_mt<128, kEpiSilu>(p.MT, tmap, a, grid, s);
-        else dispatch_mt<128, kEpiResid>(p.MT, tmap, a, grid, s);
-      } else {
-        if (epilogue == kEpiStore) dispatch_mt<32, kEpiStore>(p.MT, tmap, a, grid, s);
-        else if (epilogue == kEpiSilu) dispatch_mt<32, kEpiSilu>(p.MT, tmap, a, grid, s);
-        else dispatch_mt<32, kEpiResid>(p.MT, tmap, a, grid, s);
-      }
+      if (epilogue == kEpiStore) dispatch_mt<32, kEpiStore>(p.MT, tmap, a, grid, s);
+      else if (epilogue == kEpiSilu) dispatch_mt<32, kEpiSilu>(p.MT, tmap, a, grid, s);
+      else dispatch_mt<32, kEpiResid>(p.MT, tmap, a, grid, s);
     }
   } catch (const std::exception& ex) {
     na_error(err, err_len, std::string("cb_w4a16_gemm_noalloc: ") + ex.what());

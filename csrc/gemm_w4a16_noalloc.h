@@ -11,12 +11,14 @@
 //     PyTorch, and so without PyTorch's caching allocator to draw scratch from;
 //   * latency-critical paths, where cudaMalloc / cudaFree can synchronise the
 //     device and take unbounded time.
-// The regular entry point (the Python `w4a16_gemm`) takes its split-K scratch
-// from a caller-visible workspace tensor; this one takes it from a fixed
-// device array built into the library instead.
+// The regular entry point (the Python `w4a16_gemm`) takes its scratch from a
+// caller-visible workspace tensor; this one takes it from a fixed device
+// array built into the library instead.  Both choose the same kernel for a
+// shape: the small-M kernel for decode batches of up to 8 rows, the split-K
+// tcgen05 kernel above.
 //
 // Scratch: one file-scope device array of CB_NOALLOC_SCRATCH_BYTES (about
-// 8 MiB).  Every GPU that loads the library holds one copy until the process
+// 24 MiB).  Every GPU that loads the library holds one copy until the process
 // exits.  All calls on a device share it and it keeps the last call's
 // contents; the call clears what must start at zero.  Calls whose GPU work
 // overlaps (on different streams, or from different host threads without
@@ -38,13 +40,16 @@
 //   epilogue 0 store, 1 SiLU(gate)*up over interleaved gate/up rows,
 //            2 residual add;
 //   status   optional device int (zero it before the call): receives the
-//            first error code if a bounded wait inside the kernel gave up;
-//            NULL uses a word of the scratch array, cleared each call;
+//            first error code if a bounded wait inside the kernel gave up.
+//            With NULL the code goes to a word of the scratch array that the
+//            next call clears: a kernel-side timeout is then DISCARDED, so
+//            callers that need to detect one must pass a status word;
 //   stream   a cudaStream_t (NULL = legacy default stream);
 //   err      optional host buffer of err_len bytes for a message on failure.
-// Limits: K and N multiples of 128; the split-K partials of the chosen plan
-// must fit CB_NOALLOC_MAX_WS_FLOATS floats and its tile counters
-// CB_NOALLOC_MAX_COUNTERS; larger sizes are rejected with CB_NOALLOC_ETOOBIG.
+// Limits: K and N multiples of 128; the fp32 partials of the chosen kernel
+// must fit CB_NOALLOC_MAX_WS_FLOATS floats and its counters
+// CB_NOALLOC_MAX_COUNTERS (N up to 524288 rows); larger sizes are rejected
+// with CB_NOALLOC_ETOOBIG.
 // Returns CB_NOALLOC_OK once the kernel is enqueued.
 #pragma once
 
@@ -52,7 +57,7 @@
 extern "C" {
 #endif
 
-#define CB_NOALLOC_MAX_WS_FLOATS (2u << 20)
+#define CB_NOALLOC_MAX_WS_FLOATS (6u << 20)
 #define CB_NOALLOC_MAX_COUNTERS 16384u
 #define CB_NOALLOC_SCRATCH_BYTES \
   (CB_NOALLOC_MAX_WS_FLOATS * 4u + CB_NOALLOC_MAX_COUNTERS * 4u + 256u)

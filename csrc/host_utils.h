@@ -110,4 +110,27 @@ inline CUtensorMap make_tmap_2d_bf16(void* base, uint64_t inner, uint64_t outer,
   return m;
 }
 
+// X [rows, K] bf16 (row pitch row_bytes) viewed as 3-D {64, rows, K / 64}:
+// one load of box {64, box_rows, chunks} brings `chunks` consecutive 64-wide
+// K slices, each a [box_rows x 128 B] tile (128B swizzle), back to back in
+// shared memory.  The K-slice stride (128 B) is smaller than the row pitch.
+inline CUtensorMap make_tmap_kchunks_bf16(void* base, uint64_t K, uint64_t rows,
+                                          uint64_t row_bytes, uint32_t box_rows,
+                                          uint32_t chunks) {
+  CUtensorMap m;
+  cuuint64_t dims[3] = {64, rows, K / 64};
+  cuuint64_t strides[2] = {row_bytes, 128};
+  cuuint32_t box[3] = {64, box_rows, chunks};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    throw std::runtime_error("cuTensorMapEncodeTiled (K chunks) failed with code " +
+                             std::to_string((int)r));
+  }
+  return m;
+}
+
 }  // namespace cb

@@ -21,6 +21,7 @@ CSRC = os.path.join(HERE, "csrc")
 SOURCES = [
     "bindings.cpp",
     "gemm_w4a16.cu",
+    "gemm_stream.cu",
     "attention.cu",
     "elementwise.cu",
     "comm.cu",

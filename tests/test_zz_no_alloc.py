@@ -1,5 +1,6 @@
 """The allocation-free W4A16 GEMM entry point, called through its exported C
-symbol, against the regular entry point (same kernels, caller workspace).
+symbol, against the regular entry point (the same kernel choice: small-M up
+to 8 rows, split-K tcgen05 above; caller workspace).
 
 Collected last (file name) so that it also runs after every other test in
 one process; it must pass alone in a fresh process too.
@@ -12,7 +13,8 @@ import torch
 pytestmark = pytest.mark.gpu
 
 OK, EINVAL, ETOOBIG = 0, 1, 2
-MAX_WS_FLOATS = 2 << 20
+MAX_WS_FLOATS = 6 << 20
+MAX_COUNTERS = 16384
 
 
 def _lib():
@@ -40,10 +42,11 @@ def _call(f, x, blob, out, residual, n, gs, epi, status=None):
 
 
 @pytest.mark.parametrize("m,n,k,gs,epi", [
-    (16, 4096, 4096, 128, 0),    # split-K over 4 k-ranges (scratch partials + counters)
-    (5, 2048, 14336, 128, 2),    # split-K + residual epilogue
+    (16, 4096, 4096, 128, 0),    # split-K over several k-ranges (scratch partials + counters)
+    (5, 2048, 14336, 128, 2),    # small-M kernel + residual epilogue
     (33, 1024, 2048, 32, 1),     # group 32, SiLU(gate)*up epilogue
     (64, 6144, 4096, 128, 0),
+    (96, 4096, 4096, 128, 2),    # split-K tcgen05 kernel, residual epilogue
 ])
 def test_noalloc_matches_regular_entry_point(m, n, k, gs, epi):
     from cascadia_b200 import ops
@@ -77,10 +80,12 @@ def test_noalloc_rejects_oversized_and_bad_shapes():
 
     dev = torch.device("cuda")
     f = _lib()
-    # Find a shape whose split-K scratch exceeds the fixed maximum.
+    # A shape whose split-K counters exceed the fixed maximum (one per
+    # (token tile, 128-row tile)).
     shape = None
-    for m, n, k in ((256, 8192, 16384), (200, 16384, 16384), (128, 32768, 28672)):
-        if ops.ext().w4a16_workspace_floats(m, n, k, 0) > MAX_WS_FLOATS:
+    for m, n, k in ((256, 8192, 16384), (16, 1 << 22, 256)):
+        if (ops.ext().w4a16_workspace_floats(m, n, k, 0) > MAX_WS_FLOATS
+                or (m > 8 and (n // 128) > MAX_COUNTERS)):
             shape = (m, n, k)
             break
     assert shape is not None
