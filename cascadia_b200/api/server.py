@@ -25,7 +25,7 @@ import json
 import logging
 import time
 import uuid
-from dataclasses import dataclass, field
+from dataclasses import asdict, dataclass, field
 from typing import Any, Dict, List, Optional
 
 from fastapi import FastAPI, Request
@@ -189,6 +189,23 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
                             stop=list(stop or []))
         return sp, float(body.get("temperature") or 0.0)
 
+    def _logprobs_count(body: dict, chat: bool) -> int:
+        """Top-logprobs per position to ask the engine for (0 = off): chat's
+        `logprobs` is a bool with `top_logprobs` 1..20 (default 1), legacy
+        completions' `logprobs` is the count itself (at most 20), as in
+        crates/cascadia-api/src/lib.rs:556-560, 720-724."""
+        try:
+            if chat:
+                if not body.get("logprobs"):
+                    return 0
+                return max(1, min(20, int(body.get("top_logprobs") or 1)))
+            return max(0, min(20, int(body.get("logprobs") or 0)))
+        except (TypeError, ValueError):
+            return 0
+
+    def _lp_json(lps: list) -> Optional[dict]:
+        return {"content": [asdict(lp) for lp in lps]} if lps else None
+
     def _enable_thinking(body: dict) -> bool:
         kw = body.get("chat_template_kwargs") or {}
         if isinstance(kw, dict) and "enable_thinking" in kw:
@@ -231,8 +248,7 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
         prefix = "chatcmpl-" if chat else "cmpl-"
         task = GenerationTask(task_id=prefix + uuid.uuid4().hex, prompt=prompt,
                               max_tokens=int(body.get("max_tokens") or 256), temperature=temp,
-                              logprobs=int(body.get("top_logprobs") or 0)
-                              if body.get("logprobs") else 0,
+                              logprobs=_logprobs_count(body, chat),
                               sampling=sp, enable_thinking=_enable_thinking(body))
         ids = body.get("prompt_token_ids")
         if isinstance(ids, list) and ids:
@@ -249,7 +265,7 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
                                      headers={"Cache-Control": "no-cache",
                                               "x-accel-buffering": "no"})
         try:
-            text, finish, completion, prompt_toks, error = await _collect(task, stream)
+            text, finish, completion, prompt_toks, error, lps = await _collect(task, stream)
         finally:
             sem.release()
             stats.end()
@@ -267,23 +283,27 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
                 msg = {"role": "assistant", "content": None,
                        "tool_calls": [c.to_openai() for c in calls]}
                 finish = "tool_calls"
+            choice = {"index": 0, "message": msg, "finish_reason": finish}
+            if lps:
+                choice["logprobs"] = _lp_json(lps)
             return {"id": task.task_id, "object": "chat.completion", "created": _now(),
-                    "model": cfg.model_name,
-                    "choices": [{"index": 0, "message": msg, "finish_reason": finish}],
-                    "usage": usage}
+                    "model": cfg.model_name, "choices": [choice], "usage": usage}
         return {"id": task.task_id, "object": "text_completion", "created": _now(),
                 "model": cfg.model_name,
                 "choices": [{"index": 0, "text": text, "finish_reason": finish,
-                             "logprobs": None}],
+                             "logprobs": _lp_json(lps)}],
                 "usage": usage}
 
     async def _collect(task, stream):
         text, finish, completion, prompt_toks, error = "", "stop", 0, 0, None
+        lps = []
         stops = task.sampling.stop
         async for c in stream:
             if c.error is not None:
                 error = c.error
                 break
+            if c.logprobs is not None:
+                lps.append(c.logprobs)
             text += c.text
             completion += c.token_count()
             stats.add_tokens(c.token_count())
@@ -298,7 +318,7 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
                 stream.done = True
                 runner.cancel(task.task_id)
                 break
-        return text, finish, completion, prompt_toks, error
+        return text, finish, completion, prompt_toks, error, lps
 
     async def _sse(task, stream, chat: bool, include_usage: bool, tools_active: bool):
         model = cfg.model_name
@@ -307,13 +327,19 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
         stops = task.sampling.stop
         sent = ""       # text already emitted
         pending = ""    # text held back (possible stop-sequence prefix)
+        lp_pending = []  # logprobs of tokens whose text is not emitted yet
         first = True
 
         def frame(payload) -> bytes:
             return f"data: {json.dumps(payload, ensure_ascii=False)}\n\n".encode()
 
         def delta_frame(text: str, finish: Optional[str]):
-            nonlocal first
+            nonlocal first, lp_pending
+            # Logprobs ride on the frame that carries their tokens' text; the
+            # finishing frame flushes any whose text was empty or held back.
+            lp = _lp_json(lp_pending) if (text or finish is not None) else None
+            if text or finish is not None:
+                lp_pending = []
             if chat:
                 d: Dict[str, Any] = {}
                 if first:
@@ -322,8 +348,10 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
                     d["content"] = text
                 first = False
                 choice = {"index": 0, "delta": d, "finish_reason": finish}
+                if lp is not None:
+                    choice["logprobs"] = lp
             else:
-                choice = {"index": 0, "text": text, "finish_reason": finish, "logprobs": None}
+                choice = {"index": 0, "text": text, "finish_reason": finish, "logprobs": lp}
             return frame({"id": task.task_id, "object": obj, "created": _now(), "model": model,
                           "choices": [choice]})
 
@@ -339,6 +367,8 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
                     return
                 completion += c.token_count()
                 stats.add_tokens(c.token_count())
+                if c.logprobs is not None:
+                    lp_pending.append(c.logprobs)
                 if c.prompt_tokens:
                     prompt_toks = c.prompt_tokens
                 if c.finish_reason is not None:

@@ -33,8 +33,10 @@ from ..runtime.generator import DecodeGraph
 from ..runtime.kv_cache import BLOCK_SIZE
 from ..runtime.scheduler import PrefixCache, SchedulerState, Sequence
 from ..utils.trace import span, task_done
-from ..types import Chunk, FinishReason, GenerationTask, LoadProgress, PeerLayout, ShardSpec
-from .base import Builder, Engine, EngineError, InvalidConfig, NotLoaded, PromptTooLong, QueueFull
+from ..types import (Chunk, FinishReason, GenerationTask, LoadProgress, PeerLayout, ShardSpec,
+                     TokenLogprobs, TopLogprob)
+from .base import (BatchAborted, Builder, Engine, EngineError, InvalidConfig, NotLoaded,
+                   PromptTooLong, QueueFull)
 
 log = logging.getLogger("cascadia.engine")
 
@@ -73,6 +75,8 @@ class LLMEngine(Engine):
         self.model_id = model_id
         self._seq_counter = 0
         self.last_step_ms = 0.0
+        self.aborted_batches = 0
+        self._pending_lp: Dict[str, TokenLogprobs] = {}
         # Set for the first stage of a pipeline (parallel.pp.PipelineHead):
         # the model forward then relays through the downstream stages.
         self.pipeline = None
@@ -158,20 +162,52 @@ class LLMEngine(Engine):
         if work:
             with span("prefill"):
                 self._prefill(work, out)
+            metrics.STEP_SECONDS.labels(model=self.model_id, phase="prefill").observe(
+                time.perf_counter() - t0)
         dec = self.sched.decode_set()
-        # Sequences whose first token came from this step's prefill are not
-        # decoded again in the same iteration.
+        # Sequences whose first token came from this step's prefill (or that
+        # it aborted) are not decoded again in the same iteration.
         just = {s.seq_id for s, st, n in work}
         dec = [s for s in dec if s.seq_id not in just]
         if dec:
+            t1 = time.perf_counter()
             with span("decode"):
                 self._decode(dec, out)
+            metrics.STEP_SECONDS.labels(model=self.model_id, phase="decode").observe(
+                time.perf_counter() - t1)
         self.last_step_ms = (time.perf_counter() - t0) * 1000
         kv = self.model.kv
         metrics.KV_BLOCKS_USED.labels(model=self.model_id).set(
             kv.num_blocks - kv.allocator.num_free)
         metrics.KV_BLOCKS_TOTAL.labels(model=self.model_id).set(kv.num_blocks)
         return out
+
+    # ------------------------------------------------------------ device status
+    def _device_failed(self, seqs: List[Sequence], out) -> bool:
+        """Read the device status word after a forward (a few bytes, on the
+        same stream the forward ran on).  A bounded wait inside a kernel that
+        gave up (a peer that never signalled, a copy that never landed)
+        leaves its outputs unwritten and sets this word: the batch that ran
+        is then failed with an error chunk per sequence, its KV freed, and
+        the engine keeps serving the next requests (the reference's
+        BatchAborted, crates/cascadia-engine/src/lib.rs:56-72)."""
+        code = ops.read_status(self.dev)
+        if code == 0:
+            return False
+        err = BatchAborted(f"device status {code} ({ops.status_name(code)})")
+        log.error("%s: failing %d sequence(s)", err, len(seqs))
+        self.aborted_batches += 1
+        for s in seqs:
+            if s.finished:
+                continue
+            s.finished = True
+            tid = s.task.task_id
+            out.append((tid, Chunk.error_chunk(tid, str(err))))
+            if self.drafter is not None:
+                self.drafter.release(s.seq_id)
+            self.sched.remove(s.seq_id)
+            self.decoders.pop(tid, None)
+        return True
 
     # ------------------------------------------------------------ prefill
     def _prefill(self, work, out):
@@ -186,6 +222,8 @@ class LLMEngine(Engine):
             s.prefilled = st + n
         seqs = [s for s, _, _ in work]
         toks = self._run_model(batch, ids, seqs)
+        if self._device_failed(seqs, out):
+            return
         if self.spec == "mtp" and self.pipeline is None:
             # Queue every prompt row of a greedy sequence (the ones that
             # decode speculatively) for the MTP head, with the token after it.
@@ -196,9 +234,11 @@ class LLMEngine(Engine):
                     nxt = list(p[st + 1:st + n]) + [p[st + n] if st + n < len(p) else int(t)]
                     self.drafter.observe(s.seq_id, st, nxt, self._last_hidden[off:off + n])
                 off += n
+        lps = getattr(self, "_pending_lp", {})
         for s, t in zip(seqs, toks):
             if not s.in_prefill:
-                self._emit(s, int(t), out)
+                self._emit(s, int(t), out, lps.get(s.seq_id))
+        self._pending_lp = {}
 
     def _run_model(self, batch, ids, seqs: List[Sequence]) -> List[int]:
         """Forward the batch and pick one token per sequence (its last row)."""
@@ -209,7 +249,10 @@ class LLMEngine(Engine):
             self._last_hidden = hidden
             rows = torch.tensor(batch.last_rows, dtype=torch.long, device=self.dev)
             logits = m.head(hidden.index_select(0, rows).contiguous())
-            return self._pick(seqs, logits)
+            toks = self._pick(seqs, logits)
+            self._pending_lp = self._logprobs(
+                [(i, s) for i, s in enumerate(seqs) if not s.in_prefill], logits, toks)
+            return toks
         want = [i for i, s in enumerate(seqs)
                 if not s.in_prefill and (s.task.temperature > 0 or self._has_penalty(s))]
         toks, logits = self.pipeline.forward_tokens(batch, hidden, want)
@@ -233,19 +276,23 @@ class LLMEngine(Engine):
         m = self.model
         kv = m.kv
         if self.spec is not None and self.pipeline is None:
-            greedy = [s for s in seqs if s.task.temperature <= 0 and not self._has_penalty(s)]
+            greedy = [s for s in seqs if self._speculable(s)]
             if greedy:
                 self._spec_decode(greedy, out)
-                seqs = [s for s in seqs if not (s.task.temperature <= 0
-                                                and not self._has_penalty(s))]
+                seqs = [s for s in seqs if not self._speculable(s)]
                 if not seqs:
                     return
         if self.dev.type != "cuda" or self.pipeline is not None:
             starts = [s.total_len - 1 for s in seqs]
             batch = build_batch(m, [s.seq_id for s in seqs], [1] * len(seqs), starts, True)
             ids = torch.tensor([s.output_ids[-1] for s in seqs], dtype=torch.int32).to(self.dev)
-            for s, t in zip(seqs, self._run_model(batch, ids, seqs)):
-                self._emit(s, int(t), out)
+            toks = self._run_model(batch, ids, seqs)
+            if self._device_failed(seqs, out):
+                return
+            lps = getattr(self, "_pending_lp", {})
+            self._pending_lp = {}
+            for s, t in zip(seqs, toks):
+                self._emit(s, int(t), out, lps.get(s.seq_id))
             return
         n = len(seqs)
         B = _bucket(n)
@@ -279,8 +326,11 @@ class LLMEngine(Engine):
             toks = [int(t) for t in g.out_host[:n]]
         else:
             toks = self._pick(seqs, g.logits[:n])
+        if self._device_failed(seqs, out):
+            return
+        lps = self._logprobs(list(enumerate(seqs)), g.logits[:n], toks)
         for s, t in zip(seqs, toks):
-            self._emit(s, int(t), out)
+            self._emit(s, int(t), out, lps.get(s.seq_id))
 
     def _spec_decode(self, seqs: List[Sequence], out):
         """One speculative round for greedy sequences: draft, verify in one
@@ -309,8 +359,13 @@ class LLMEngine(Engine):
         kv_lens = [s.total_len - 1 for s in seqs]
         hid = [] if self.spec == "mtp" else None
         results = verify_batch(m, ids, [s.output_ids[-1] for s in seqs], drafts, kv_lens, hid)
+        if self._device_failed(seqs, out):
+            return
         st = self.spec_stats
         st.rounds += 1
+        metrics.SPEC_PROPOSED.labels(model=self.model_id).inc(sum(len(d) for d in drafts))
+        metrics.SPEC_ACCEPTED.labels(model=self.model_id).inc(
+            sum(len(r) - 1 for r in results))
         for i, (s, d, acc, kl) in enumerate(zip(seqs, drafts, results, kv_lens)):
             a = len(acc) - 1
             st.drafted += len(d)
@@ -379,13 +434,46 @@ class LLMEngine(Engine):
                    torch.tensor(offs, dtype=torch.int64, device=self.dev), outt)
         return [int(t) for t in outt.tolist()]
 
+    def _speculable(self, s: Sequence) -> bool:
+        """Greedy, unpenalised sequences without logprobs decode speculatively."""
+        return s.task.temperature <= 0 and not self._has_penalty(s) and s.task.logprobs <= 0
+
+    def _logprobs(self, rows, logits: torch.Tensor, toks) -> Dict[str, TokenLogprobs]:
+        """Per-token logprobs for the rows whose task asked for them: the
+        chosen token's log-probability under the model's distribution
+        (log-softmax of the raw logits, before temperature and penalties) and
+        the task's top-N alternatives (the OpenAI `logprobs` /
+        `top_logprobs` semantics; at most 20)."""
+        want = [(i, s) for i, s in rows if s.task.logprobs > 0]
+        if not want:
+            return {}
+        full = self.model.full_logits(logits)
+        idx = torch.tensor([i for i, _ in want], dtype=torch.long, device=full.device)
+        lp = torch.log_softmax(full.index_select(0, idx).float(), dim=-1)
+        k = max(min(20, s.task.logprobs) for _, s in want)
+        top_v, top_i = lp.topk(k, dim=-1)
+        chosen = torch.tensor([int(toks[i]) for i, _ in want], dtype=torch.long,
+                              device=full.device)
+        ch = lp.gather(1, chosen.unsqueeze(1)).squeeze(1)
+        top_v, top_i, ch = top_v.cpu().tolist(), top_i.cpu().tolist(), ch.cpu().tolist()
+        out = {}
+        for r, (i, s) in enumerate(want):
+            n = min(20, s.task.logprobs)
+            tid = int(toks[i])
+            out[s.seq_id] = TokenLogprobs(
+                token=self.tok.decode([tid]), token_id=tid, logprob=float(ch[r]),
+                top_logprobs=[TopLogprob(token=self.tok.decode([int(t)]), token_id=int(t),
+                                         logprob=float(v))
+                              for t, v in zip(top_i[r][:n], top_v[r][:n])])
+        return out
+
     @staticmethod
     def _has_penalty(s: Sequence) -> bool:
         sp = s.task.sampling
         return sp.frequency_penalty != 0.0 or sp.presence_penalty != 0.0
 
     # ------------------------------------------------------------ emission
-    def _emit(self, s: Sequence, tok: int, out):
+    def _emit(self, s: Sequence, tok: int, out, lp: Optional[TokenLogprobs] = None):
         s.output_ids.append(tok)
         if s.first_token_at is None:
             s.first_token_at = time.monotonic()
@@ -402,12 +490,16 @@ class LLMEngine(Engine):
         # n_tokens is set on every token chunk: a token whose text is still
         # an incomplete UTF-8 sequence (empty text) must still be counted.
         if finish is None:
-            out.append((tid, Chunk.token(tid, tok, text).with_n_tokens(1)))
+            c = Chunk.token(tid, tok, text).with_n_tokens(1)
+            c.logprobs = lp
+            out.append((tid, c))
             return
         if self.drafter is not None:
             self.drafter.release(s.seq_id)
         if tok not in self.eos:
-            out.append((tid, Chunk.token(tid, tok, text).with_n_tokens(1)))
+            c = Chunk.token(tid, tok, text).with_n_tokens(1)
+            c.logprobs = lp
+            out.append((tid, c))
         fin = Chunk.final_marker(tid, "").with_finish_reason(finish).with_prompt_tokens(
             len(s.prompt_ids))
         task_done(tid, getattr(s, "submitted_at", 0.0) or 0.0, s.first_token_at or 0.0,

@@ -91,6 +91,22 @@ def status_buffer(device: torch.device) -> torch.Tensor:
     return buf
 
 
+# Codes written by the kernels' bounded waits (csrc/common.cuh StatusCode).
+STATUS_NAMES = {
+    101: "GEMM weight/activation load timed out",
+    102: "GEMM MMA issue timed out",
+    103: "GEMM epilogue timed out",
+    104: "GEMM dequantisation timed out",
+    201: "attention load timed out",
+    301: "peer (NVLink) signal timed out",
+    401: "MoE expert-parallel exchange timed out",
+}
+
+
+def status_name(code: int) -> str:
+    return STATUS_NAMES.get(int(code), "unknown device status")
+
+
 def read_status(device: torch.device, clear: bool = True) -> int:
     buf = status_buffer(device)
     v = int(buf.item())
