@@ -100,19 +100,93 @@ def _builder(args, tp=None):
 
 
 def cmd_run(args):
-    """Single-process server: the whole model on one device."""
+    """Serve the model: one process on one device, or, under
+    ``torch.distributed.run``, one rank per GPU with ``--tp`` or ``--pp``."""
     from .runtime.runner import Runner
     from .types import PeerLayout, ShardSpec
 
     _init_logging(args.log_level)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.tp > 1 or args.pp > 1:
+        return _run_distributed(args)
     name = args.served_model_name or os.path.basename(str(args.model).rstrip("/"))
     runner = Runner(_builder(args), model_id=name, device=args.device)
     nl = _num_layers(args.model)
     runner.start(PeerLayout(), ShardSpec(name, 0, nl, nl, args.device, True, True))
     try:
-        _serve(runner, args.api, name, args.max_concurrent)
+        _serve_or_prompt(runner, args, name)
     finally:
         runner.close()
+
+
+def _run_distributed(args):
+    """Ranks of one box (torch.distributed.run): tensor parallel with a
+    replicated scheduler (--tp) or an NCCL pipeline (--pp); rank 0 serves the
+    API (or, with --prompt, generates once and prints)."""
+    import torch.distributed as dist
+
+    from .parallel.serve import (DistContext, ReplicatedEngine, build_pp_stage, build_tp_engine,
+                                 follower_loop)
+    from .runtime.runner import RelayExit, Runner
+
+    ctx = DistContext.from_env("cuda" if args.device.startswith("cuda") else "cpu",
+                               timeout_s=args.dist_timeout)
+    tp = args.tp if args.tp > 1 else (1 if args.pp > 1 else ctx.world)
+    pp = args.pp
+    if tp * pp != ctx.world:
+        raise SystemExit(f"--tp {tp} x --pp {pp} must equal the {ctx.world} ranks")
+    if tp > 1 and pp > 1:
+        raise SystemExit("serving combines TP or PP per job: use --tp N or --pp N")
+    code = 0
+    try:
+        if pp == 1:
+            engine, name = build_tp_engine(args, ctx)
+            if ctx.rank != 0:
+                follower_loop(engine, ctx.control)
+                return
+            eng = ReplicatedEngine(engine, ctx.control)
+            eng.warmup()
+            runner = Runner(None, model_id=name, device=str(ctx.device))
+            runner.start_with_engine(eng)
+            try:
+                _serve_or_prompt(runner, args, name)
+            finally:
+                runner.close()
+        else:
+            engine, worker, name = build_pp_stage(args, ctx)
+            if worker is not None:
+                r = Runner(None, model_id=name, device=str(ctx.device))
+                r.start_with_engine(worker, drive=False)
+                code = 1 if r.run_relay_loop() is RelayExit.CONNECTION_FATAL else 0
+                return
+            runner = Runner(None, model_id=name, device=str(ctx.device))
+            runner.start_with_engine(engine)
+            try:
+                _serve_or_prompt(runner, args, name)
+            finally:
+                engine.pipeline.shutdown()
+                runner.close()
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+        if code:
+            sys.exit(code)
+
+
+def _serve_or_prompt(runner, args, name: str):
+    if getattr(args, "prompt", None):
+        import uuid
+
+        from .types import GenerationTask
+
+        ids = [int(x) for x in args.prompt_ids.split(",")] if args.prompt_ids else None
+        s = runner.generate(GenerationTask("cli-" + uuid.uuid4().hex[:8], args.prompt,
+                                           max_tokens=args.max_tokens, prompt_ids=ids))
+        chunks = list(s)
+        print(json.dumps({"text": "".join(c.text for c in chunks),
+                          "token_ids": [c.token_id for c in chunks if not c.is_final],
+                          "error": chunks[-1].error if chunks else None}), flush=True)
+        return
+    _serve(runner, args.api, name, args.max_concurrent)
 
 
 def _num_layers(model: str) -> int:
@@ -252,9 +326,18 @@ def main(argv=None):
     p = argparse.ArgumentParser(prog="cascadia_b200")
     sub = p.add_subparsers(dest="cmd", required=True)
 
-    r = sub.add_parser("run", help="serve the whole model from one process")
+    r = sub.add_parser("run", help="serve the model (one process, or one rank per GPU "
+                                   "under torch.distributed.run with --tp / --pp)")
     _common(r)
     r.add_argument("--api", default="0.0.0.0:8000")
+    r.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks (torchrun)")
+    r.add_argument("--pp", type=int, default=1, help="pipeline stages over NCCL (torchrun)")
+    r.add_argument("--dist-timeout", type=float, default=300.0,
+                   help="process-group timeout, seconds")
+    r.add_argument("--prompt", default=None,
+                   help="generate once for this prompt, print JSON, exit (no API)")
+    r.add_argument("--prompt-ids", default=None, help="comma-separated token ids for --prompt")
+    r.add_argument("--max-tokens", type=int, default=64)
     r.set_defaults(fn=cmd_run)
 
     w = sub.add_parser("worker", help="run one pipeline stage")

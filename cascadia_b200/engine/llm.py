@@ -192,6 +192,13 @@ class LLMEngine(Engine):
         the engine keeps serving the next requests (the reference's
         BatchAborted, crates/cascadia-engine/src/lib.rs:56-72)."""
         code = ops.read_status(self.dev)
+        tp = getattr(self.model, "tp", None)
+        if tp is not None and tp.size > 1:
+            # Every replica must fail the same batch: the worst status of the
+            # TP ranks decides (one tiny collective per iteration).
+            t = torch.tensor([code], dtype=torch.int32, device=self.dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=tp.group)
+            code = int(t.item())
         if code == 0:
             return False
         err = BatchAborted(f"device status {code} ({ops.status_name(code)})")
@@ -400,7 +407,8 @@ class LLMEngine(Engine):
             for s, row in zip(seqs, full):
                 sp = s.task.sampling
                 if not hasattr(s, "_rng"):
-                    s._rng = ref.init_rng(sp.seed)
+                    s._rng = ref.init_rng(sp.seed if sp.seed is not None
+                                          else self._seq_seed(s))
                 outs.append(ref.sample(row, s.prompt_ids + s.output_ids, s.task.temperature,
                                        sp.top_p, sp.top_k, sp.frequency_penalty,
                                        sp.presence_penalty, 1.0, 0, s._rng))
@@ -417,7 +425,7 @@ class LLMEngine(Engine):
             h = s.prompt_ids + s.output_ids if self._has_penalty(s) else []
             hist.append(h)
             hist_len.append(len(h))
-            seed = sp.seed if sp.seed is not None else (hash(s.seq_id) & 0x7FFFFFFF)
+            seed = sp.seed if sp.seed is not None else self._seq_seed(s)
             seeds.append(seed)
             offs.append(s.rng_offset)
             s.rng_offset += 1
@@ -433,6 +441,14 @@ class LLMEngine(Engine):
                    torch.tensor(seeds, dtype=torch.int64, device=self.dev),
                    torch.tensor(offs, dtype=torch.int64, device=self.dev), outt)
         return [int(t) for t in outt.tolist()]
+
+    @staticmethod
+    def _seq_seed(s: Sequence) -> int:
+        """Sampling seed of a request without one: a stable hash of its id, so
+        every replica of a tensor-parallel engine draws the same tokens."""
+        import zlib
+
+        return zlib.crc32(s.seq_id.encode()) & 0x7FFFFFFF
 
     def _speculable(self, s: Sequence) -> bool:
         """Greedy, unpenalised sequences without logprobs decode speculatively."""
@@ -614,6 +630,15 @@ class LLMBuilder(Builder):
                 blocks = max(64, int(free * self.kv_fraction) // per)
             else:
                 blocks = max(64, (self.max_running * self.max_model_len) // BLOCK_SIZE // 4)
+        tp = self.tp
+        if tp is not None and tp.size > 1:
+            # Replicated schedulers must see the same pool: the smallest
+            # rank's block count wins.
+            t = torch.tensor([blocks], dtype=torch.int64,
+                             device=self.device if torch.device(self.device).type == "cuda"
+                             else "cpu")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN, group=tp.group)
+            blocks = int(t.item())
         if hybrid:
             self.model.allocate_kv(blocks, max_seqs=self.max_running)
         else:
