@@ -136,18 +136,9 @@ def main():
                 print("    waits (kcycles p50/max):", {w: (round(float(tr[:, 8 + i].median()) / 1000, 1),
                                                              round(float(tr[:, 8 + i].max()) / 1000, 1))
                                                           for i, w in enumerate(waits)})
-                jt = buf[4096:4096 + 256].view(64, 4).double().cpu()
-                base = jt[:, 0].min()
-                print("    CTA 0 per job (clock cycles from first A ready): A ready | issue start | "
-                      "issue end | buffer seen free by job+4's group")
-                for jj in range(0, 40):
-                    r = (jt[jj] - base).tolist()
-                    nxt = (jt[jj + 4, 3] - base).item() if jj + 4 < 64 else float('nan')
-                    print(f"      job {jj:2d}: {r[0]:8.0f} {r[1]:8.0f} {r[2]:8.0f}   free seen {nxt:8.0f}")
                 print("    issuer 0 clock cycles (p50): 8-MMA issue", float(tr[:, 16].median()),
                       "job commit", float(tr[:, 17].median()), "step commits",
-                      float(tr[:, 18].median()), "loop total", float(tr[:, 19].median()),
-                      "fence", float(tr[:, 20].median()), "step_info", float(tr[:, 21].median()))
+                      float(tr[:, 18].median()), "loop total", float(tr[:, 19].median()))
     print("status", ops.read_status(dev))
 
 

@@ -106,9 +106,13 @@ struct StreamArgs {
   int pairs, ksteps;     // steps = pairs * ksteps
   int ub, ur;            // CTA c owns steps [c*ub + min(c, ur), ...): ub or ub + 1 steps
   int pdl;
-  // Optional per-CTA %globaltimer stamps (bench/bench_gemm.py --trace):
-  // start, TMEM held, first stage landed, first MMA issued, last MMA
-  // issued, first unit stored, last unit stored, end.
+  // Optional per-CTA trace (bench/bench_gemm.py --trace), 24 words per CTA:
+  // 0-7 %globaltimer stamps (start, TMEM held, first stage landed, first
+  // MMA issued, last MMA issued, first unit stored, last unit stored, end);
+  // 8-14 clock64 cycles each role spent waiting (issuer 0 on stages, A
+  // buffers and accumulators; dequant warp 4 on stages, on A buffers and
+  // working; the producer on free stages); 16-19 issuer 0's cycles issuing
+  // MMAs, in per-job commits, in per-step commits and in its whole loop.
   unsigned long long* trace;
 };
 
@@ -278,7 +282,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
       for (int i = pre; i < s1 - s0; ++i) {
         const int s = i % SL;
         const unsigned long long tp = a.trace ? (unsigned long long)clock64() : 0ull;
-        if (!mbar_wait_sleep(&empty_w[s], ((i / SL) & 1) ^ 1, a.status, kStatusGemmLoadTimeout,
+        if (!mbar_wait_sleep(&empty_w[s], ((i / SL) & 1) ^ 1, a.status,
+                             kStatusGemmLoadTimeout,
                        abort_flag))
           break;
         if (a.trace) p_wait += clock64() - tp;
@@ -305,25 +310,24 @@ __global__ void __launch_bounds__(kSThreads, 1)
       int j = 0, u = 0;
       bool ok = true, fresh = true;
       unsigned long long w_stage = 0, w_a = 0, w_acc = 0;
-      long long c_issue = 0, c_commit = 0, c_step = 0, c_fence = 0, c_top = 0;
+      long long c_issue = 0, c_commit = 0, c_step = 0;
       long long c_total = a.trace ? clock64() : 0;
       for (int it = s0; it < s1 && ok; ++it) {
         const int i = it - s0;
         const int s = i % SL;
-        const long long ct = a.trace ? clock64() : 0;
         const StepInfo si = step_info(a, it, s0, s1);
         unsigned long long tw = a.trace ? (unsigned long long)clock64() : 0ull;
-        if (a.trace) c_top += tw - ct;
         if (si.unit_first) {
           fresh = true;
-          if (!mbar_wait_sleep(&acc_empty[u & 1], ((u >> 1) & 1) ^ 1, a.status, kStatusGemmMmaTimeout,
-                         abort_flag)) {
+          if (!mbar_wait_sleep(&acc_empty[u & 1], ((u >> 1) & 1) ^ 1, a.status,
+                               kStatusGemmMmaTimeout, abort_flag)) {
             ok = false;
             break;
           }
         }
         if (a.trace) { const unsigned long long t1 = clock64(); w_acc += t1 - tw; tw = t1; }
-        if (!mbar_wait_sleep(&full_w[s], (i / SL) & 1, a.status, kStatusGemmMmaTimeout, abort_flag)) {
+        if (!mbar_wait_sleep(&full_w[s], (i / SL) & 1, a.status, kStatusGemmMmaTimeout,
+                             abort_flag)) {
           ok = false;
           break;
         }
@@ -345,14 +349,11 @@ __global__ void __launch_bounds__(kSThreads, 1)
               break;
             }
             if (a.trace) w_a += clock64() - ta;
-            const long long cf = a.trace ? clock64() : 0;
             tc_fence_after();
-            if (a.trace) c_fence += clock64() - cf;
             if (j == 0) s_stamp(a, 3);
             const uint32_t a_tm = tmem_base + g * kSACols;
             const uint64_t db = x_desc + (uint64_t)((b * Plan::kXBytes) >> 4);
             const long long c0 = a.trace ? clock64() : 0;
-            if (a.trace && cta == 0 && j < 64) a.trace[4096 + j * 4 + 1] = c0;
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
               mma_bf16_ts(d_tm, a_tm + kk * 8,
@@ -360,7 +361,6 @@ __global__ void __launch_bounds__(kSThreads, 1)
                           (fresh && kk == 0) ? 0u : 1u);
             }
             const long long c1 = a.trace ? clock64() : 0;
-            if (a.trace && cta == 0 && j < 64) a.trace[4096 + j * 4 + 2] = c1;
             fresh = false;
             mma_commit(&a_empty[g]);
             if (a.trace) {
@@ -388,8 +388,6 @@ __global__ void __launch_bounds__(kSThreads, 1)
         s_put(a, 17, (unsigned long long)c_commit);
         s_put(a, 18, (unsigned long long)c_step);
         s_put(a, 19, (unsigned long long)c_total);
-        s_put(a, 20, (unsigned long long)c_fence);
-        s_put(a, 21, (unsigned long long)c_top);
       }
       // Also on the abort path: TMEM is freed only after the MMAs issued
       // so far have completed.
@@ -458,7 +456,6 @@ __global__ void __launch_bounds__(kSThreads, 1)
         break;
       }
       if (a.trace) { const unsigned long long t1 = clock64(); d_aempty += t1 - td; td = t1; }
-      if (a.trace && cta == 0 && lane == 0 && q == 0 && jj < 64) a.trace[4096 + jj * 4 + 3] = clock64();
       tc_fence_after();
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -480,7 +477,6 @@ __global__ void __launch_bounds__(kSThreads, 1)
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (a.trace && cta == 0 && lane == 0 && q == 0 && jj < 64) a.trace[4096 + jj * 4 + 0] = clock64();
       if (lane == 0) mbar_arrive(&a_full[grp]);
       if (a.trace) d_work += clock64() - td;
     }
