@@ -284,8 +284,7 @@ def main():
     sweep_ms = {}
     for nb in sweep:
         ids, lst = start_batch(nb, f"s{nb}_")
-        ms, _, _ = timed_steps(ids, lst)
-        sweep_ms[nb] = ms
+        sweep_ms[nb] = timed_steps(ids, lst)[0]
         free(ids)
         gen.graphs.clear()
 
@@ -369,7 +368,14 @@ def main():
         }
         print(json.dumps(out))
     if world > 1:
+        # Every captured graph holding an NCCL call must be gone before the
+        # process group is destroyed, or the exit waits for ever.
+        import gc
+
         gen.graphs.clear()
+        del gen
+        gc.collect()
+        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
 

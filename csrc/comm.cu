@@ -47,7 +47,9 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
   return v;
 }
 
-// Peer data written in earlier launches: fetch from memory, never from L1.
+// Peer data written by the peers' previous kernels: fetch from memory,
+// never from L1.  The caller issues all of a row's loads before using any
+// of them, so their NVLink round trips overlap.
 __device__ __forceinline__ uint4 ld_cv128(const void* p) {
   uint4 v;
   asm volatile("ld.global.cv.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -108,7 +110,10 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_kernel(const ArArgs a) 
   }
   __syncthreads();
   if (s_ok) {
-    // 3. reduce rows: each thread owns 8 consecutive columns per pass.
+    // 3. reduce rows: each thread owns 8 consecutive columns per pass.  All
+    //    peers' 16-byte pieces (and the residual) are loaded first, so the
+    //    NVLink round trips overlap, then summed in rank order (the same
+    //    result on every rank).
     const int nvec = a.H / 8;
     for (int row = blockIdx.x; row < a.M; row += gridDim.x) {
       float ss = 0.f;
@@ -120,15 +125,25 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_kernel(const ArArgs a) 
 #pragma unroll
         for (int q = 0; q < 8; ++q) acc[k][q] = 0.f;
         if (i < nvec) {
-          for (int p = 0; p < a.world; ++p) {
-            const uint4 u = ld_cv128(a.bufs[p] + (size_t)row * a.H + i * 8);
-            const bf16* v = reinterpret_cast<const bf16*>(&u);
+          uint4 part[kMaxRanks];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) acc[k][q] += __bfloat162float(v[q]);
-          }
+          for (int p = 0; p < kMaxRanks; ++p)
+            if (p < a.world) part[p] = ld_cv128(a.bufs[p] + (size_t)row * a.H + i * 8);
+          uint4 ru = make_uint4(0, 0, 0, 0);
+          bf16* rp = nullptr;
           if (a.residual != nullptr) {
-            bf16* rp = a.residual + (size_t)row * a.ldr + i * 8;
-            uint4 ru = *reinterpret_cast<const uint4*>(rp);
+            rp = a.residual + (size_t)row * a.ldr + i * 8;
+            ru = *reinterpret_cast<const uint4*>(rp);
+          }
+#pragma unroll
+          for (int p = 0; p < kMaxRanks; ++p) {
+            if (p < a.world) {
+              const bf16* v = reinterpret_cast<const bf16*>(&part[p]);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) acc[k][q] += __bfloat162float(v[q]);
+            }
+          }
+          if (rp != nullptr) {
             bf16* re = reinterpret_cast<bf16*>(&ru);
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
