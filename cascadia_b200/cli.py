@@ -85,7 +85,7 @@ def _builder(args, tp=None):
     if args.engine == "mock":
         return MockBuilder()
     if args.engine == "moe":
-        from .engine.moe import MoEBuilder
+        from .engine.llm import MoEBuilder
 
         return MoEBuilder(args.model, device=args.device, kv_blocks=args.kv_blocks,
                           max_running=args.max_running, max_model_len=args.max_model_len,

@@ -675,3 +675,17 @@ class LLMBuilder(Builder):
                          prefix_cache_blocks=self.prefix_cache_blocks,
                          model_id=self.model_name, spec=self.spec, draft_model=self.draft,
                          spec_k=self.spec_k, mtp_head=self.mtp)
+
+
+class MoEBuilder(LLMBuilder):
+    """Builder of the sparse-MoE engine (Qwen3-MoE / Kimi-K2 / GLM-5 / Qwen3.6
+    shapes).  The counterpart of the reference's sparse-MoE engines
+    (crates/cascadia-engine-sparse-moe/src/engine.rs, glm/model.rs): the same
+    continuous-batching LLMEngine drives the routed-expert model (fused
+    router/top-k kernel, counting-sort permute, grouped INT4 expert GEMMs,
+    weighted combine); dense presets are rejected."""
+
+    def model_class(self, cfg):
+        if not cfg.is_moe:
+            raise InvalidConfig(f"{self.model_name}: not a sparse-MoE config")
+        return super().model_class(cfg)

@@ -227,6 +227,25 @@ class MoEModel(LlamaModel):
             return shared_out
         return (shared_out.float() * torch.sigmoid(gate.float()).view(-1, 1)).to(torch.bfloat16)
 
+    # Every this many eager MoE layer calls, the tokens routed to each expert
+    # are added to the expert-load histogram (a device-to-host copy of E
+    # counts; never inside a CUDA-graph capture).  0 turns it off.
+    expert_load_every = 16
+
+    def _record_expert_load(self, ids: torch.Tensor, num_experts: int):
+        every = self.expert_load_every
+        if every <= 0 or (ids.is_cuda and torch.cuda.is_current_stream_capturing()):
+            return
+        self._moe_calls = getattr(self, "_moe_calls", 0) + 1
+        if (self._moe_calls - 1) % every:
+            return
+        from .. import metrics
+
+        counts = torch.bincount(ids.reshape(-1).long(), minlength=num_experts).cpu().tolist()
+        hist = metrics.EXPERT_LOAD.labels(model=self.cfg.arch)
+        for c in counts:
+            hist.observe(c)
+
     def _moe(self, lw: MoELayer, h: torch.Tensor, hidden: torch.Tensor):
         cfg = self.cfg
         k = cfg.num_experts_per_tok
@@ -240,6 +259,7 @@ class MoEModel(LlamaModel):
             else:
                 ids, w = ref_topk_gate(h, lw.router, lw.router_bias, k, scoring,
                                        cfg.norm_topk_prob, cfg.routed_scaling_factor)
+            self._record_expert_load(ids, bank.E if bank is not None else cfg.num_experts)
             so = self._gated(shared_out, shared_gate)
             add = hidden if so is None else (hidden.float() + so.float()).to(torch.bfloat16)
             self.ep.moe(bank, h, ids, w.float(), add, hidden)
@@ -247,6 +267,7 @@ class MoEModel(LlamaModel):
         if self.device.type == "cuda":
             ids, w = ops.moe_topk_gate(h, lw.router, k, scoring, cfg.norm_topk_prob,
                                        cfg.routed_scaling_factor, lw.router_bias)
+            self._record_expert_load(ids, bank.E)
             T = h.shape[0]
             if T <= SMALL_M_TOKENS and bank.gs == 128:
                 # Decode: a few rows per expert -> grouped small-M kernel on
@@ -271,6 +292,7 @@ class MoEModel(LlamaModel):
         # CPU oracle.
         ids, w = ref_topk_gate(h, lw.router, lw.router_bias, k, scoring, cfg.norm_topk_prob,
                                cfg.routed_scaling_factor)
+        self._record_expert_load(ids, bank.E)
         out = torch.zeros(h.shape[0], cfg.hidden_size)
         for t in range(h.shape[0]):
             for j in range(k):

@@ -83,7 +83,7 @@ def test_moe_builder_rejects_dense():
     import pytest
 
     from cascadia_b200.engine.base import InvalidConfig
-    from cascadia_b200.engine.moe import MoEBuilder
+    from cascadia_b200.engine.llm import MoEBuilder
 
     with pytest.raises(InvalidConfig):
         MoEBuilder("tiny-llama", device="cpu").model_class(get_config("tiny-llama"))
@@ -91,7 +91,7 @@ def test_moe_builder_rejects_dense():
 
 
 def test_moe_engine_cpu_generates():
-    from cascadia_b200.engine.moe import MoEBuilder
+    from cascadia_b200.engine.llm import MoEBuilder
     from cascadia_b200.runtime.runner import Runner
     from cascadia_b200.types import GenerationTask, PeerLayout, ShardSpec
 
@@ -102,3 +102,28 @@ def test_moe_engine_cpu_generates():
     r.close()
     assert chunks[-1].is_final
     assert sum(1 for c in chunks if not c.is_final) == 6
+
+
+def test_expert_load_metric_observed():
+    import torch
+
+    from cascadia_b200 import metrics
+    from cascadia_b200.models.config import get_config
+    from cascadia_b200.models.moe import MoEModel
+
+    def count():
+        for m in metrics.EXPERT_LOAD.collect():
+            for s in m.samples:
+                if s.name.endswith("_count") and s.labels.get("model") == "qwen3_moe":
+                    return s.value
+        return 0.0
+
+    cfg = get_config("tiny-moe")
+    m = MoEModel(cfg, "cpu").init_random(seed=3, gen_device="cpu")
+    m.allocate_kv(64)
+    from cascadia_b200.runtime.generator import BatchGenerator
+
+    before = count()
+    BatchGenerator(m, use_graph=False).generate([[3, 4, 5, 6]], max_new_tokens=2)
+    # One observation per expert for the sampled layer calls.
+    assert count() >= before + cfg.num_experts
