@@ -39,6 +39,10 @@ def main():
                    help="0 auto; > 0 split-K kernel with that split; -1 stream kernel; "
                         "-2 small-M kernel")
     p.add_argument("--graph", type=int, default=1, help="time a CUDA graph of the reps launches")
+    p.add_argument("--tp", type=int, default=1,
+                   help="shapes of one tensor-parallel rank (N or K divided by tp)")
+    p.add_argument("--sweep-splits", default="",
+                   help="comma-separated split-K factors to time per shape (best reported)")
     p.add_argument("--trace", action="store_true",
                    help="tcgen05 path: print per-CTA phase times of one launch")
     a = p.parse_args()
@@ -51,6 +55,55 @@ def main():
     res = {}
     for name in a.shapes.split(","):
         n, k, epi = SHAPES[name]
+        if a.tp > 1:
+            # Column-parallel: rows split (lm_head padded to 128-row tiles);
+            # row-parallel (o, down): K split.
+            if name in ("o", "down"):
+                k //= a.tp
+            elif name == "lm_head":
+                n = -(-n // (a.tp * 128)) * 128
+            else:
+                n //= a.tp
+        if a.sweep_splits:
+            sweep = [int(x) for x in a.sweep_splits.split(",")]
+            g = torch.Generator(device=dev).manual_seed(0)
+            blobs = [Int4Weight.random(n, k, generator=g, device=dev).blob(epi == ops.EPI_SILU)
+                     for _ in range(a.copies)]
+            x = torch.randn(a.m, k, device=dev).to(torch.bfloat16)
+            resid = torch.randn(a.m, n, device=dev).to(torch.bfloat16)
+            outs = torch.empty(a.m, n, dtype=torch.bfloat16, device=dev)
+            times = {}
+            for sp in sweep:
+                if sp > k // 128:
+                    continue
+
+                def run_s(i, sp=sp):
+                    kw = dict(residual=resid, out=outs) if epi == ops.EPI_RESID else {}
+                    return ops.w4a16_gemm(x, blobs[i % a.copies], n, 128, epi, splits=sp, **kw)
+                for i in range(3):
+                    run_s(i)
+                torch.cuda.synchronize()
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr):
+                    for i in range(a.reps):
+                        run_s(i)
+                gr.replay()
+                torch.cuda.synchronize()
+                ts = []
+                for _ in range(3):
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    gr.replay()
+                    e1.record()
+                    torch.cuda.synchronize()
+                    ts.append(e0.elapsed_time(e1) * 1000 / a.reps)
+                times[sp] = round(min(ts), 2)
+                del gr
+            auto = ops.w4a16_plan(a.m, n, k, 0)
+            best = min(times, key=times.get)
+            print(name, json.dumps({"n": n, "k": k, "m": a.m, "us_by_splits": times,
+                                    "best_splits": best, "auto_plan": auto}), flush=True)
+            continue
         g = torch.Generator(device=dev).manual_seed(0)
         copies = a.copies if a.reps > 1 else 1
         blobs = [Int4Weight.random(n, k, generator=g, device=dev).blob(epi == ops.EPI_SILU)
