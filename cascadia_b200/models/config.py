@@ -309,6 +309,10 @@ PRESETS = {
     "tiny-llama-128": ModelConfig(vocab_size=1024, hidden_size=512, num_layers=2, num_heads=8,
                                   num_kv_heads=2, head_dim=128, intermediate_size=1024,
                                   eos_token_ids=(1,)),
+    # Eight KV heads: splits over up to 8 tensor-parallel ranks.
+    "tiny-llama-kv8": ModelConfig(vocab_size=1024, hidden_size=1024, num_layers=2, num_heads=8,
+                                  num_kv_heads=8, head_dim=128, intermediate_size=1024,
+                                  eos_token_ids=(1,)),
     "tiny-moe": ModelConfig(arch="qwen3_moe", vocab_size=512, hidden_size=256, num_layers=2,
                             num_heads=4, num_kv_heads=2, head_dim=64, intermediate_size=512,
                             num_experts=8, num_experts_per_tok=2, moe_intermediate_size=128,

@@ -331,11 +331,19 @@ class LlamaModel:
         for i, lw in enumerate(self.layers):
             qkv = lw.qkv(h)
             attn = self._attention(i, qkv, batch)
+            nxt = self.layers[i + 1].in_norm if i + 1 < len(self.layers) else None
+            if fz.push:
+                # The GEMM delivers its partial into every rank's slots.
+                fz.gemm_push(lw.o, attn, 0)
+                fz.allreduce_pushed(0, T, hidden, lw.post_norm, h, eps)
+                act = lw.gate_up(h, ops.EPI_SILU)
+                fz.gemm_push(lw.down, act, 1)
+                fz.allreduce_pushed(1, T, hidden, nxt, h, eps)
+                continue
             lw.o(attn, out=fz.partial_out(0, T))
             fz.allreduce(0, T, hidden, lw.post_norm, h, eps)
             act = lw.gate_up(h, ops.EPI_SILU)
             lw.down(act, out=fz.partial_out(1, T))
-            nxt = self.layers[i + 1].in_norm if i + 1 < len(self.layers) else None
             fz.allreduce(1, T, hidden, nxt, h if nxt is not None else h, eps)
         return hidden
 

@@ -29,6 +29,10 @@ void ffn_sparse_forward(torch::Tensor x, torch::Tensor gate_packed, torch::Tenso
                         int64_t down_group_size);
 bool pdl_enabled();
 int64_t w4a16_counter_count(int64_t M, int64_t N);
+void w4a16_gemm_push(torch::Tensor x, torch::Tensor wblob, int64_t N, int64_t group_size,
+                     torch::Tensor out_ptrs, int64_t ldo, torch::Tensor sig_ptrs, int64_t my_rank,
+                     torch::Tensor push_done, torch::Tensor push_epoch, torch::Tensor ws,
+                     torch::Tensor counters, torch::Tensor status);
 void w4a16_set_trace(c10::optional<torch::Tensor> buf);
 std::vector<int64_t> w4a16_plan(int64_t M, int64_t N, int64_t K, int64_t forced_splits);
 void w4a16_gemm_grouped(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t N,
@@ -114,6 +118,10 @@ void spec_verify(torch::Tensor target, torch::Tensor draft, torch::Tensor out);
 void head_rmsnorm(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, int64_t Hq,
                   int64_t Hkv, int64_t D, double eps);
 // comm.cu
+void ar_rmsnorm_pushed(torch::Tensor slot_ptrs, torch::Tensor sig_ptrs, torch::Tensor epoch,
+                       torch::Tensor done, torch::Tensor status, int64_t rank, int64_t world,
+                       int64_t M, int64_t H, c10::optional<torch::Tensor> residual,
+                       c10::optional<torch::Tensor> w, torch::Tensor out, double eps);
 void ar_rmsnorm(torch::Tensor buf_ptrs, int64_t buf_offset_bytes, torch::Tensor sig_ptrs,
                 torch::Tensor epoch, torch::Tensor done, torch::Tensor status, int64_t rank,
                 int64_t world, int64_t M, int64_t H, c10::optional<torch::Tensor> residual,
@@ -125,6 +133,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("w4a16_gemm", &cb::w4a16_gemm);
   m.def("w4a16_workspace_floats", &cb::w4a16_workspace_floats);
   m.def("w4a16_counter_count", &cb::w4a16_counter_count);
+  m.def("w4a16_gemm_push", &cb::w4a16_gemm_push);
   m.def("w4a16_plan", &cb::w4a16_plan);
   m.def("w4a16_set_trace", &cb::w4a16_set_trace);
   m.def("set_pdl", &cb::set_pdl);
@@ -147,6 +156,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &cb::sample);
   m.def("spec_verify", &cb::spec_verify);
   m.def("ar_rmsnorm", &cb::ar_rmsnorm);
+  m.def("ar_rmsnorm_pushed", &cb::ar_rmsnorm_pushed);
   m.def("w4a16_gemm_grouped", &cb::w4a16_gemm_grouped);
   m.def("moe_topk_gate", &cb::moe_topk_gate);
   m.def("moe_permute", &cb::moe_permute);

@@ -73,6 +73,10 @@ struct ArArgs {
   bf16* out;                    // [M, H]
   int rank, world, M, H, ldr, ldo;
   float eps;
+  // 1: signal the peers (the partials are in each rank's own buffer);
+  // 0: the producing GEMM already pushed every rank's partial into this
+  // rank's slots (bufs[] are local) and raised the flags.
+  int signal;
 };
 
 __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_kernel(const ArArgs a) {
@@ -89,7 +93,7 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_kernel(const ArArgs a) 
   const int e = s_epoch;
   // 1. signal peers (one CTA does it; the partials were written by the
   //    previous kernel on this stream, so they are complete here).
-  if (blockIdx.x == 0 && threadIdx.x < a.world) {
+  if (a.signal && blockIdx.x == 0 && threadIdx.x < a.world) {
     __threadfence_system();
     st_release_sys(a.sigs[threadIdx.x] + a.rank, e);
   }
@@ -233,7 +237,48 @@ void ar_rmsnorm(torch::Tensor buf_ptrs, int64_t buf_offset_bytes, torch::Tensor 
   a.M = (int)M;
   a.H = (int)H;
   a.eps = (float)eps;
+  a.signal = 1;
   // Every CTA must be resident at once (they wait on peers): at most one per SM.
+  const int grid = (int)std::min<int64_t>(M, std::min(num_sms(), 128));
+  launch_kernel(ar_rmsnorm_kernel, dim3(grid), dim3(kArThreads), 0,
+                at::cuda::getCurrentCUDAStream(), a);
+}
+
+// The all-reduce after a pushing GEMM (w4a16_gemm_push): slot_ptrs are the
+// `world` receive slots in THIS rank's memory (slot p holds rank p's
+// partial), sig_ptrs[rank] is this rank's pad that the GEMMs' last tiles
+// raise.  Waits for every rank's flag, sums the slots in rank order, adds
+// the residual and applies RMSNorm, like ar_rmsnorm.
+void ar_rmsnorm_pushed(torch::Tensor slot_ptrs, torch::Tensor sig_ptrs, torch::Tensor epoch,
+                       torch::Tensor done, torch::Tensor status, int64_t rank, int64_t world,
+                       int64_t M, int64_t H, c10::optional<torch::Tensor> residual,
+                       c10::optional<torch::Tensor> w, torch::Tensor out, double eps) {
+  TORCH_CHECK(world <= kMaxRanks, "at most 8 ranks");
+  TORCH_CHECK(H % 8 == 0 && H / 8 <= 2 * kArThreads, "hidden size unsupported");
+  TORCH_CHECK(slot_ptrs.device().is_cpu() && sig_ptrs.device().is_cpu(), "pointer lists on host");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(out.device());
+  ArArgs a{};
+  auto bp = slot_ptrs.accessor<int64_t, 1>();
+  auto sp = sig_ptrs.accessor<int64_t, 1>();
+  for (int p = 0; p < world; ++p) {
+    a.bufs[p] = reinterpret_cast<const bf16*>(bp[p]);
+    a.sigs[p] = reinterpret_cast<int*>(sp[p]);
+  }
+  a.epoch = epoch.data_ptr<int>();
+  a.done = done.data_ptr<int>();
+  a.status = status.data_ptr<int>();
+  a.residual = residual.has_value() ? reinterpret_cast<bf16*>(residual->data_ptr()) : nullptr;
+  a.ldr = residual.has_value() ? (int)residual->stride(0) : 0;
+  a.w = w.has_value() ? reinterpret_cast<const bf16*>(w->data_ptr()) : nullptr;
+  a.out = reinterpret_cast<bf16*>(out.data_ptr());
+  a.ldo = (int)out.stride(0);
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.M = (int)M;
+  a.H = (int)H;
+  a.eps = (float)eps;
+  a.signal = 0;
   const int grid = (int)std::min<int64_t>(M, std::min(num_sms(), 128));
   launch_kernel(ar_rmsnorm_kernel, dim3(grid), dim3(kArThreads), 0,
                 at::cuda::getCurrentCUDAStream(), a);

@@ -125,6 +125,17 @@ struct GemmArgs {
   // Launched with programmatic stream serialisation: the producer issues the
   // first stages' weight copies (constant data) before griddepcontrol.wait.
   int pdl;
+  // Tensor-parallel push (row-parallel GEMM, store epilogue), npeer > 0:
+  // every output tile is stored into each rank's receive slot for this rank
+  // (peer_out[q] + row * ldo, plain P2P stores over NVLink) instead of out,
+  // and the last tile of the launch to finish raises this rank's flag in
+  // every rank's signal pad (peer_sig[q][my_rank] = *push_epoch + 1), after
+  // a system-scope fence.
+  __nv_bfloat16* peer_out[8];
+  int* peer_sig[8];
+  int npeer, my_rank;
+  int* push_done;          // local: tiles finished in this launch (self-resetting)
+  const int* push_epoch;   // local: last completed all-reduce epoch
 };
 
 __device__ __forceinline__ __nv_bfloat16* gemm_out_row(const GemmArgs& a, int gm) {
@@ -534,7 +545,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if constexpr (EPI == kEpiResid) y += __bfloat162float(re[e]);
                 oe[e] = __float2bfloat16(y);
               }
-              *reinterpret_cast<uint4*>(gemm_out_row(args, gm) + n0 + r8) = o;
+              if (args.npeer > 0) {
+                for (int q = 0; q < args.npeer; ++q)
+                  *reinterpret_cast<uint4*>(args.peer_out[q] + (size_t)gm * args.ldo + n0 + r8) =
+                      o;
+              } else {
+                *reinterpret_cast<uint4*>(gemm_out_row(args, gm) + n0 + r8) = o;
+              }
             }
           }
         } else {
@@ -546,7 +563,33 @@ __global__ void __launch_bounds__(kThreads, 1)
               float y = tile[rr * (MT + 1) + m];
               if constexpr (EPI == kEpiResid)
                 y += __bfloat162float(args.residual[(size_t)gm * args.ldr + n0 + rr]);
-              gemm_out_row(args, gm)[n0 + rr] = __float2bfloat16(y);
+              if (args.npeer > 0) {
+                for (int q = 0; q < args.npeer; ++q)
+                  args.peer_out[q][(size_t)gm * args.ldo + n0 + rr] = __float2bfloat16(y);
+              } else {
+                gemm_out_row(args, gm)[n0 + rr] = __float2bfloat16(y);
+              }
+            }
+          }
+        }
+        if (args.npeer > 0) {
+          // This tile is in every rank's slot: count it; the launch's last
+          // tile raises the flag in every rank's pad.
+          __threadfence_system();
+          named_bar_sync(1, kDequantThreads);
+          if (t == 0) {
+            const int total = (int)(gridDim.x * gridDim.z);
+            const int old = atomicAdd(args.push_done, 1);
+            if (old == total - 1) {
+              *args.push_done = 0;  // ready for the next launch
+              const int e = *reinterpret_cast<const volatile int*>(args.push_epoch) + 1;
+              __threadfence_system();
+              for (int q = 0; q < args.npeer; ++q) {
+                asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(args.peer_sig[q] +
+                                                                          args.my_rank),
+                             "r"(e)
+                             : "memory");
+              }
             }
           }
         }
@@ -785,6 +828,69 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
     else if (epilogue == kEpiSilu) dispatch_mt<32, kEpiSilu>(p.MT, tmap, a, grid, stream);
     else dispatch_mt<32, kEpiResid>(p.MT, tmap, a, grid, stream);
   }
+}
+
+// Row-parallel GEMM of one tensor-parallel rank with the push epilogue (see
+// GemmArgs::npeer): out_ptrs / sig_ptrs are int64 host tensors of `world`
+// device addresses (every rank's receive slot for this rank, every rank's
+// signal pad), ldo the slot's row pitch.  Always the split-K tcgen05 kernel.
+void w4a16_gemm_push(torch::Tensor x, torch::Tensor wblob, int64_t N, int64_t group_size,
+                     torch::Tensor out_ptrs, int64_t ldo, torch::Tensor sig_ptrs, int64_t my_rank,
+                     torch::Tensor push_done, torch::Tensor push_epoch, torch::Tensor ws,
+                     torch::Tensor counters, torch::Tensor status) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(1) == 1, "x");
+  TORCH_CHECK(out_ptrs.device().is_cpu() && sig_ptrs.device().is_cpu(), "pointer lists on host");
+  const int world = (int)out_ptrs.numel();
+  TORCH_CHECK(world >= 1 && world <= 8 && sig_ptrs.numel() == world, "1..8 ranks");
+  const int M = (int)x.size(0);
+  const int K = (int)x.size(1);
+  TORCH_CHECK(K % 128 == 0 && N % 128 == 0, "K and N must be multiples of 128");
+  TORCH_CHECK(ldo % 8 == 0 && ldo >= N, "slot row pitch");
+  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+              "x must be 16-byte aligned");
+  const int64_t blob_bytes =
+      (int64_t)(N / 128) * (K / 128) * (8192 + 128 * (128 / group_size) * 2);
+  TORCH_CHECK(wblob.numel() == blob_bytes, "weight blob has wrong size");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(x.device());
+  GemmPlanInfo p = plan_gemm(M, (int)N, K, 0);
+  if (p.splits > 1) {
+    TORCH_CHECK(ws.numel() >= (int64_t)p.splits * p.token_tiles * p.MT * N, "workspace too small");
+    TORCH_CHECK(counters.numel() >= (int64_t)p.token_tiles * p.row_tiles, "counters too small");
+  }
+  GemmArgs a{};
+  a.wblob = wblob.data_ptr<uint8_t>();
+  a.ws = p.splits > 1 ? ws.data_ptr<float>() : nullptr;
+  a.counters = p.splits > 1 ? counters.data_ptr<int>() : nullptr;
+  a.status = status.data_ptr<int>();
+  a.M = M;
+  a.N = (int)N;
+  a.K = K;
+  a.ldo = (int)ldo;
+  a.kb_per_split = p.kbps;
+  a.splits = p.splits;
+  a.trace = g_gemm_trace;
+  a.pdl = pdl_flag();
+  auto op = out_ptrs.accessor<int64_t, 1>();
+  auto sp = sig_ptrs.accessor<int64_t, 1>();
+  bool aligned = true;
+  for (int q = 0; q < world; ++q) {
+    a.peer_out[q] = reinterpret_cast<__nv_bfloat16*>(op[q]);
+    a.peer_sig[q] = reinterpret_cast<int*>(sp[q]);
+    aligned = aligned && (op[q] % 16 == 0);
+  }
+  a.vec_out = aligned ? 1 : 0;
+  a.npeer = world;
+  a.my_rank = (int)my_rank;
+  a.push_done = push_done.data_ptr<int>();
+  a.push_epoch = push_epoch.data_ptr<int>();
+  CUtensorMap tmap = make_tmap_2d_bf16(x.data_ptr(), (uint64_t)K, (uint64_t)M,
+                                       (uint64_t)x.stride(0) * 2, 64, (uint32_t)p.MT,
+                                       CU_TENSOR_MAP_SWIZZLE_128B);
+  dim3 grid(p.row_tiles, p.splits, p.token_tiles);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (group_size == 128) dispatch_mt<128, kEpiStore>(p.MT, tmap, a, grid, stream);
+  else dispatch_mt<32, kEpiStore>(p.MT, tmap, a, grid, stream);
 }
 
 // Grouped (MoE) GEMM: x holds the tokens of all experts in expert order,

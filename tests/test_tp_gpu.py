@@ -1,4 +1,5 @@
-"""Tensor parallelism on 2+ GPUs: peer-memory fused all-reduce vs NCCL vs TP=1.
+"""Tensor parallelism on 2+ GPUs: peer-memory fused all-reduce, the GEMM
+that pushes its partial into every rank's slots, NCCL, and TP=1.
 
 Runs as child processes (one per GPU, NCCL).  Skipped when fewer than two
 GPUs are visible.
@@ -44,7 +45,7 @@ def _logits(m, prompts, decode_tokens):
     return pre, dec
 
 
-def _worker(rank, world, port, prompts, decode_tokens, fused, q):
+def _worker(rank, world, port, prompts, decode_tokens, mode, q, cfg_name="tiny-llama-128"):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -57,10 +58,11 @@ def _worker(rank, world, port, prompts, decode_tokens, fused, q):
         from cascadia_b200.models.llama import LlamaModel, TPGroup
         from cascadia_b200.parallel.tp import FusedTP
 
-        cfg = get_config("tiny-llama-128")
+        cfg = get_config(cfg_name)
         tp = TPGroup(rank, world, dist.group.WORLD)
-        if fused:
-            tp.fused = FusedTP(dist.group.WORLD, rank, world, dev, cfg.hidden_size, 64)
+        if mode in ("fused", "push"):
+            tp.fused = FusedTP(dist.group.WORLD, rank, world, dev, cfg.hidden_size, 64,
+                               push=mode == "push")
         m = LlamaModel(cfg, dev, tp=tp).init_random(seed=17, gen_device="cpu")
         m.allocate_kv(64)
         out = _logits(m, prompts, decode_tokens)
@@ -73,11 +75,12 @@ def _worker(rank, world, port, prompts, decode_tokens, fused, q):
         dist.destroy_process_group()
 
 
-def _run(world, fused, prompts, decode_tokens):
+def _run(world, mode, prompts, decode_tokens, cfg_name="tiny-llama-128"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, world, port, prompts, decode_tokens, fused, q))
+    ps = [ctx.Process(target=_worker, args=(r, world, port, prompts, decode_tokens, mode, q,
+                                            cfg_name))
           for r in range(world)]
     for p in ps:
         p.start()
@@ -101,9 +104,34 @@ def test_fused_tp_matches_nccl_and_tp1():
     m.allocate_kv(64)
     ref_pre, ref_dec = _logits(m, prompts, decode_tokens)
     world = 2 if WORLD < 4 else min(WORLD, 4)
-    (f_pre, f_dec), st = _run(world, True, prompts, decode_tokens)
+    (f_pre, f_dec), st = _run(world, "fused", prompts, decode_tokens)
     assert st == 0
-    (n_pre, n_dec), _ = _run(world, False, prompts, decode_tokens)
+    (p_pre, p_dec), st = _run(world, "push", prompts, decode_tokens)
+    assert st == 0
+    (n_pre, n_dec), _ = _run(world, "nccl", prompts, decode_tokens)
     scale = ref_pre.abs().max().item()
-    for a, b in ((f_pre, ref_pre), (f_dec, ref_dec), (n_pre, ref_pre), (n_dec, ref_dec)):
+    for a, b in ((f_pre, ref_pre), (f_dec, ref_dec), (n_pre, ref_pre), (n_dec, ref_dec),
+                 (p_pre, ref_pre), (p_dec, ref_dec)):
+        assert (a - b).abs().max().item() <= 0.03 * scale + 1e-3
+    # Prefill rows run the same GEMM kernel and sum the same bf16 partials
+    # in rank order either way: pushing changes nothing in the result.
+    assert torch.equal(p_pre, f_pre)
+
+
+@pytest.mark.skipif(WORLD < 8, reason="needs 8 GPUs")
+def test_push_tp8_matches_tp1():
+    from cascadia_b200.models.config import get_config
+    from cascadia_b200.models.llama import LlamaModel
+
+    cfg = get_config("tiny-llama-kv8")
+    g = torch.Generator().manual_seed(6)
+    prompts = [torch.randint(3, cfg.vocab_size, (n,), generator=g).tolist() for n in (17, 40)]
+    decode_tokens = [5, 9]
+    m = LlamaModel(cfg, torch.device("cuda", 0)).init_random(seed=17, gen_device="cpu")
+    m.allocate_kv(64)
+    ref_pre, ref_dec = _logits(m, prompts, decode_tokens)
+    (p_pre, p_dec), st = _run(8, "push", prompts, decode_tokens, "tiny-llama-kv8")
+    assert st == 0
+    scale = ref_pre.abs().max().item()
+    for a, b in ((p_pre, ref_pre), (p_dec, ref_dec)):
         assert (a - b).abs().max().item() <= 0.03 * scale + 1e-3
