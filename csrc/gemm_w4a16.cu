@@ -513,6 +513,23 @@ __global__ void __launch_bounds__(kThreads, 1)
               gemm_out_row(args, gm)[rt * 64 + j] = __float2bfloat16(y);
             }
           }
+        } else if (args.npeer > 0) {
+          // Push to every rank's slot: 16 consecutive threads write one
+          // row's 256 contiguous bytes, so that a warp's P2P stores are two
+          // full 256-byte row pieces (NVLink carries them as a few large
+          // writes instead of one 16-byte write per thread).
+          for (int idx = t; idx < 16 * MT; idx += kDequantThreads) {
+            const int r8 = (idx & 15) * 8, m = idx >> 4;
+            const int gm = m_base + m;
+            if (gm < m_lim) {
+              uint4 o;
+              __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) oe[e] = __float2bfloat16(tile[(r8 + e) * (MT + 1) + m]);
+              for (int q = 0; q < args.npeer; ++q)
+                *reinterpret_cast<uint4*>(args.peer_out[q] + (size_t)gm * args.ldo + n0 + r8) = o;
+            }
+          }
         } else if (args.vec_out) {
           // 8 outputs (16 bytes) per thread and step, token index fastest
           // (conflict-free tile reads); residual loads all issued up front.
@@ -545,13 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if constexpr (EPI == kEpiResid) y += __bfloat162float(re[e]);
                 oe[e] = __float2bfloat16(y);
               }
-              if (args.npeer > 0) {
-                for (int q = 0; q < args.npeer; ++q)
-                  *reinterpret_cast<uint4*>(args.peer_out[q] + (size_t)gm * args.ldo + n0 + r8) =
-                      o;
-              } else {
-                *reinterpret_cast<uint4*>(gemm_out_row(args, gm) + n0 + r8) = o;
-              }
+              *reinterpret_cast<uint4*>(gemm_out_row(args, gm) + n0 + r8) = o;
             }
           }
         } else {
