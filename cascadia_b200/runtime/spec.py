@@ -8,8 +8,10 @@ One round for every running sequence at once (batched):
    n-gram prompt-lookup table (crates/cascadia-engine-sparse-moe/src/ngram_draft.rs);
 2. verify: ONE target forward over ``[pending, d1 .. dk]`` per sequence
    (a ragged multi-token batch through the prefill attention kernel), LM head
-   on every row, argmax per row, and the device verify kernel
-   (``ops.spec_verify``: longest accepted prefix + correction token);
+   on every row, then on one GPU a single kernel (``ops.spec_verify_fused``:
+   argmax of every row, longest accepted prefix, correction token, accepted
+   count and the advanced KV length), with tensor parallelism the
+   vocab-parallel argmax merge followed by ``ops.spec_verify``;
 3. rewind: the target's KV length is reset to the accepted prefix (paged
    blocks past it go back to the pool), the draft's likewise.  No data moves.
 
@@ -159,9 +161,30 @@ def verify_batch(m, seq_ids: List[str], pending: List[int], drafts: List[List[in
         for r in rows:
             hidden_out.append(hidden[o:o + len(r)])
             o += len(r)
-    picks = m.greedy(m.head(hidden)).to(torch.int32)  # argmax of every row
     kmax = max(len(d) for d in drafts)
     B = len(rows)
+    if m.device.type == "cuda" and m.tp.size == 1:
+        # One kernel: argmax of every row, comparison with the drafts,
+        # correction token, accepted count and the new KV lengths.
+        logits = m.head(hidden)[:, :m.vocab_valid]
+        offs = np.cumsum([0] + [len(r) for r in rows]).astype(np.int32)
+        row_seq = np.repeat(np.arange(B, dtype=np.int32), [len(r) for r in rows])
+        dr = np.full((B, max(kmax, 1)), -1, dtype=np.int32)
+        for i, d in enumerate(drafts):
+            dr[i, :len(d)] = d
+        packed = torch.from_numpy(np.concatenate([offs, row_seq, dr.reshape(-1),
+                                                  np.asarray(kv_lens, np.int32)]))
+        dev = packed.to(m.device, non_blocking=True)
+        o = 0
+        row_start_t = dev[o:o + B + 1]; o += B + 1
+        row_seq_t = dev[o:o + len(row_seq)]; o += len(row_seq)
+        dr_t = dev[o:o + dr.size].view(B, dr.shape[1]); o += dr.size
+        kvl = dev[o:o + B]
+        out = torch.empty(B, dr.shape[1] + 2, dtype=torch.int32, device=m.device)
+        ops.spec_verify_fused(logits, row_seq_t, row_start_t, dr_t, kvl, out)
+        out = out.cpu()
+        return [out[i, :int(out[i, -1])].tolist() for i in range(B)]
+    picks = m.greedy(m.head(hidden)).to(torch.int32)  # argmax of every row
     if kmax == 0:
         return [[int(t)] for t in picks.cpu()]
     # Pad to [B, kmax+1] / [B, kmax] for the device verify kernel; padded

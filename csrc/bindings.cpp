@@ -114,6 +114,9 @@ void argmax(torch::Tensor logits, torch::Tensor out_idx, c10::optional<torch::Te
 void sample(torch::Tensor logits, torch::Tensor params, c10::optional<torch::Tensor> history,
             c10::optional<torch::Tensor> hist_len, torch::Tensor work, torch::Tensor seeds,
             torch::Tensor offsets, torch::Tensor out);
+void spec_verify_fused(torch::Tensor logits, torch::Tensor row_seq, torch::Tensor row_start,
+                       torch::Tensor draft, torch::Tensor picks, torch::Tensor done,
+                       torch::Tensor kv_len, torch::Tensor out);
 void spec_verify(torch::Tensor target, torch::Tensor draft, torch::Tensor out);
 void head_rmsnorm(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, int64_t Hq,
                   int64_t Hkv, int64_t D, double eps);
@@ -155,6 +158,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax", &cb::argmax);
   m.def("sample", &cb::sample);
   m.def("spec_verify", &cb::spec_verify);
+  m.def("spec_verify_fused", &cb::spec_verify_fused);
   m.def("ar_rmsnorm", &cb::ar_rmsnorm);
   m.def("ar_rmsnorm_pushed", &cb::ar_rmsnorm_pushed);
   m.def("w4a16_gemm_grouped", &cb::w4a16_gemm_grouped);

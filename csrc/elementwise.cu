@@ -665,11 +665,11 @@ void sample(torch::Tensor logits, torch::Tensor params, c10::optional<torch::Ten
 // target: int32 [B, k+1] greedy target tokens for rows [prev, d1..dk];
 // draft: int32 [B, k].  out: int32 [B, k+2] = accepted tokens (accepted drafts
 // followed by the correction/bonus token), then the count n = accepted + 1 in
-// the last column.
+// the last column.  One thread per sequence.
 __global__ void spec_verify_kernel(const int* __restrict__ target, const int* __restrict__ draft,
-                                   int k, int* __restrict__ out) {
+                                   int B, int k, int* __restrict__ out) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= gridDim.x * blockDim.x) return;
+  if (b >= B) return;
   const int* t = target + (size_t)b * (k + 1);
   const int* d = draft + (size_t)b * k;
   int* o = out + (size_t)b * (k + 2);
@@ -688,9 +688,136 @@ void spec_verify(torch::Tensor target, torch::Tensor draft, torch::Tensor out) {
   const int k = (int)draft.size(1);
   if (B == 0) return;
   const c10::cuda::CUDAGuard guard(target.device());
-  spec_verify_kernel<<<B, 1, 0, at::cuda::getCurrentCUDAStream()>>>(
-      target.data_ptr<int>(), draft.data_ptr<int>(), k, out.data_ptr<int>());
+  const int threads = 128;
+  spec_verify_kernel<<<(B + threads - 1) / threads, threads, 0,
+                       at::cuda::getCurrentCUDAStream()>>>(
+      target.data_ptr<int>(), draft.data_ptr<int>(), B, k, out.data_ptr<int>());
   CB_CUDA_CHECK(cudaGetLastError());
+}
+
+// Fused verify of one speculative round (whole vocabulary on this GPU):
+// one CTA per verify row takes the argmax of its logits row (lowest index on
+// ties), and the last CTA to finish among a sequence's rows compares the
+// drafts with the target's picks, writes out[b] = accepted drafts, the
+// correction token, -1 padding and the count (accepted + 1) in column k + 1,
+// and sets kv_len[b] += count: the paged-KV length after the round (the
+// forward wrote entries for every row; those past the accepted prefix are
+// dropped).  picks: int32 [R] scratch; done: int32 [B], zero on entry and
+// zero again on exit.
+__global__ void __launch_bounds__(1024) spec_verify_fused_kernel(
+    const bf16* __restrict__ logits, int ld, int V, const int* __restrict__ row_seq,
+    const int* __restrict__ row_start, const int* __restrict__ draft, int k,
+    int* __restrict__ picks, int* __restrict__ done, int* __restrict__ kv_len,
+    int* __restrict__ out) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const int r = blockIdx.x;
+  const bf16* x = logits + (size_t)r * ld;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  const bool vec_ok = (V % 8 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  if (vec_ok) {
+    for (int i = threadIdx.x * 8; i < V; i += blockDim.x * 8) {
+      const uint4 u = *reinterpret_cast<const uint4*>(x + i);
+      const bf16* e = reinterpret_cast<const bf16*>(&u);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float v = __bfloat162float(e[q]);
+        if (v > best) {
+          best = v;
+          bi = i + q;
+        }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float v = __bfloat162float(x[i]);
+      if (v > best) {
+        best = v;
+        bi = i;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ int s_last;
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    sv[w] = best;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    best = l < nw ? sv[l] : -INFINITY;
+    bi = l < nw ? si[l] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (l == 0) {
+      picks[r] = bi == 0x7fffffff ? 0 : bi;
+      __threadfence();
+      const int b = row_seq[r];
+      const int n = row_start[b + 1] - row_start[b];
+      const int old = atomicAdd(&done[b], 1);
+      s_last = old == n - 1 ? 1 : 0;
+    }
+  }
+  __syncthreads();
+  if (!s_last || threadIdx.x != 0) return;
+  __threadfence();
+  const int b = row_seq[r];
+  const int r0 = row_start[b];
+  const int n = row_start[b + 1] - r0;
+  done[b] = 0;  // ready for the next round
+  const int* d = draft + (size_t)b * k;
+  int* o = out + (size_t)b * (k + 2);
+  const volatile int* pk = picks;
+  int acc = 0;
+  while (acc < n - 1 && d[acc] == pk[r0 + acc]) {
+    o[acc] = d[acc];
+    ++acc;
+  }
+  o[acc] = pk[r0 + acc];
+  for (int i = acc + 1; i < k + 1; ++i) o[i] = -1;
+  o[k + 1] = acc + 1;
+  kv_len[b] += acc + 1;
+}
+
+void spec_verify_fused(torch::Tensor logits, torch::Tensor row_seq, torch::Tensor row_start,
+                       torch::Tensor draft, torch::Tensor picks, torch::Tensor done,
+                       torch::Tensor kv_len, torch::Tensor out) {
+  TORCH_CHECK(logits.scalar_type() == at::kBFloat16 && logits.stride(1) == 1, "bf16 logits");
+  const int R = (int)logits.size(0);
+  const int V = (int)logits.size(1);
+  const int B = (int)draft.size(0);
+  const int k = (int)draft.size(1);
+  TORCH_CHECK(row_seq.numel() >= R && row_start.numel() >= B + 1 && picks.numel() >= R &&
+                  done.numel() >= B && kv_len.numel() >= B && out.size(1) == k + 2,
+              "spec_verify_fused: buffer sizes");
+  if (R == 0) return;
+  const c10::cuda::CUDAGuard guard(logits.device());
+  launch_kernel(spec_verify_fused_kernel, dim3(R), dim3(1024), 0,
+                at::cuda::getCurrentCUDAStream(),
+                reinterpret_cast<const bf16*>(logits.data_ptr()), (int)logits.stride(0), V,
+                row_seq.data_ptr<int>(), row_start.data_ptr<int>(), draft.data_ptr<int>(), k,
+                picks.data_ptr<int>(), done.data_ptr<int>(), kv_len.data_ptr<int>(),
+                out.data_ptr<int>());
 }
 
 }  // namespace cb

@@ -381,3 +381,45 @@ def test_attn_sliding_window_decode_and_prefill(d, window, sinks):
         e = ref.attention(qp[row:row + qlen[b]].view(-1, hq, d), k, v, pos, scale, window, sinks)
         _close(out[row:row + qlen[b]].view(-1, hq, d), e, rtol=2e-2, atol=2e-2)
         row += qlen[b]
+
+
+@pytest.mark.parametrize("lens", [[5], [1, 5, 3], [2, 2, 2, 2, 5, 1]])
+def test_spec_verify_fused(lens):
+    """Fused verify (argmax of every row + accept + correction + KV length)
+    against the row-wise argmax and the CPU reference rule."""
+    g = torch.Generator().manual_seed(sum(lens))
+    V = 1000
+    R, B, k = sum(lens), len(lens), max(lens) - 1
+    logits = (torch.randn(R, V, generator=g) * 3).to(torch.bfloat16)
+    picks = logits.float().argmax(-1)
+    offs = [0]
+    for n in lens:
+        offs.append(offs[-1] + n)
+    drafts = []
+    for b, n in enumerate(lens):
+        # Plant matches for a prefix of random length, then a mismatch.
+        d = [int(picks[offs[b] + i]) for i in range(n - 1)]
+        cut = int(torch.randint(0, n, (1,), generator=g))
+        if cut < n - 1:
+            d[cut] = (d[cut] + 1) % V
+        drafts.append(d)
+    dr = torch.full((B, max(k, 1)), -1, dtype=torch.int32)
+    for b, d in enumerate(drafts):
+        dr[b, :len(d)] = torch.tensor(d, dtype=torch.int32)
+    row_seq = torch.repeat_interleave(torch.arange(B, dtype=torch.int32),
+                                      torch.tensor(lens)).to(DEV)
+    kv = torch.tensor([100 + 10 * b for b in range(B)], dtype=torch.int32, device=DEV)
+    out = torch.empty(B, dr.shape[1] + 2, dtype=torch.int32, device=DEV)
+    for _ in range(2):  # twice: the per-sequence counters must reset
+        kv_run = kv.clone()
+        ops.spec_verify_fused(logits.to(DEV), row_seq, torch.tensor(offs, dtype=torch.int32,
+                                                                    device=DEV),
+                              dr.to(DEV), kv_run, out)
+        torch.cuda.synchronize()
+        _status_ok()
+        o = out.cpu()
+        for b, n in enumerate(lens):
+            want = ref.spec_verify([int(picks[offs[b] + i]) for i in range(n)], drafts[b])
+            cnt = int(o[b, -1])
+            assert o[b, :cnt].tolist() == want
+            assert int(kv_run[b]) == 100 + 10 * b + cnt
