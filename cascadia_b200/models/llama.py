@@ -256,6 +256,25 @@ class LlamaModel:
             lw.sparse = SparseFFN(gu.rows(0, inter), gu.rows(inter, 2 * inter), dn, self.device,
                                   tau_all, taus[i] if taus is not None else None)
 
+    def early_exit(self, num_layers: int) -> "LlamaModel":
+        """A model that shares this one's embedding, first ``num_layers``
+        layers, final norm and LM head (no weight copies) and has its own KV
+        cache: the draft of self-speculative decoding by early exit
+        (LayerSkip, Elhoushi et al. 2024).  Single GPU, whole model only."""
+        assert self.tp.size == 1 and self.layer_start == 0 and self.has_embed and self.has_head
+        assert 0 < num_layers <= len(self.layers)
+        import copy
+
+        cfg = copy.copy(self.cfg)
+        cfg.num_layers = num_layers
+        d = LlamaModel(cfg, self.device)
+        d.cos_sin = self.cos_sin
+        d.embed = self.embed
+        d.layers = self.layers[:num_layers]
+        d.final_norm = self.final_norm
+        d.lm_head = self.lm_head
+        return d
+
     def allocate_kv(self, num_blocks: int) -> KVCache:
         self.kv = KVCache(self.num_local_layers, num_blocks, self.hkv, self.d, self.device)
         return self.kv

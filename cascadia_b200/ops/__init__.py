@@ -283,18 +283,23 @@ def spec_verify(target, draft, out):
 _VERIFY_SCRATCH: dict = {}
 
 
-def spec_verify_fused(logits, row_seq, row_start, draft, kv_len, out):
+def spec_verify_fused(logits, row_seq, row_start, draft, kv_len, out, scratch=None):
     """One kernel for a speculative round on a single GPU: argmax of every
     verify row of `logits` [R, V], comparison with `draft` [B, k] (-1
     padded), out [B, k+2] = accepted drafts + correction token, -1 padding,
-    count in the last column, and kv_len[b] += count on the device."""
+    count in the last column, and kv_len[b] += count on the device.
+    ``scratch`` = (picks int32 [>=R], done int32 [>=B] zeroed; the kernel
+    leaves it zeroed): a captured graph passes its own, eager calls share a
+    cached pair."""
     R, B = logits.shape[0], draft.shape[0]
-    key = logits.device.index or 0
-    sc = _VERIFY_SCRATCH.get(key)
-    if sc is None or sc[0].numel() < R or sc[1].numel() < B:
-        sc = (torch.empty(max(R, 256), dtype=torch.int32, device=logits.device),
-              torch.zeros(max(B, 64), dtype=torch.int32, device=logits.device))
-        _VERIFY_SCRATCH[key] = sc
+    sc = scratch
+    if sc is None:
+        key = logits.device.index or 0
+        sc = _VERIFY_SCRATCH.get(key)
+        if sc is None or sc[0].numel() < R or sc[1].numel() < B:
+            sc = (torch.empty(max(R, 256), dtype=torch.int32, device=logits.device),
+                  torch.zeros(max(B, 64), dtype=torch.int32, device=logits.device))
+            _VERIFY_SCRATCH[key] = sc
     ext().spec_verify_fused(logits, row_seq, row_start, draft, sc[0], sc[1], kv_len, out)
     LAUNCHES.add(1)
     return out

@@ -21,6 +21,7 @@ tokens the target itself would have produced).
 """
 from __future__ import annotations
 
+import time
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Sequence, Tuple
 
@@ -29,6 +30,7 @@ import torch
 
 from .. import ops
 from ..models.llama import build_batch
+from .generator import DecodeGraph
 from .kv_cache import BLOCK_SIZE
 
 MIN_NGRAM = 2
@@ -138,20 +140,108 @@ class SpecStats:
     drafted: int = 0
     accepted: int = 0
     emitted: int = 0
+    draft_s: float = 0.0    # host wall time in the drafter (ends with a device sync)
+    verify_s: float = 0.0   # host wall time in verify_batch (ends with a device sync)
 
     @property
     def accept_rate(self) -> float:
         return self.accepted / self.drafted if self.drafted else 0.0
 
 
+class VerifyGraph(DecodeGraph):
+    """A captured verify step for B sequences of exactly T rows each (the
+    usual round: every sequence drafted T-1 tokens), run as a decode step of
+    B*T rows: row (b, j) is token j of sequence b at position p0+j with
+    sequence length p0+j+1 over sequence b's block table.  Every row's K/V
+    is written before the layer's attention runs, so row j sees exactly the
+    keys up to its own position (causal), and the split-KV decode attention
+    kernel serves the verify (the rows of one sequence re-read the same
+    blocks, from L2).  After the LM head and the argmax of every row, the
+    verify kernel writes the accepted drafts, the correction token and the
+    count; one D2H copy brings them back.  Plain decoding and verification
+    share every kernel."""
+
+    def __init__(self, m, B: int, T: int, W: int):
+        super().__init__(m, B * T, W, use_graph=True)
+        self.nseq, self.T = B, T
+        dev = m.device
+        # drafts [B, T-1] | KV lengths before the round [B], one H2D copy
+        self.vin_host = torch.zeros(B * T, dtype=torch.int32, pin_memory=True)
+        self.vin = torch.zeros(B * T, dtype=torch.int32, device=dev)
+        self.draft = self.vin[:B * (T - 1)].view(B, T - 1)
+        self.kv_len = self.vin[B * (T - 1):]
+        self.row_seq = torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(T)
+        self.row_start = torch.arange(0, (B + 1) * T, T, dtype=torch.int32, device=dev)
+        self.scratch = (torch.empty(B * T, dtype=torch.int32, device=dev),
+                        torch.zeros(B, dtype=torch.int32, device=dev))
+        self.out = torch.empty(B, T + 1, dtype=torch.int32, device=dev)
+        self.vout_host = torch.zeros(B, T + 1, dtype=torch.int32, pin_memory=True)
+
+    def _step(self):
+        m = self.model
+        m.embed_tokens(self.ids, out=self.hidden)
+        m.forward(self.batch_view, self.hidden)
+        self.logits = m.head(self.hidden)
+        if m.tp.size == 1:
+            # argmax of every row + accept + correction + KV length: one kernel
+            ops.spec_verify_fused(self.logits[:, :m.vocab_valid], self.row_seq, self.row_start,
+                                  self.draft, self.kv_len, self.out, self.scratch)
+        else:
+            self.next_ids = m.greedy(self.logits)
+            ops.spec_verify(self.next_ids.view(self.nseq, self.T), self.draft, self.out)
+        return self.out
+
+    def stage(self, seq_ids, rows: List[List[int]], kv_lens: List[int]):
+        m, kv, B, T = self.model, self.model.kv, self.nseq, self.T
+        pos = np.empty((B, T), dtype=np.int32)
+        slots = np.empty((B, T), dtype=np.int32)
+        table = np.zeros((B, T, self.W), dtype=np.int32)
+        for i, (sid, p0) in enumerate(zip(seq_ids, kv_lens)):
+            kv.reserve(sid, p0 + T)
+            kv.slide(sid, m.cfg, p0)
+            s = kv.seqs[sid]
+            s.length = max(s.length, p0 + T)
+            pos[i] = np.arange(p0, p0 + T)
+            slots[i] = s.slots(p0, p0 + T)
+            table[i, :, :len(s.blocks)] = np.maximum(s.blocks, 0)
+        self.fill(np.asarray(rows, dtype=np.int32).reshape(-1), pos.reshape(-1),
+                  slots.reshape(-1), pos.reshape(-1) + 1, table.reshape(B * T, self.W))
+        v = self.vin_host.numpy()
+        v[:B * (T - 1)] = np.asarray([r[1:] for r in rows], dtype=np.int32).reshape(-1)
+        v[B * (T - 1):] = kv_lens
+        self.upload()
+        self.vin.copy_(self.vin_host, non_blocking=True)
+
+    def verify(self) -> List[List[int]]:
+        if self.graph is None:
+            self.capture()
+        self.run()
+        self.vout_host.copy_(self.out, non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        return [r[:r[-1]] for r in self.vout_host.tolist()]
+
+
 def verify_batch(m, seq_ids: List[str], pending: List[int], drafts: List[List[int]],
-                 kv_lens: List[int], hidden_out: Optional[list] = None) -> List[List[int]]:
+                 kv_lens: List[int], hidden_out: Optional[list] = None,
+                 graphs: Optional[dict] = None, width: int = 0) -> List[List[int]]:
     """One target forward over ``[pending, *drafts]`` per sequence (positions
     from ``kv_lens``), argmax of every row, device verify.  Returns, per
     sequence, the accepted drafts followed by the correction token.  The
     caller rewinds the KV to ``kv_len + len(result)``.  ``hidden_out``, when
-    given, receives the pre-norm hidden rows of each sequence's forward."""
+    given, receives the pre-norm hidden rows of each sequence's forward.
+    With ``graphs`` (a dict the caller keeps) and every sequence carrying
+    the same number of drafts, the step replays a captured VerifyGraph."""
     rows = [[p] + d for p, d in zip(pending, drafts)]
+    T = len(rows[0])
+    if (graphs is not None and hidden_out is None and m.device.type == "cuda" and T > 1
+            and T <= 64 and width > 0 and all(len(r) == T for r in rows)):
+        w = -(-width // 64) * 64  # one graph for nearby table widths
+        key = (len(rows), T, w)
+        g = graphs.get(key)
+        if g is None:
+            g = graphs[key] = VerifyGraph(m, len(rows), T, w)
+        g.stage(seq_ids, rows, kv_lens)
+        return g.verify()
     batch = build_batch(m, seq_ids, [len(r) for r in rows], kv_lens, False)
     flat = torch.tensor([t for r in rows for t in r], dtype=torch.int32).to(m.device)
     hidden = m.embed_tokens(flat)
@@ -231,7 +321,14 @@ class ModelDrafter:
                 d.kv.add_sequence(sid)
                 self.kv_len[sid] = 0
         starts = [self.kv_len[sid] for sid in seq_ids]
-        first = self.gen.prefill(seq_ids, [h[st:] for h, st in zip(histories, starts)], starts)
+        tails = [h[st:] for h, st in zip(histories, starts)]
+        if d.device.type == "cuda" and all(len(t) == 1 for t in tails):
+            # The usual round: only the last verified token is new, so the
+            # first draft step is a decode step too (graph replay, no eager
+            # ragged prefill).
+            first = self.gen.decode(seq_ids, [t[0] for t in tails], width)
+        else:
+            first = self.gen.prefill(seq_ids, tails, starts)
         for sid, h in zip(seq_ids, histories):
             self.kv_len[sid] = len(h)
         drafts = [[int(t)] for t in first.cpu()]
@@ -330,11 +427,18 @@ class SpecDecoder:
     model (``draft``: a model with its own KV cache) or n-gram drafts."""
 
     def __init__(self, target, draft=None, k: int = 4, ngram_k: int = DEFAULT_NGRAM_K,
-                 use_graph: bool = True, mtp=None):
+                 use_graph: bool = True, mtp=None, remote_draft: bool = False):
+        """With a tensor-parallel target the draft model lives on TP rank 0
+        only (``draft`` given there); every other rank passes
+        ``remote_draft=True`` and receives each round's drafts by a broadcast
+        over the TP group (the reference's driver-side draft,
+        crates/cascadia-engine-openvino/src/dist_spec.rs:958-1128)."""
         from .generator import BatchGenerator
 
         self.target = target
-        self.k = k if (draft is not None or mtp is not None) else ngram_k
+        self.remote_draft = remote_draft and draft is None
+        self.share = target.tp.size > 1 and (draft is not None or self.remote_draft)
+        self.k = k if (draft is not None or mtp is not None or self.remote_draft) else ngram_k
         self.tgen = BatchGenerator(target, use_graph=use_graph)
         if mtp is not None:
             self.drafter = MTPDrafter(mtp)
@@ -342,6 +446,25 @@ class SpecDecoder:
             self.drafter = ModelDrafter(draft, use_graph) if draft is not None else None
         self.mtp = self.drafter if mtp is not None else None
         self.stats = SpecStats()
+        self.use_graph = use_graph
+        self.vgraphs: Dict[tuple, VerifyGraph] = {}
+
+    def _share_drafts(self, drafts: Optional[List[List[int]]], n: int) -> List[List[int]]:
+        """Broadcast TP rank 0's drafts ([n, 1 + k] int32: length, tokens)."""
+        import torch.distributed as dist
+
+        tp = self.target.tp
+        dev = self.target.device
+        buf = torch.zeros(n, 1 + self.k, dtype=torch.int32)
+        if drafts is not None:
+            for i, d in enumerate(drafts):
+                buf[i, 0] = len(d)
+                buf[i, 1:1 + len(d)] = torch.tensor(d, dtype=torch.int32)
+        buf = buf.to(dev)
+        src = dist.get_global_rank(tp.group, 0) if tp.group is not None else 0
+        dist.broadcast(buf, src, group=tp.group)
+        rows = buf.cpu().tolist()
+        return [r[1:1 + r[0]] for r in rows]
 
     def generate(self, prompts: Sequence[Sequence[int]], max_new_tokens: int,
                  eos: Sequence[int] = (), prefix: str = "spec") -> List[List[int]]:
@@ -358,7 +481,7 @@ class SpecDecoder:
             if self.mtp is not None:
                 self.mtp.observe(sid, 0, list(p[1:]) + [int(t)], hid[o:o + len(p)])
                 o += len(p)
-            if self.drafter is None:
+            if self.drafter is None and not self.remote_draft:
                 s.ngram = NGramDraft(self.k)
                 s.ngram.extend(s.tokens)
             s.done = max_new_tokens <= 1 or int(t) in eos
@@ -367,16 +490,25 @@ class SpecDecoder:
             live = [s for s in states if not s.done]
             if not live:
                 break
+            t0 = time.perf_counter()
             if self.drafter is not None:
                 drafts = self.drafter.propose([s.sid for s in live], [s.tokens for s in live],
                                               self.k, width)
+            elif self.remote_draft:
+                drafts = None
             else:
                 drafts = [s.ngram.propose(self.k) for s in live]
+            if self.share:
+                drafts = self._share_drafts(drafts, len(live))
             # Never draft past the token budget.
             drafts = [d[:max(0, max_new_tokens - s.generated - 1)] for s, d in zip(live, drafts)]
             hid = [] if self.mtp is not None else None
+            t1 = time.perf_counter()
             accepted = verify_batch(m, [s.sid for s in live], [s.tokens[-1] for s in live],
-                                    drafts, [s.kv_len for s in live], hid)
+                                    drafts, [s.kv_len for s in live], hid,
+                                    self.vgraphs if self.use_graph else None, width)
+            self.stats.draft_s += t1 - t0
+            self.stats.verify_s += time.perf_counter() - t1
             self.stats.rounds += 1
             for i, (s, d, acc) in enumerate(zip(live, drafts, accepted)):
                 a = len(acc) - 1

@@ -715,6 +715,9 @@ void attn_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
   TORCH_CHECK(tiles.scalar_type() == at::kInt && tiles.is_contiguous() && tiles.size(1) == 4,
               "tiles must be int32 [n, 4]");
   TORCH_CHECK(q.stride(1) == 1 && out.stride(1) == 1, "q/out inner stride must be 1");
+  // The kernel reads each tile descriptor as one int4.
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(tiles.data_ptr()) % 16 == 0,
+              "tiles must start on a 16-byte boundary");
   if (n_tiles == 0) return;
   const c10::cuda::CUDAGuard guard(q.device());
   PrefillArgs a;

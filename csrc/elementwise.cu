@@ -686,6 +686,10 @@ __global__ void spec_verify_kernel(const int* __restrict__ target, const int* __
 void spec_verify(torch::Tensor target, torch::Tensor draft, torch::Tensor out) {
   const int B = (int)draft.size(0);
   const int k = (int)draft.size(1);
+  TORCH_CHECK(target.is_contiguous() && draft.is_contiguous() && out.is_contiguous() &&
+                  target.size(0) == B && target.size(1) == k + 1 && out.size(0) == B &&
+                  out.size(1) == k + 2,
+              "spec_verify: target [B, k+1], draft [B, k], out [B, k+2]");
   if (B == 0) return;
   const c10::cuda::CUDAGuard guard(target.device());
   const int threads = 128;
@@ -808,7 +812,8 @@ void spec_verify_fused(torch::Tensor logits, torch::Tensor row_seq, torch::Tenso
   const int B = (int)draft.size(0);
   const int k = (int)draft.size(1);
   TORCH_CHECK(row_seq.numel() >= R && row_start.numel() >= B + 1 && picks.numel() >= R &&
-                  done.numel() >= B && kv_len.numel() >= B && out.size(1) == k + 2,
+                  done.numel() >= B && kv_len.numel() >= B && out.size(1) == k + 2 &&
+                  draft.is_contiguous() && out.is_contiguous(),
               "spec_verify_fused: buffer sizes");
   if (R == 0) return;
   const c10::cuda::CUDAGuard guard(logits.device());

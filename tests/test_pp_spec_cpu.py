@@ -78,3 +78,63 @@ def test_distributed_spec_equals_greedy(mode):
         assert out == want, (rank, out, want)
         if mode == "draft":
             assert drafted > 0 and acc == drafted  # identical draft: all accepted
+
+
+def _tp_worker(rank, world, port, prompts, n_new, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        from cascadia_b200.models.config import get_config
+        from cascadia_b200.models.llama import LlamaModel, TPGroup
+        from cascadia_b200.runtime.spec import SpecDecoder
+
+        cfg = get_config("tiny-llama")
+        m = LlamaModel(cfg, "cpu", tp=TPGroup(rank, world, dist.group.WORLD)).init_random(
+            seed=13, gen_device="cpu")
+        m.allocate_kv(256)
+        draft = None
+        if rank == 0:
+            # The whole target as the draft: every draft must be accepted.
+            draft = LlamaModel(cfg, "cpu").init_random(seed=13, gen_device="cpu")
+            draft.allocate_kv(256)
+        dec = SpecDecoder(m, draft=draft, k=3, use_graph=False, remote_draft=rank != 0)
+        out = dec.generate(prompts, n_new)
+        q.put((rank, out, dec.stats.accepted, dec.stats.drafted))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_target_draft_on_rank0_equals_greedy():
+    """Target at TP=2, draft model on rank 0 only; the drafts reach rank 1 by
+    a broadcast each round.  Both ranks emit plain greedy tokens of the
+    full target."""
+    from cascadia_b200.models.config import get_config
+    from cascadia_b200.models.llama import LlamaModel
+    from cascadia_b200.runtime.generator import BatchGenerator
+
+    cfg = get_config("tiny-llama")
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(3, 500, (n,), generator=g).tolist() for n in (7, 12)]
+    n_new = 9
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_tp_worker, args=(r, 2, port, prompts, n_new, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    ref = LlamaModel(cfg, "cpu").init_random(seed=13, gen_device="cpu")
+    ref.allocate_kv(256)
+    want = BatchGenerator(ref, use_graph=False).generate(prompts, n_new)
+    for rank, out, acc, drafted in res:
+        assert out == want, (rank, out, want)
+        assert drafted > 0 and acc == drafted
