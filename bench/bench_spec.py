@@ -232,6 +232,18 @@ def main():
             report("emulated", best, stats, {"emulated_accept": rate, "q_per_position": round(q, 4),
                                              "outputs_equal_oracle": f"{same}/{B}"})
     if world > 1:
+        # CUDA graphs that captured NCCL calls keep the communicator busy:
+        # release every graph before tearing the process group down.
+        import gc
+
+        plain.graphs.clear()
+        sd.vgraphs.clear()
+        for d in (sd.drafter, getattr(sd.drafter, "inner", None)):
+            if d is not None and hasattr(d, "gen"):
+                d.gen.graphs.clear()
+        del plain, sd
+        gc.collect()
+        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
 
