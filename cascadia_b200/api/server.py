@@ -264,11 +264,17 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
                                      media_type="text/event-stream",
                                      headers={"Cache-Control": "no-cache",
                                               "x-accel-buffering": "no"})
+        done = False
         try:
             text, finish, completion, prompt_toks, error, lps = await _collect(task, stream)
+            done = True
         finally:
             sem.release()
             stats.end()
+            if not done:
+                # The client went away (the handler was cancelled): stop the
+                # generation instead of running it to max_tokens.
+                runner.cancel(task.task_id)
         if error is not None:
             health.ok = False
             return JSONResponse({"error": error}, status_code=500)
@@ -329,6 +335,7 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
         pending = ""    # text held back (possible stop-sequence prefix)
         lp_pending = []  # logprobs of tokens whose text is not emitted yet
         first = True
+        finished = False  # False on exit = the client disconnected mid-stream
 
         def frame(payload) -> bytes:
             return f"data: {json.dumps(payload, ensure_ascii=False)}\n\n".encode()
@@ -363,6 +370,7 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
                     health.ok = False
                     yield frame({"id": task.task_id, "object": "error",
                                  "error": {"message": c.error, "type": "engine_error"}})
+                    finished = True
                     yield b"data: [DONE]\n\n"
                     return
                 completion += c.token_count()
@@ -417,10 +425,13 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
                              "choices": [], "usage": {
                                  "prompt_tokens": prompt_toks, "completion_tokens": completion,
                                  "total_tokens": prompt_toks + completion}})
+            finished = True
             yield b"data: [DONE]\n\n"
         finally:
             sem.release()
             stats.end()
+            if not finished:
+                runner.cancel(task.task_id)
 
     @app.post("/v1/chat/completions")
     async def chat_completions(request: Request):

@@ -36,19 +36,20 @@ SMALL_M_TOKENS = 64
 
 class BF16Linear:
     """Plain bf16 projection (the MoE config's attention is bf16); on CUDA
-    this is a cuBLAS GEMM through torch.matmul."""
+    it runs our tcgen05 bf16 GEMM with the residual add fused into its
+    epilogue."""
 
     def __init__(self, w: torch.Tensor, device):
-        self.w = w.to(torch.bfloat16).to(device)
+        self.w = w.to(torch.bfloat16).to(device).contiguous()
         self.n, self.k = self.w.shape
 
     def __call__(self, x, epilogue=ops.EPI_STORE, residual=None, out=None):
         if self.w.device.type == "cuda":
-            y = torch.matmul(x, self.w.t())
-        else:
-            y = (x.float() @ self.w.float().t()).to(torch.bfloat16)
+            return ops.bf16_gemm(x, self.w, residual if epilogue == ops.EPI_RESID else None, out)
+        y = (x.float() @ self.w.float().t())
         if epilogue == ops.EPI_RESID:
-            y = (y.float() + residual.float()).to(torch.bfloat16)
+            y = y + residual.float()
+        y = y.to(torch.bfloat16)
         if out is not None:
             out.copy_(y)
             return out

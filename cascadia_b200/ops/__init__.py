@@ -176,6 +176,27 @@ def w4a16_gemm(x: torch.Tensor, blob: torch.Tensor, n: int, group_size: int = 12
     return out
 
 
+def bf16_gemm(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None,
+              out: Optional[torch.Tensor] = None, workspace: Optional[GemmWorkspace] = None,
+              splits: int = 0) -> torch.Tensor:
+    """Y = X @ W^T (+ residual) on the tcgen05 bf16 GEMM (both operands
+    TMA-staged in shared memory, fp32 accumulator in tensor memory, split-K
+    with a deterministic last-CTA reduction for small tile counts)."""
+    m, k = x.shape
+    n = w.shape[0]
+    if x.stride(1) != 1 or (x.stride(0) * 2) % 16 or x.data_ptr() % 16:
+        x = x.contiguous()
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+    e = ext()
+    plan = e.bf16_gemm_plan(m, n, k, splits)
+    ws = workspace or default_workspace(x.device)
+    ws.ensure(plan[4], plan[5])
+    e.bf16_gemm(x, w, out, residual, ws.ws, ws.counters, status_buffer(x.device), splits)
+    LAUNCHES.add(1)
+    return out
+
+
 def w4a16_plan(m: int, n: int, k: int, splits: int = 0):
     return ext().w4a16_plan(m, n, k, splits)
 

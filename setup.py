@@ -22,6 +22,7 @@ SOURCES = [
     "bindings.cpp",
     "gemm_w4a16.cu",
     "gemm_stream.cu",
+    "gemm_bf16.cu",
     "attention.cu",
     "elementwise.cu",
     "comm.cu",
