@@ -34,18 +34,34 @@ from .llama import Batch, LlamaModel, QLinear, TPGroup, _layer_generator, random
 SMALL_M_TOKENS = 64
 
 
+# Token counts up to this run the bf16 projections on our tcgen05 GEMM;
+# prefill-sized batches go to cuBLAS, which measured 2.5x faster there
+# (1.28-1.37 PFLOP/s against 0.48-0.83 for our one-SM tiles at M = 2048:
+# a 128 x 256 tile per SM is bound by shared-memory bandwidth; the 2-SM
+# cta_group::2 tile is what closes the gap).
+BF16_TCGEN05_MAX_M = 256
+
+
 class BF16Linear:
-    """Plain bf16 projection (the MoE config's attention is bf16); on CUDA
-    it runs our tcgen05 bf16 GEMM with the residual add fused into its
-    epilogue."""
+    """Plain bf16 projection (the MoE config's attention is bf16).  On CUDA,
+    decode-sized token counts run our tcgen05 bf16 GEMM (residual add fused
+    into its epilogue); prefill-sized ones run cuBLAS."""
 
     def __init__(self, w: torch.Tensor, device):
         self.w = w.to(torch.bfloat16).to(device).contiguous()
         self.n, self.k = self.w.shape
 
     def __call__(self, x, epilogue=ops.EPI_STORE, residual=None, out=None):
-        if self.w.device.type == "cuda":
+        if self.w.device.type == "cuda" and x.shape[0] <= BF16_TCGEN05_MAX_M:
             return ops.bf16_gemm(x, self.w, residual if epilogue == ops.EPI_RESID else None, out)
+        if self.w.device.type == "cuda":
+            y = torch.matmul(x, self.w.t())
+            if epilogue == ops.EPI_RESID:
+                y = (y.float() + residual.float()).to(torch.bfloat16)
+            if out is not None:
+                out.copy_(y)
+                return out
+            return y
         y = (x.float() @ self.w.float().t())
         if epilogue == ops.EPI_RESID:
             y = y + residual.float()

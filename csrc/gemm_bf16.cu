@@ -39,12 +39,16 @@ namespace {
 
 constexpr int kBfThreads = 128;
 
-template <int TN>
+// KS = 64-wide K slices per stage.  With KS > 1 each row of a weight tile
+// arrives as KS x 128 contiguous bytes (a 3-D tensor map over the slices),
+// which streams from HBM better than one 128-byte piece per row.
+template <int TN, int KS>
 struct BfPlan {
-  static constexpr int kWBytes = 128 * 128;  // 128 rows x 64 bf16
-  static constexpr int kXBytes = TN * 128;   // TN rows x 64 bf16
+  static constexpr int kWBytes = 128 * 128 * KS;  // 128 rows x 64*KS bf16
+  static constexpr int kXBytes = TN * 128 * KS;   // TN rows x 64*KS bf16
   static constexpr int kStage = kWBytes + kXBytes;
-  static constexpr int kStages = TN >= 256 ? 4 : (TN >= 128 ? 6 : 8);
+  static constexpr int kStagesRaw = (200 * 1024) / kStage;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
   static constexpr int kBarOff = kStages * kStage;
   static constexpr int kSmem = kBarOff + 256 + 1024;  // barriers + alignment slack
   static constexpr uint32_t kTmemCols = TN < 32 ? 32 : TN;
@@ -63,11 +67,11 @@ struct BfArgs {
   int pdl;
 };
 
-template <int TN>
+template <int TN, int KS, bool T3>
 __global__ void __launch_bounds__(kBfThreads, 1)
     bf16_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_x, const BfArgs a) {
-  using P = BfPlan<TN>;
+  using P = BfPlan<TN, KS>;
   constexpr int S = P::kStages;
   constexpr uint32_t kIdesc = umma_idesc_bf16(128, TN);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -84,7 +88,7 @@ __global__ void __launch_bounds__(kBfThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rt = blockIdx.x, split = blockIdx.y, tt = blockIdx.z;
   const int n0 = rt * 128, m0 = tt * TN;
-  const int KB = (a.K + 63) / 64;
+  const int KB = (a.K + 64 * KS - 1) / (64 * KS);  // k-blocks of 64*KS
   const int kb0 = split * a.kb_per_split;
   const int nkb = max(0, min(KB, kb0 + a.kb_per_split) - kb0);
 
@@ -114,14 +118,19 @@ __global__ void __launch_bounds__(kBfThreads, 1)
     prefetch_tmap(&tm_w);
     prefetch_tmap(&tm_x);
     const int pre = a.pdl ? min(nkb, S) : 0;
+    // T3: 3-D maps {64, rows, K/64}; slice coordinate = k-block * KS.
+    auto load = [&](const CUtensorMap* m, uint8_t* dst, int row, int kb, uint64_t* bar) {
+      if constexpr (T3) tma_load_3d(dst, m, 0, row, kb * KS, bar);
+      else tma_load_2d(dst, m, kb * 64, row, bar);
+    };
     for (int i = 0; i < pre; ++i) {
       uint8_t* st = smem + i * P::kStage;
       mbar_arrive_expect_tx(&full[i], P::kStage);
-      tma_load_2d(st, &tm_w, (kb0 + i) * 64, n0, &full[i]);
+      load(&tm_w, st, n0, kb0 + i, &full[i]);
     }
     grid_dep_wait();
     for (int i = 0; i < pre; ++i)
-      tma_load_2d(smem + i * P::kStage + P::kWBytes, &tm_x, (kb0 + i) * 64, m0, &full[i]);
+      load(&tm_x, smem + i * P::kStage + P::kWBytes, m0, kb0 + i, &full[i]);
     int issued = pre;
     for (int i = pre; i < nkb; ++i) {
       const int s = i % S;
@@ -129,8 +138,8 @@ __global__ void __launch_bounds__(kBfThreads, 1)
         break;
       uint8_t* st = smem + s * P::kStage;
       mbar_arrive_expect_tx(&full[s], P::kStage);
-      tma_load_2d(st, &tm_w, (kb0 + i) * 64, n0, &full[s]);
-      tma_load_2d(st + P::kWBytes, &tm_x, (kb0 + i) * 64, m0, &full[s]);
+      load(&tm_w, st, n0, kb0 + i, &full[s]);
+      load(&tm_x, st + P::kWBytes, m0, kb0 + i, &full[s]);
       ++issued;
     }
     // Never leave while a copy still writes into shared memory.
@@ -146,10 +155,13 @@ __global__ void __launch_bounds__(kBfThreads, 1)
       const uint32_t w_addr = smem_u32(smem + s * P::kStage);
       const uint32_t x_addr = w_addr + P::kWBytes;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        mma_bf16_ss(tmem, umma_desc_sw128(w_addr + kk * 32), umma_desc_sw128(x_addr + kk * 32),
-                    kIdesc, (i | kk) != 0 ? 1u : 0u);
-      }
+      for (int sl = 0; sl < KS; ++sl)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          mma_bf16_ss(tmem, umma_desc_sw128(w_addr + sl * (128 * 128) + kk * 32),
+                      umma_desc_sw128(x_addr + sl * (TN * 128) + kk * 32), kIdesc,
+                      (i | sl | kk) != 0 ? 1u : 0u);
+        }
       mma_commit(&empty[s]);
       ++done;
     }
@@ -277,39 +289,43 @@ __global__ void __launch_bounds__(kBfThreads, 1)
 }
 
 struct BfPlanHost {
-  int TN, tiles_n, tiles_m, splits, kbps;
+  int TN, KS, t3, tiles_n, tiles_m, splits, kbps;
 };
 
 BfPlanHost bf16_plan(int M, int N, int K, int forced) {
   BfPlanHost p;
   p.TN = M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  p.t3 = (K % 64) == 0;
+  p.KS = (p.t3 && p.TN <= 64) ? 2 : 1;
   p.tiles_n = (N + 127) / 128;
   p.tiles_m = (M + p.TN - 1) / p.TN;
-  const int KB = (K + 63) / 64;
+  const int KB64 = (K + 63) / 64;
   const int tiles = p.tiles_n * p.tiles_m;
   int s = 1;
   if (forced > 0) {
     s = forced;
-  } else if (tiles < num_sms() / 2 && KB >= 16) {
-    s = std::min(8, std::min(num_sms() / tiles, KB / 8));
+  } else if (tiles < num_sms() / 2 && KB64 >= 16) {
+    s = std::min(8, std::min(num_sms() / tiles, KB64 / 8));
   }
+  const int KB = (KB64 + p.KS - 1) / p.KS;  // k-blocks of 64 * KS
   s = std::max(1, std::min(s, KB));
   p.kbps = (KB + s - 1) / s;
   p.splits = (KB + p.kbps - 1) / p.kbps;  // no empty split
   return p;
 }
 
-template <int TN>
+template <int TN, int KS, bool T3>
 void launch_bf16(const CUtensorMap& tw, const CUtensorMap& tx, const BfArgs& a, dim3 grid,
                  cudaStream_t stream) {
-  using P = BfPlan<TN>;
+  using P = BfPlan<TN, KS>;
   static bool attr = false;
   if (!attr) {
-    CB_CUDA_CHECK(cudaFuncSetAttribute(bf16_gemm_kernel<TN>,
+    CB_CUDA_CHECK(cudaFuncSetAttribute(bf16_gemm_kernel<TN, KS, T3>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, P::kSmem));
     attr = true;
   }
-  launch_kernel(bf16_gemm_kernel<TN>, grid, dim3(kBfThreads), P::kSmem, stream, tw, tx, a);
+  launch_kernel(bf16_gemm_kernel<TN, KS, T3>, grid, dim3(kBfThreads), P::kSmem, stream, tw, tx,
+                a);
 }
 
 }  // namespace
@@ -366,19 +382,33 @@ void bf16_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out,
   a.counters = counters.data_ptr<int>();
   a.status = status.data_ptr<int>();
   a.pdl = pdl_flag();
-  const CUtensorMap tw = make_tmap_2d_bf16(w.data_ptr(), (uint64_t)K, (uint64_t)N,
-                                           (uint64_t)w.stride(0) * 2, 64, 128,
-                                           CU_TENSOR_MAP_SWIZZLE_128B);
-  const CUtensorMap tx = make_tmap_2d_bf16(x.data_ptr(), (uint64_t)K, (uint64_t)M,
-                                           (uint64_t)x.stride(0) * 2, 64, (uint32_t)p.TN,
-                                           CU_TENSOR_MAP_SWIZZLE_128B);
   const dim3 grid(p.tiles_n, p.splits, p.tiles_m);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  switch (p.TN) {
-    case 32: launch_bf16<32>(tw, tx, a, grid, stream); break;
-    case 64: launch_bf16<64>(tw, tx, a, grid, stream); break;
-    case 128: launch_bf16<128>(tw, tx, a, grid, stream); break;
-    default: launch_bf16<256>(tw, tx, a, grid, stream); break;
+  if (p.t3) {
+    // K-slice maps: dims {64, rows, K / 64}; one load = KS slices of a tile.
+    const CUtensorMap tw = make_tmap_kchunks_bf16(w.data_ptr(), (uint64_t)K, (uint64_t)N,
+                                                  (uint64_t)w.stride(0) * 2, 128, p.KS);
+    const CUtensorMap tx = make_tmap_kchunks_bf16(x.data_ptr(), (uint64_t)K, (uint64_t)M,
+                                                  (uint64_t)x.stride(0) * 2, p.TN, p.KS);
+    switch (p.TN) {
+      case 32: launch_bf16<32, 2, true>(tw, tx, a, grid, stream); break;
+      case 64: launch_bf16<64, 2, true>(tw, tx, a, grid, stream); break;
+      case 128: launch_bf16<128, 1, true>(tw, tx, a, grid, stream); break;
+      default: launch_bf16<256, 1, true>(tw, tx, a, grid, stream); break;
+    }
+  } else {
+    const CUtensorMap tw = make_tmap_2d_bf16(w.data_ptr(), (uint64_t)K, (uint64_t)N,
+                                             (uint64_t)w.stride(0) * 2, 64, 128,
+                                             CU_TENSOR_MAP_SWIZZLE_128B);
+    const CUtensorMap tx = make_tmap_2d_bf16(x.data_ptr(), (uint64_t)K, (uint64_t)M,
+                                             (uint64_t)x.stride(0) * 2, 64, (uint32_t)p.TN,
+                                             CU_TENSOR_MAP_SWIZZLE_128B);
+    switch (p.TN) {
+      case 32: launch_bf16<32, 1, false>(tw, tx, a, grid, stream); break;
+      case 64: launch_bf16<64, 1, false>(tw, tx, a, grid, stream); break;
+      case 128: launch_bf16<128, 1, false>(tw, tx, a, grid, stream); break;
+      default: launch_bf16<256, 1, false>(tw, tx, a, grid, stream); break;
+    }
   }
 }
 
