@@ -197,6 +197,16 @@ def bf16_gemm(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor]
     return out
 
 
+def hc_pre(copies: torch.Tensor, fn: torch.Tensor, base: torch.Tensor, scale: torch.Tensor,
+           iters: int, hc_eps: float, norm_eps: float):
+    """DeepSeek-V4 Hyper-Connections pre-mix in one kernel: copies
+    [T, hc, dim] fp32 -> (y [T, dim] bf16-valued, post [T, hc],
+    comb [T, hc, hc], pre [T, hc])."""
+    out = ext().hc_pre(copies.contiguous(), fn, base, scale, iters, hc_eps, norm_eps)
+    LAUNCHES.add(1)
+    return out
+
+
 def w4a16_plan(m: int, n: int, k: int, splits: int = 0):
     return ext().w4a16_plan(m, n, k, splits)
 

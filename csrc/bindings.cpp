@@ -33,6 +33,9 @@ void bf16_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor out,
                c10::optional<torch::Tensor> residual, torch::Tensor ws, torch::Tensor counters,
                torch::Tensor status, int64_t splits);
 std::vector<int64_t> bf16_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t splits);
+std::vector<torch::Tensor> hc_pre(torch::Tensor copies, torch::Tensor fn, torch::Tensor base,
+                                  torch::Tensor scale, int64_t iters, double hc_eps,
+                                  double norm_eps);
 void w4a16_gemm_push(torch::Tensor x, torch::Tensor wblob, int64_t N, int64_t group_size,
                      torch::Tensor out_ptrs, int64_t ldo, torch::Tensor sig_ptrs, int64_t my_rank,
                      torch::Tensor push_done, torch::Tensor push_epoch, torch::Tensor ws,
@@ -143,6 +146,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("w4a16_gemm_push", &cb::w4a16_gemm_push);
   m.def("bf16_gemm", &cb::bf16_gemm);
   m.def("bf16_gemm_plan", &cb::bf16_gemm_plan);
+  m.def("hc_pre", &cb::hc_pre);
   m.def("w4a16_plan", &cb::w4a16_plan);
   m.def("w4a16_set_trace", &cb::w4a16_set_trace);
   m.def("set_pdl", &cb::set_pdl);

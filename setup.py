@@ -23,6 +23,7 @@ SOURCES = [
     "gemm_w4a16.cu",
     "gemm_stream.cu",
     "gemm_bf16.cu",
+    "hc.cu",
     "attention.cu",
     "elementwise.cu",
     "comm.cu",
