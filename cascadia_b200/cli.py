@@ -22,6 +22,7 @@ ENGINES = {
     "llama": "dense Llama-family INT4 engine (continuous batching, paged KV, TP, PP)",
     "moe": "sparse-MoE INT4 engine (Qwen3-MoE / Kimi-K2 shapes, expert parallel)",
     "spec": "distributed speculative decoding (draft stage + target stages)",
+    "dsv4": "DeepSeek-V4 export directory (--model DIR): hyper-connections, compressed KV",
 }
 
 
@@ -84,6 +85,10 @@ def _builder(args, tp=None):
 
     if args.engine == "mock":
         return MockBuilder()
+    if args.engine == "dsv4":
+        from .engine.dsv4 import DSV4Builder
+
+        return DSV4Builder(args.model, device=args.device, max_seq=args.max_model_len)
     if args.engine == "moe":
         from .engine.llm import MoEBuilder
 
@@ -190,6 +195,11 @@ def _serve_or_prompt(runner, args, name: str):
 
 
 def _num_layers(model: str) -> int:
+    if os.path.isfile(os.path.join(model, "manifest.json")):
+        import json
+
+        with open(os.path.join(model, "manifest.json")) as f:
+            return int(json.load(f).get("num_layers", 1))  # export directory (V4 / MoE)
     if os.path.isdir(model):
         from .shard.format import read_pipeline
 

@@ -78,3 +78,52 @@ def test_sinkhorn_is_doubly_stochastic():
     assert torch.allclose(comb.sum(-2), torch.ones(5, hc), atol=1e-4)
     assert torch.allclose(comb.sum(-1), torch.ones(5, hc), atol=1e-3)
     assert (post > 0).all() and (post < 2).all() and (pre > 0).all()
+
+
+def test_engine_serves_through_api():
+    """The V4 engine behind the runner and the OpenAI API: greedy tokens of
+    the recorded prompt, and a second request served after the first."""
+    from fastapi.testclient import TestClient
+
+    from cascadia_b200.api.server import ApiConfig, make_app
+    from cascadia_b200.engine.dsv4 import DSV4Builder
+    from cascadia_b200.runtime.runner import Runner
+    from cascadia_b200.types import PeerLayout, ShardSpec
+
+    ref = _ref()
+    r = Runner(DSV4Builder(FIX, "cpu", max_seq=64), model_id="dsv4-tiny", device="cpu")
+    r.start(PeerLayout(), ShardSpec("dsv4-tiny", 0, 4, 4))
+    with TestClient(make_app(r, ApiConfig(model_name="dsv4-tiny"))) as c:
+        for _ in range(2):
+            j = c.post("/v1/completions", json={
+                "prompt": "x", "prompt_token_ids": ref["prompt_ids"],
+                "max_tokens": len(ref["generated"]), "logprobs": 0}).json()
+            assert j["usage"]["completion_tokens"] == len(ref["generated"])
+            assert j["usage"]["prompt_tokens"] == len(ref["prompt_ids"])
+        too_long = c.post("/v1/completions", json={"prompt": "x",
+                                                   "prompt_token_ids": list(range(70))})
+        assert too_long.status_code == 500
+    r.close()
+
+
+def test_engine_greedy_tokens():
+    from cascadia_b200.engine.dsv4 import DSV4Engine
+    from cascadia_b200.types import GenerationTask
+
+    ref = _ref()
+    e = DSV4Engine(DSV4Model(FIX, "cpu", max_seq=64))
+    e.submit(GenerationTask("a", "x", max_tokens=len(ref["generated"]),
+                            prompt_ids=ref["prompt_ids"]))
+    e.submit(GenerationTask("b", "x", max_tokens=3, prompt_ids=ref["prompt_ids"]))
+    toks = {"a": [], "b": []}
+    fins = {}
+    for _ in range(50):
+        for tid, ch in e.step():
+            if ch.is_final:
+                fins[tid] = ch.finish_reason
+            elif ch.error is None:
+                toks[tid].append(ch.token_id)
+        if not e.has_work():
+            break
+    assert toks["a"] == ref["generated"] and toks["b"] == ref["generated"][:3]
+    assert fins["b"].name == "LENGTH"
