@@ -326,10 +326,23 @@ def cmd_topology(args):
 
 
 def cmd_place(args):
-    from .utils.placement import choose_parallelism
+    from .utils import placement as pl
 
-    print(json.dumps(choose_parallelism(args.model, args.gpus, args.batch, args.context,
-                                        gpu_mem_gb=args.gpu_mem_gb), indent=1))
+    layer_us = None
+    if args.calibrate:
+        layer_us = pl.calibrate_layer_us(args.model, args.batch, args.context)
+    res = pl.choose_parallelism(args.model, args.gpus, args.batch, args.context,
+                                gpu_mem_gb=args.gpu_mem_gb,
+                                hbm_gbs=pl.measured_hbm_gbs(args.peaks), layer_us=layer_us)
+    best = res["best"]
+    if best is not None and best["ep"] == 1:
+        res["launch"] = " ".join(pl.launch_command(args.model, best, args.api))
+    print(json.dumps(res, indent=1), flush=True)
+    if args.launch:
+        if best is None:
+            sys.exit("no split fits in memory")
+        sys.exit(pl.supervise(pl.launch_command(args.model, best, args.api),
+                              max_restarts=args.max_restarts))
 
 
 def main(argv=None):
@@ -386,6 +399,13 @@ def main(argv=None):
     pl.add_argument("--batch", type=int, default=64)
     pl.add_argument("--context", type=int, default=4096)
     pl.add_argument("--gpu-mem-gb", type=float, default=180.0)
+    pl.add_argument("--peaks", default=None, help="measured peaks JSON (hbm_gbs)")
+    pl.add_argument("--calibrate", action="store_true",
+                    help="time two layers of the model on this GPU and use the measured cost")
+    pl.add_argument("--launch", action="store_true",
+                    help="serve the chosen split under a restart-on-crash supervisor")
+    pl.add_argument("--api", default="0.0.0.0:8000")
+    pl.add_argument("--max-restarts", type=int, default=3)
     pl.set_defaults(fn=cmd_place)
 
     args = p.parse_args(argv)
