@@ -3,7 +3,12 @@
 The reference runs Gemma-4 as a multi-stage OpenVINO chain with cross-KV
 frames for the shared-KV layers (crates/cascadia-engine-openvino/src/
 gemma4.rs:1-27, engine :1012, builder :1208; docs/architectures/
-gemma4-support.md).  Here one model object runs it on our kernels:
+gemma4-support.md).  Here a model object runs one stage (or all layers) on
+our kernels; across pipeline stages each stage hands the next its hidden
+rows widened by the per-layer inputs of the later layers and by the K/V rows
+of every shared-cache source layer that a later stage reads, which the
+receiving stage keeps in mirror pools (``pack_payload`` /
+``unpack_payload``):
 
 * layer types: sliding-window attention (head_dim 256, window masked inside
   the attention kernels) and full attention (head_dim 512: the decode
@@ -123,30 +128,38 @@ class Gemma4Model(LlamaModel):
                  layer_end: Optional[int] = None, has_embed: bool = True, has_head: bool = True,
                  **_):
         super().__init__(cfg, device, tp, layer_start, layer_end, has_embed, has_head)
-        assert self.tp.size == 1 and layer_start == 0 and (layer_end in (None, cfg.num_layers)), \
-            "Gemma-4: one stage, TP=1 (the per-layer inputs need the token ids)"
+        assert self.tp.size == 1, "Gemma-4: TP=1"
         self.types = list(cfg.layer_types)
         L = cfg.num_layers
         first_shared = L - cfg.num_kv_shared_layers
         self.first_shared = first_shared
         self.spec: List[dict] = []
-        n1 = n2 = 0
-        own: Dict[str, int] = {}
+        self.src_of: Dict[int, int] = {}  # shared layer -> the layer whose cache it reads
         for li in range(L):
             full = self.types[li] == FULL
             shared = cfg.num_kv_shared_layers > 0 and li >= first_shared
             if shared:
-                src = max(j for j in range(first_shared) if self.types[j] == self.types[li])
-                idx = own[f"{src}"]
-            else:
-                idx = n2 if full else n1
-                if full:
-                    n2 += 1
-                else:
-                    n1 += 1
-                own[f"{li}"] = idx
-            self.spec.append(dict(full=full, shared=shared, cache_idx=idx))
-        self.n1, self.n2 = n1, n2
+                self.src_of[li] = max(j for j in range(first_shared)
+                                      if self.types[j] == self.types[li])
+            self.spec.append(dict(full=full, shared=shared))
+        # Pipeline stages: this stage's pools are its own cache layers plus
+        # mirrors of source layers that live on earlier stages (their K/V
+        # rows arrive with the hidden rows, see pack_payload).  A stage also
+        # forwards the rows of sources that later stages need.
+        S, E = self.layer_start, self.layer_end
+        owners = [li for li in range(S, E) if not self.spec[li]["shared"]]
+        self.mirror_in = sorted({src for li, src in self.src_of.items() if li >= S and src < S})
+        self.mirror_out = sorted({src for li, src in self.src_of.items() if li >= E and src < E})
+        self.pool: Dict[int, int] = {}
+        cnt = {False: 0, True: 0}
+        for li in sorted(owners + self.mirror_in):
+            full = self.spec[li]["full"]
+            self.pool[li] = cnt[full]
+            cnt[full] += 1
+        for li in range(S, E):
+            self.spec[li]["cache_idx"] = self.pool[self.src_of.get(li, li)]
+        self.n1, self.n2 = cnt[False], cnt[True]
+        self._ple_start = 0
         self.P = cfg.hidden_size_per_layer_input
         self.embed_scale = math.sqrt(cfg.hidden_size)
         self._ple = None
@@ -173,7 +186,7 @@ class Gemma4Model(LlamaModel):
                                                                   device=dev) * std
             sd["per_layer_projection_norm.weight"] = torch.ones(P, device=dev)
         sd["norm.weight"] = torch.ones(H, device=dev)
-        for li in range(L):
+        for li in range(self.layer_start, self.layer_end):
             g = _layer_generator(seed, li, dev)
             p = f"layers.{li}."
             sp = self.spec[li]
@@ -248,6 +261,86 @@ class Gemma4Model(LlamaModel):
                 self.ple_proj_norm.float()
             self._ple = ((proj.to(torch.bfloat16).float() + ple.to(torch.bfloat16).float()) *
                          (2 ** -0.5)).to(torch.bfloat16)
+            self._ple_start = 0
+        return out
+
+    # ------------------------------------------------ pipeline stage payload
+    def _kv_shape(self, li: int):
+        cfg = self.cfg
+        if self.spec[li]["full"]:
+            hkv = cfg.num_global_kv_heads if cfg.attention_k_eq_v else cfg.num_kv_heads
+            return hkv, cfg.global_head_dim
+        return cfg.num_kv_heads, cfg.head_dim
+
+    def _mirror_width(self, layers) -> int:
+        return sum(2 * h * d for h, d in (self._kv_shape(li) for li in layers))
+
+    @property
+    def payload_in_width(self) -> int:
+        L, P = self.cfg.num_layers, self.P
+        return self.cfg.hidden_size + (L - self.layer_start) * P + self._mirror_width(
+            self.mirror_in)
+
+    @property
+    def payload_out_width(self) -> int:
+        L, P = self.cfg.num_layers, self.P
+        return self.cfg.hidden_size + (L - self.layer_end) * P + self._mirror_width(
+            self.mirror_out)
+
+    def _pool_of(self, li: int):
+        kv = self.kv
+        kc, vc = (kv.k2, kv.v2) if self.spec[li]["full"] else (kv.k, kv.v)
+        return kc, vc, self.pool[li]
+
+    @staticmethod
+    def _slot_index(slots: torch.Tensor):
+        sl = slots.long()
+        return sl // BLOCK_SIZE, sl % BLOCK_SIZE
+
+    def pack_payload(self, hidden: torch.Tensor, batch: Batch) -> torch.Tensor:
+        """hidden | per-layer inputs of the later layers | K and V rows (as
+        cached: normed, roped) of every source layer that a later stage's
+        shared layers read."""
+        T = hidden.shape[0]
+        L, E = self.cfg.num_layers, self.layer_end
+        parts = [hidden]
+        if self.P and E < L:
+            parts.append(self._ple[:, E - self._ple_start:].reshape(T, -1).to(torch.bfloat16))
+        if self.mirror_out:
+            blk, off = self._slot_index(batch.slots)
+            for src in self.mirror_out:
+                kc, vc, p = self._pool_of(src)
+                parts.append(kc[p, blk, :, off, :].reshape(T, -1))
+                parts.append(vc[p, blk, :, off, :].reshape(T, -1))
+        return torch.cat(parts, 1) if len(parts) > 1 else hidden
+
+    def unpack_payload(self, buf: torch.Tensor, batch: Batch,
+                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Inverse of the previous stage's pack_payload: returns the hidden
+        rows, keeps the per-layer inputs (a view of `buf`) and writes the
+        mirrored K/V rows into this stage's pools at the batch's slots."""
+        cfg = self.cfg
+        H, L, S, P = cfg.hidden_size, cfg.num_layers, self.layer_start, self.P
+        T = buf.shape[0]
+        if out is None:
+            out = buf[:, :H].clone()
+        else:
+            out.copy_(buf[:, :H])
+        off = H
+        if P:
+            n = (L - S) * P
+            self._ple = buf[:, off:off + n].reshape(T, L - S, P)
+            self._ple_start = S
+            off += n
+        if self.mirror_in:
+            blk, so = self._slot_index(batch.slots)
+            for src in self.mirror_in:
+                h, d = self._kv_shape(src)
+                kc, vc, p = self._pool_of(src)
+                kc[p, blk, :, so, :] = buf[:, off:off + h * d].reshape(T, h, d).to(kc.dtype)
+                off += h * d
+                vc[p, blk, :, so, :] = buf[:, off:off + h * d].reshape(T, h, d).to(vc.dtype)
+                off += h * d
         return out
 
     def _rms(self, x, w, eps=None):
@@ -288,7 +381,8 @@ class Gemma4Model(LlamaModel):
             hidden.copy_((hidden.float() + t2.float()).to(torch.bfloat16))
             if lw.ple_gate is not None:
                 gte = lw.ple_gate(hidden)
-                gte = (F.gelu(gte.float(), approximate="tanh") * self._ple[:, i].float()).to(
+                ple_i = self._ple[:, self.layer_start + i - self._ple_start]
+                gte = (F.gelu(gte.float(), approximate="tanh") * ple_i.float()).to(
                     torch.bfloat16)
                 pr = lw.ple_proj(gte)
                 self._norm_to(pr, lw.ple_norm, t2)
@@ -468,7 +562,7 @@ def load_hf_weights(model: Gemma4Model, sd: Dict[str, torch.Tensor],
         model.ple_proj_norm = bf(W("per_layer_projection_norm.weight"))
     model.layers = []
     model._ones_h = torch.ones(cfg.hidden_size, dtype=torch.bfloat16, device=dev)
-    for li in range(cfg.num_layers):
+    for li in range(model.layer_start, model.layer_end):
         p = f"layers.{li}."
         sp = model.spec[li]
         moe = None

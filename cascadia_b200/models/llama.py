@@ -275,6 +275,29 @@ class LlamaModel:
         d.lm_head = self.lm_head
         return d
 
+    # ------------------------------------------------ pipeline stage payload
+    # What one stage hands the next per token row.  For most families it is
+    # the hidden row itself; a family whose later layers need more (Gemma-4:
+    # per-layer inputs and the K/V rows of shared-cache source layers)
+    # widens it.
+    @property
+    def payload_in_width(self) -> int:
+        return self.cfg.hidden_size
+
+    @property
+    def payload_out_width(self) -> int:
+        return self.cfg.hidden_size
+
+    def pack_payload(self, hidden: torch.Tensor, batch: "Batch") -> torch.Tensor:
+        return hidden
+
+    def unpack_payload(self, buf: torch.Tensor, batch: "Batch",
+                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if out is None:
+            return buf
+        out.copy_(buf)
+        return out
+
     def allocate_kv(self, num_blocks: int) -> KVCache:
         self.kv = KVCache(self.num_local_layers, num_blocks, self.hkv, self.d, self.device)
         return self.kv

@@ -221,10 +221,13 @@ class PipelineWorker(Engine):
             if not self.is_last:
                 self.ch.send_down(meta, None)
             return []
-        hidden = hidden.to(self.model.device)
+        m = self.model
+        buf = hidden.to(m.device)
+        hidden = m.unpack_payload(buf, batch, out=torch.empty(
+            buf.shape[0], m.cfg.hidden_size, dtype=buf.dtype, device=m.device))
         self.model.forward(batch, hidden)
         if not self.is_last:
-            self.ch.send_down(meta, hidden)
+            self.ch.send_down(meta, m.pack_payload(hidden, batch))
             reply, logits = self.ch.recv_reply_down(bool(want))
             self.ch.send_reply_up(reply, logits)
         else:
@@ -254,7 +257,7 @@ class PipelineHead:
         seq = next(self._seq)
         self.model.forward(batch, hidden)
         meta = encode_meta(KIND_FORWARD, seq, batch, want)
-        self.ch.send_down(meta, hidden)
+        self.ch.send_down(meta, self.model.pack_payload(hidden, batch))
         reply, logits = self.ch.recv_reply_down(bool(want))
         r = reply.tolist()
         if r[0] != seq:

@@ -98,7 +98,7 @@ class PipelinedDecoder:
             g.run()
             if not self.last:
                 self._pending[mb].append(
-                    dist.isend(g.hidden, self._peer(self.stage + 1), group=self.group))
+                    dist.isend(g.payload_out, self._peer(self.stage + 1), group=self.group))
             else:
                 self._pending[mb].append(
                     dist.isend(g.next_ids.to(torch.int32), self._peer(0), group=self.group))
@@ -139,11 +139,14 @@ def pp_prefill(model, stage: int, n_stages: int, seq_ids: List[str], prompts: Li
         hidden = m.embed_tokens(torch.tensor([t for p in prompts for t in p], dtype=torch.int32,
                                              device=m.device))
     else:
-        hidden = torch.empty(T, m.cfg.hidden_size, dtype=torch.bfloat16, device=m.device)
-        dist.recv(hidden, ranks[stage - 1], group=group)
+        buf = torch.empty(T, m.payload_in_width, dtype=torch.bfloat16, device=m.device)
+        dist.recv(buf, ranks[stage - 1], group=group)
+        hidden = m.unpack_payload(buf, batch,
+                                  out=torch.empty(T, m.cfg.hidden_size, dtype=torch.bfloat16,
+                                                  device=m.device))
     m.forward(batch, hidden)
     if stage < n_stages - 1:
-        dist.send(hidden, ranks[stage + 1], group=group)
+        dist.send(m.pack_payload(hidden, batch).contiguous(), ranks[stage + 1], group=group)
     else:
         rows = torch.tensor(batch.last_rows, dtype=torch.long, device=m.device)
         toks = m.greedy(m.head(hidden.index_select(0, rows).contiguous())).to(torch.int32)

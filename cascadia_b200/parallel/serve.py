@@ -204,8 +204,9 @@ def build_pp_stage(args, ctx: DistContext):
     for p in builder.load(shard):
         log.info("rank %d load: %s", ctx.rank, p.message)
     model = builder.model
-    hidden = model.cfg.hidden_size
-    ch = NcclChannel(ctx.rank, ctx.world, ctx.device, hidden)
+    # Rows a stage receives: the hidden row, widened by the families that
+    # ship more per token (Gemma-4's per-layer inputs and shared K/V rows).
+    ch = NcclChannel(ctx.rank, ctx.world, ctx.device, model.payload_in_width)
     if not first:
         return None, PipelineWorker(model, ch, is_last=last), name
     engine = builder.build()

@@ -46,7 +46,9 @@ class DecodeGraph:
         # Pipeline stages after the first receive their input rows here; the
         # step copies them into `hidden` (the layers update it in place), so
         # replaying or re-running a step is idempotent.
-        self.hidden_in = None if model.has_embed else torch.zeros_like(self.hidden)
+        self.hidden_in = None if model.has_embed else torch.zeros(
+            batch, model.payload_in_width, dtype=torch.bfloat16, device=dev)
+        self.payload_out = None  # what a non-last stage sends on
         if num_splits is None:
             num_splits, bps = ops.decode_split_plan(batch, model.hkv, width)
         else:
@@ -75,8 +77,10 @@ class DecodeGraph:
         if m.has_embed:
             m.embed_tokens(self.ids, out=self.hidden)
         else:
-            self.hidden.copy_(self.hidden_in)
+            m.unpack_payload(self.hidden_in, self.batch_view, out=self.hidden)
         m.forward(self.batch_view, self.hidden)
+        if not m.has_head:
+            self.payload_out = m.pack_payload(self.hidden, self.batch_view)
         if m.has_head:
             self.logits = m.head(self.hidden)
             self.next_ids = m.greedy(self.logits)

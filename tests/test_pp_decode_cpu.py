@@ -68,7 +68,7 @@ def _worker(rank, world, port, prompts, steps, q, preset="tiny-llama"):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("preset", ["tiny-llama", "tiny-qwen36", "tiny-glm5"])
+@pytest.mark.parametrize("preset", ["tiny-llama", "tiny-qwen36", "tiny-glm5", "tiny-gemma4"])
 def test_pipelined_decode_matches_single_stage(preset):
     from cascadia_b200.runtime.generator import BatchGenerator
 

@@ -123,3 +123,14 @@ def test_tp2_served_on_two_gpus_matches_tp1():
     # bf16 partial sums are rounded differently at TP=2: require the opening
     # tokens (far from ties on this model) to agree.
     assert tp2["token_ids"][:4] == one["token_ids"][:4], (tp2, one)
+
+
+def test_gemma4_pp2_serving_equals_one_process_cpu():
+    """Gemma-4 split over two served stages: the second stage's shared-KV
+    layer reads a source layer of the first stage (its K/V rows travel with
+    the hidden rows, beside the per-layer inputs)."""
+    args = [a if a != "tiny-llama" else "tiny-gemma4" for a in CPU_ARGS]
+    one = _run(args)
+    pp2 = _run(args + ["--pp", "2"], nproc=2)
+    assert one["error"] is None and len(one["token_ids"]) == 8
+    assert pp2["token_ids"] == one["token_ids"]
