@@ -52,7 +52,7 @@ def parse():
     p.add_argument("--layers", type=int, default=0, help="debug only: override layer count")
     p.add_argument("--no-sweep", action="store_true",
                    help="skip the batch 1/8/32 measurements after the headline batch")
-    p.add_argument("--tp-comm", default="fused", choices=["fused", "push", "nccl"],
+    p.add_argument("--tp-comm", default="fused", choices=["fused", "push", "multimem", "nccl"],
                    help="row-parallel all-reduce: peer-memory fused kernel or NCCL")
     return p.parse_args()
 
@@ -153,11 +153,11 @@ def main():
     if args.layers:
         cfg.num_layers = args.layers
     tp = TPGroup(rank, world, group)
-    if world > 1 and args.tp_comm in ("fused", "push"):
+    if world > 1 and args.tp_comm in ("fused", "push", "multimem"):
         from cascadia_b200.parallel.tp import FusedTP
 
         tp.fused = FusedTP(group, rank, world, dev, cfg.hidden_size, max(64, args.batch),
-                           push=args.tp_comm == "push")
+                           push=args.tp_comm == "push", multimem=args.tp_comm == "multimem")
     t0 = time.time()
     ep = None
     if cfg.is_moe:

@@ -64,7 +64,7 @@ def main():
     p.add_argument("--layers", type=int, default=0)
     p.add_argument("--steps", type=int, default=4)
     p.add_argument("--model", default="llama-3.1-8b")
-    p.add_argument("--tp-comm", default="fused", choices=["fused", "push", "nccl"])
+    p.add_argument("--tp-comm", default="fused", choices=["fused", "push", "multimem", "nccl"])
     a = p.parse_args()
 
     from cascadia_b200 import ops
@@ -87,11 +87,11 @@ def main():
     if a.layers:
         cfg.num_layers = a.layers
     tp = TPGroup(rank, world, group)
-    if world > 1 and a.tp_comm in ("fused", "push"):
+    if world > 1 and a.tp_comm in ("fused", "push", "multimem"):
         from cascadia_b200.parallel.tp import FusedTP
 
         tp.fused = FusedTP(group, rank, world, dev, cfg.hidden_size, max(64, a.batch),
-                           push=a.tp_comm == "push")
+                           push=a.tp_comm == "push", multimem=a.tp_comm == "multimem")
     model = LlamaModel(cfg, dev, tp=tp).init_random(seed=1234)
     width = -(-(a.prompt_len + a.steps + 8) // BLOCK_SIZE)
     model.allocate_kv(a.batch * width + 16)

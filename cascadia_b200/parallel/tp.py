@@ -8,6 +8,10 @@ Two paths, same semantics (sum of row-parallel partials over the TP group):
   same allocation mapped on every GPU of the group); one kernel then signals,
   waits (bounded) for the peers, sums the partials with P2P loads, adds the
   residual and applies the next RMSNorm.  Used for decode-sized token counts.
+* ``FusedTP(multimem=True)``: as the default path, but the partials are
+  summed by ``multimem.ld_reduce`` on the buffer's NVLink multicast address
+  (NVLS: the NVSwitch adds the ranks' rows and returns one sum), so each
+  rank reads M x H once instead of once per peer.
 * ``FusedTP(push=True)``: the row-parallel GEMM itself stores each finished
   output tile into every rank's receive slot for this rank (plain P2P stores
   from the GEMM epilogue, so the transfer overlaps the rest of the GEMM) and
@@ -30,7 +34,7 @@ from .. import ops
 
 class FusedTP:
     def __init__(self, group, rank: int, world: int, device, hidden: int, max_tokens: int = 256,
-                 push: bool = False):
+                 push: bool = False, multimem: bool = False):
         import torch.distributed._symmetric_memory as symm_mem
 
         self.rank, self.world = rank, world
@@ -46,6 +50,12 @@ class FusedTP:
         shdl = symm_mem.rendezvous(self.sig, gname)
         self.buf_ptrs = torch.tensor([int(p) for p in hdl.buffer_ptrs], dtype=torch.int64)
         self.sig_ptrs = torch.tensor([int(p) for p in shdl.buffer_ptrs], dtype=torch.int64)
+        self.mc_ptr = 0
+        if multimem:
+            if not (hdl.has_multicast_support and int(hdl.multicast_ptr)):
+                raise RuntimeError("multimem all-reduce asked for, but this group's symmetric "
+                                   "memory has no NVLink multicast object (NVLS)")
+            self.mc_ptr = int(hdl.multicast_ptr)
         self.epoch = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.done = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self._handles = (hdl, shdl)
@@ -105,6 +115,6 @@ class FusedTP:
         ops.ext().ar_rmsnorm(self.buf_ptrs, slot * self.max_tokens * self.hidden * 2,
                              self.sig_ptrs, self.epoch, self.done,
                              ops.status_buffer(self.dev), self.rank, self.world, m, self.hidden,
-                             residual, weight, out, eps)
+                             residual, weight, out, eps, self.mc_ptr)
         ops.LAUNCHES.add(1)
         return out

@@ -135,7 +135,7 @@ void ar_rmsnorm_pushed(torch::Tensor slot_ptrs, torch::Tensor sig_ptrs, torch::T
 void ar_rmsnorm(torch::Tensor buf_ptrs, int64_t buf_offset_bytes, torch::Tensor sig_ptrs,
                 torch::Tensor epoch, torch::Tensor done, torch::Tensor status, int64_t rank,
                 int64_t world, int64_t M, int64_t H, c10::optional<torch::Tensor> residual,
-                c10::optional<torch::Tensor> w, torch::Tensor out, double eps);
+                c10::optional<torch::Tensor> w, torch::Tensor out, double eps, int64_t mc_ptr);
 }  // namespace cb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {

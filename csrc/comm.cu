@@ -50,6 +50,17 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
 // Peer data written by the peers' previous kernels: fetch from memory,
 // never from L1.  The caller issues all of a row's loads before using any
 // of them, so their NVLink round trips overlap.
+// Sum of the 8 bf16 at `mc` over every GPU bound to the NVLink multicast
+// object (the reduction runs in the NVSwitch; one 16-byte reply per load).
+__device__ __forceinline__ uint4 multimem_ld_sum_bf16x8(const void* mc) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ uint4 ld_cv128(const void* p) {
   uint4 v;
   asm volatile("ld.global.cv.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -77,6 +88,10 @@ struct ArArgs {
   // 0: the producing GEMM already pushed every rank's partial into this
   // rank's slots (bufs[] are local) and raised the flags.
   int signal;
+  // Multicast address of this all-reduce's buffer (NVLS), or null: with it,
+  // the partials are summed by multimem.ld_reduce (one reply per 16 bytes
+  // instead of one P2P load per peer).
+  const bf16* mc;
 };
 
 __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_kernel(const ArArgs a) {
@@ -130,9 +145,14 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_kernel(const ArArgs a) 
         for (int q = 0; q < 8; ++q) acc[k][q] = 0.f;
         if (i < nvec) {
           uint4 part[kMaxRanks];
+          const int np = a.mc != nullptr ? 1 : a.world;
+          if (a.mc != nullptr) {
+            part[0] = multimem_ld_sum_bf16x8(a.mc + (size_t)row * a.H + i * 8);
+          } else {
 #pragma unroll
-          for (int p = 0; p < kMaxRanks; ++p)
-            if (p < a.world) part[p] = ld_cv128(a.bufs[p] + (size_t)row * a.H + i * 8);
+            for (int p = 0; p < kMaxRanks; ++p)
+              if (p < a.world) part[p] = ld_cv128(a.bufs[p] + (size_t)row * a.H + i * 8);
+          }
           uint4 ru = make_uint4(0, 0, 0, 0);
           bf16* rp = nullptr;
           if (a.residual != nullptr) {
@@ -141,7 +161,7 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_kernel(const ArArgs a) 
           }
 #pragma unroll
           for (int p = 0; p < kMaxRanks; ++p) {
-            if (p < a.world) {
+            if (p < np) {
               const bf16* v = reinterpret_cast<const bf16*>(&part[p]);
 #pragma unroll
               for (int q = 0; q < 8; ++q) acc[k][q] += __bfloat162float(v[q]);
@@ -208,10 +228,11 @@ __global__ void __launch_bounds__(kArThreads) ar_rmsnorm_kernel(const ArArgs a) 
 }
 
 // bufs / sigs: int64 tensors [world] of device addresses (peer mappings).
+// mc_ptr: multicast address of the symmetric buffer (0 = per-peer loads).
 void ar_rmsnorm(torch::Tensor buf_ptrs, int64_t buf_offset_bytes, torch::Tensor sig_ptrs,
                 torch::Tensor epoch, torch::Tensor done, torch::Tensor status, int64_t rank,
                 int64_t world, int64_t M, int64_t H, c10::optional<torch::Tensor> residual,
-                c10::optional<torch::Tensor> w, torch::Tensor out, double eps) {
+                c10::optional<torch::Tensor> w, torch::Tensor out, double eps, int64_t mc_ptr) {
   TORCH_CHECK(world <= kMaxRanks, "at most 8 ranks");
   TORCH_CHECK(H % 8 == 0 && H / 8 <= 2 * kArThreads, "hidden size unsupported");
   TORCH_CHECK(buf_ptrs.device().is_cpu() && sig_ptrs.device().is_cpu(), "pointer lists on host");
@@ -238,6 +259,7 @@ void ar_rmsnorm(torch::Tensor buf_ptrs, int64_t buf_offset_bytes, torch::Tensor 
   a.H = (int)H;
   a.eps = (float)eps;
   a.signal = 1;
+  a.mc = mc_ptr != 0 ? reinterpret_cast<const bf16*>(mc_ptr + buf_offset_bytes) : nullptr;
   // Every CTA must be resident at once (they wait on peers): at most one per SM.
   const int grid = (int)std::min<int64_t>(M, std::min(num_sms(), 128));
   launch_kernel(ar_rmsnorm_kernel, dim3(grid), dim3(kArThreads), 0,
@@ -279,6 +301,7 @@ void ar_rmsnorm_pushed(torch::Tensor slot_ptrs, torch::Tensor sig_ptrs, torch::T
   a.H = (int)H;
   a.eps = (float)eps;
   a.signal = 0;
+  a.mc = nullptr;
   const int grid = (int)std::min<int64_t>(M, std::min(num_sms(), 128));
   launch_kernel(ar_rmsnorm_kernel, dim3(grid), dim3(kArThreads), 0,
                 at::cuda::getCurrentCUDAStream(), a);

@@ -27,8 +27,9 @@ def test_fused_allreduce_times_out_on_a_silent_peer():
     sp = torch.tensor([s.data_ptr() for s in sigs], dtype=torch.int64)
     t0 = time.time()
     # rank 0 of a 2-rank group whose rank 1 never runs
+    # (plain peer loads: mc_ptr 0, no multicast object is involved)
     ops.ext().ar_rmsnorm(bp, 0, sp, epoch, done, ops.status_buffer(DEV), 0, 2, M, H, None,
-                         None, out, 1e-5)
+                         None, out, 1e-5, 0)
     torch.cuda.synchronize()
     assert time.time() - t0 < 30
     assert ops.read_status(DEV) == PEER_TIMEOUT

@@ -60,9 +60,9 @@ def _worker(rank, world, port, prompts, decode_tokens, mode, q, cfg_name="tiny-l
 
         cfg = get_config(cfg_name)
         tp = TPGroup(rank, world, dist.group.WORLD)
-        if mode in ("fused", "push"):
+        if mode in ("fused", "push", "multimem"):
             tp.fused = FusedTP(dist.group.WORLD, rank, world, dev, cfg.hidden_size, 64,
-                               push=mode == "push")
+                               push=mode == "push", multimem=mode == "multimem")
         m = LlamaModel(cfg, dev, tp=tp).init_random(seed=17, gen_device="cpu")
         m.allocate_kv(64)
         out = _logits(m, prompts, decode_tokens)
@@ -109,9 +109,11 @@ def test_fused_tp_matches_nccl_and_tp1():
     (p_pre, p_dec), st = _run(world, "push", prompts, decode_tokens)
     assert st == 0
     (n_pre, n_dec), _ = _run(world, "nccl", prompts, decode_tokens)
+    (m_pre, m_dec), st = _run(world, "multimem", prompts, decode_tokens)
+    assert st == 0
     scale = ref_pre.abs().max().item()
     for a, b in ((f_pre, ref_pre), (f_dec, ref_dec), (n_pre, ref_pre), (n_dec, ref_dec),
-                 (p_pre, ref_pre), (p_dec, ref_dec)):
+                 (p_pre, ref_pre), (p_dec, ref_dec), (m_pre, ref_pre), (m_dec, ref_dec)):
         assert (a - b).abs().max().item() <= 0.03 * scale + 1e-3
     # Prefill rows run the same GEMM kernel and sum the same bf16 partials
     # in rank order either way: pushing changes nothing in the result.
