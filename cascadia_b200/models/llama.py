@@ -339,8 +339,7 @@ class LlamaModel:
         for i, lw in enumerate(self.layers):
             self._norm(pending if pending is not None else hidden, lw.in_norm, h,
                        residual=hidden if pending is not None else None)
-            qkv = lw.qkv(h)
-            attn = self._attention(i, qkv, batch)
+            attn = self._qkv_attention(i, lw, h, batch)
             if tp1:
                 lw.o(attn, ops.EPI_RESID, residual=hidden, out=hidden)
                 self._norm(hidden, lw.post_norm, h)
@@ -371,8 +370,7 @@ class LlamaModel:
         eps = self.cfg.rms_eps
         self._norm(hidden, self.layers[0].in_norm, h)
         for i, lw in enumerate(self.layers):
-            qkv = lw.qkv(h)
-            attn = self._attention(i, qkv, batch)
+            attn = self._qkv_attention(i, lw, h, batch)
             nxt = self.layers[i + 1].in_norm if i + 1 < len(self.layers) else None
             if fz.push:
                 # The GEMM delivers its partial into every rank's slots.
@@ -389,13 +387,29 @@ class LlamaModel:
             fz.allreduce(1, T, hidden, nxt, h if nxt is not None else h, eps)
         return hidden
 
-    def _attention(self, li: int, qkv: torch.Tensor, batch: "Batch") -> torch.Tensor:
+    def _qkv_attention(self, li: int, lw: LayerWeights, h: torch.Tensor, batch: "Batch"):
+        """q/k/v projection + attention.  On the GPU, when the shapes allow,
+        the projection's epilogue applies RoPE and writes K / V into the
+        paged cache (one launch less per layer)."""
+        T = h.shape[0]
+        if (self.device.type == "cuda" and lw.qkv.blob is not None and
+                ops.rope_fusable(T, self.d, self.cfg.rot_dim, lw.qkv.group_size)):
+            qkv = torch.empty(T, lw.qkv.n, dtype=torch.bfloat16, device=self.device)
+            ops.w4a16_gemm_rope_kv(h, lw.qkv.blob, lw.qkv.n, lw.qkv.group_size, qkv,
+                                   batch.positions, self.cos_sin, batch.slots, self.kv.k,
+                                   self.kv.v, li, self.hq, self.hkv)
+            return self._attention(li, qkv, batch, roped=True)
+        return self._attention(li, lw.qkv(h), batch)
+
+    def _attention(self, li: int, qkv: torch.Tensor, batch: "Batch",
+                   roped: bool = False) -> torch.Tensor:
         hq, hkv, d = self.hq, self.hkv, self.d
         kv = self.kv
         T = qkv.shape[0]
         if self.device.type == "cuda":
-            ops.rope_kv_write(qkv, batch.positions, self.cos_sin, batch.slots, kv.k, kv.v, li,
-                              hq, hkv, d, self.cfg.rot_dim)
+            if not roped:
+                ops.rope_kv_write(qkv, batch.positions, self.cos_sin, batch.slots, kv.k, kv.v,
+                                  li, hq, hkv, d, self.cfg.rot_dim)
             out = torch.empty(T, hq * d, dtype=torch.bfloat16, device=self.device)
             q = qkv[:, :hq * d]
             win, sinks = self.cfg.sliding_window, self.cfg.attention_sinks

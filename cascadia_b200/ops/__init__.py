@@ -9,6 +9,7 @@ the same math (used by the CPU engine and as test oracles) live in
 from __future__ import annotations
 
 import math
+import os
 import threading
 from typing import Optional
 
@@ -203,6 +204,39 @@ def hc_pre(copies: torch.Tensor, fn: torch.Tensor, base: torch.Tensor, scale: to
     [T, hc, dim] fp32 -> (y [T, dim] bf16-valued, post [T, hc],
     comb [T, hc, hc], pre [T, hc])."""
     out = ext().hc_pre(copies.contiguous(), fn, base, scale, iters, hc_eps, norm_eps)
+    LAUNCHES.add(1)
+    return out
+
+
+def _gemv_max_m() -> int:
+    try:
+        return int(os.environ.get("CASCADIA_GEMV_MAX_M", "8"))
+    except ValueError:
+        return 8
+
+
+FUSE_ROPE = os.environ.get("CASCADIA_FUSE_ROPE", "1") != "0"
+
+
+def rope_fusable(m: int, head_dim: int, rot: int, group_size: int) -> bool:
+    """The q/k/v GEMM can carry RoPE and the KV write in its epilogue: the
+    tcgen05 kernel runs (more rows than the small-M kernel takes), head_dim
+    128 with full rotate-half rotation."""
+    return (FUSE_ROPE and m > _gemv_max_m() and head_dim == 128 and rot == 128
+            and group_size in (32, 128))
+
+
+def w4a16_gemm_rope_kv(x, blob, n, group_size, out, positions, cos_sin, slots, k_cache,
+                       v_cache, layer, hq, hkv, workspace: Optional[GemmWorkspace] = None):
+    """The q/k/v projection with RoPE + paged-KV write in its epilogue: out
+    gets the rotated q heads; K and V go straight into the caches."""
+    m, k = x.shape
+    e = ext()
+    ws = workspace or default_workspace(x.device)
+    ws.ensure(e.w4a16_workspace_floats(m, n, k, 0), e.w4a16_counter_count(m, n))
+    e.w4a16_gemm_rope_kv(x, blob, out, n, group_size, ws.ws, ws.counters,
+                         status_buffer(x.device), positions, cos_sin, slots, k_cache, v_cache,
+                         layer, hq, hkv)
     LAUNCHES.add(1)
     return out
 

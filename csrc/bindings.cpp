@@ -36,6 +36,11 @@ std::vector<int64_t> bf16_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t spl
 std::vector<torch::Tensor> hc_pre(torch::Tensor copies, torch::Tensor fn, torch::Tensor base,
                                   torch::Tensor scale, int64_t iters, double hc_eps,
                                   double norm_eps);
+void w4a16_gemm_rope_kv(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t N,
+                        int64_t group_size, torch::Tensor ws, torch::Tensor counters,
+                        torch::Tensor status, torch::Tensor positions, torch::Tensor cos_sin,
+                        torch::Tensor slots, torch::Tensor k_cache, torch::Tensor v_cache,
+                        int64_t layer, int64_t hq, int64_t hkv);
 void w4a16_gemm_push(torch::Tensor x, torch::Tensor wblob, int64_t N, int64_t group_size,
                      torch::Tensor out_ptrs, int64_t ldo, torch::Tensor sig_ptrs, int64_t my_rank,
                      torch::Tensor push_done, torch::Tensor push_epoch, torch::Tensor ws,
@@ -144,6 +149,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("w4a16_workspace_floats", &cb::w4a16_workspace_floats);
   m.def("w4a16_counter_count", &cb::w4a16_counter_count);
   m.def("w4a16_gemm_push", &cb::w4a16_gemm_push);
+  m.def("w4a16_gemm_rope_kv", &cb::w4a16_gemm_rope_kv);
   m.def("bf16_gemm", &cb::bf16_gemm);
   m.def("bf16_gemm_plan", &cb::bf16_gemm_plan);
   m.def("hc_pre", &cb::hc_pre);

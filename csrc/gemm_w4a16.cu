@@ -136,6 +136,17 @@ struct GemmArgs {
   int npeer, my_rank;
   int* push_done;          // local: tiles finished in this launch (self-resetting)
   const int* push_epoch;   // local: last completed all-reduce epoch
+  // Fused RoPE + paged-KV write (the q/k/v projection, store epilogue),
+  // rope_on: head_dim 128 = one 128-row tile per head.  Tile rt < hq is a
+  // q head: rotated (pairs d, d + 64) at rope_pos[m] and stored to out.  A
+  // k head is rotated and written to the K cache row of slot rope_slots[m],
+  // a v head written to the V cache; neither is stored to out.
+  int rope_on, rope_hq, rope_hkv, rope_nb;
+  const int* rope_pos;
+  const float* rope_cs;     // [max_pos, 128] fp32: cos (64) then sin (64)
+  const int* rope_slots;
+  __nv_bfloat16* rope_kc;   // this layer's K cache [blocks, hkv, 16, 128]
+  __nv_bfloat16* rope_vc;
 };
 
 __device__ __forceinline__ __nv_bfloat16* gemm_out_row(const GemmArgs& a, int gm) {
@@ -513,6 +524,37 @@ __global__ void __launch_bounds__(kThreads, 1)
               gemm_out_row(args, gm)[rt * 64 + j] = __float2bfloat16(y);
             }
           }
+        } else if (EPI == kEpiStore && args.rope_on) {
+          const int hh = rt;
+          const bool isq = hh < args.rope_hq;
+          const bool isk = !isq && hh < args.rope_hq + args.rope_hkv;
+          const int kvh = isq ? 0 : (isk ? hh - args.rope_hq : hh - args.rope_hq - args.rope_hkv);
+          for (int idx = t; idx < 64 * MT; idx += kDequantThreads) {
+            const int j = idx & 63, m = idx >> 6;
+            const int gm = m_base + m;
+            if (gm >= m_lim) continue;
+            // The unfused path rotates the bf16 GEMM output: round first.
+            const float x0 = __bfloat162float(__float2bfloat16(tile[j * (MT + 1) + m]));
+            const float x1 = __bfloat162float(__float2bfloat16(tile[(j + 64) * (MT + 1) + m]));
+            float y0 = x0, y1 = x1;
+            if (isq || isk) {
+              const float* cs = args.rope_cs + (size_t)args.rope_pos[gm] * 128;
+              const float c = cs[j], sn = cs[64 + j];
+              y0 = x0 * c - x1 * sn;
+              y1 = x1 * c + x0 * sn;
+            }
+            __nv_bfloat16* dst;
+            if (isq) {
+              dst = gemm_out_row(args, gm) + n0;
+            } else {
+              const int slot = args.rope_slots[gm];
+              if (slot < 0) continue;
+              dst = (isk ? args.rope_kc : args.rope_vc) +
+                    ((((size_t)(slot / 16) * args.rope_hkv + kvh) * 16) + slot % 16) * 128;
+            }
+            dst[j] = __float2bfloat16(y0);
+            dst[64 + j] = __float2bfloat16(y1);
+          }
         } else if (args.npeer > 0) {
           // Push to every rank's slot: 16 consecutive threads write one
           // row's 256 contiguous bytes, so that a warp's P2P stores are two
@@ -839,6 +881,77 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
     else if (epilogue == kEpiSilu) dispatch_mt<32, kEpiSilu>(p.MT, tmap, a, grid, stream);
     else dispatch_mt<32, kEpiResid>(p.MT, tmap, a, grid, stream);
   }
+}
+
+// The q/k/v projection with RoPE and the paged-KV write fused into its
+// epilogue (see GemmArgs::rope_on): out receives the rotated q heads only;
+// k_cache / v_cache are [layers, blocks, hkv, 16, 128], `layer` selects the
+// layer.  Head dim 128, full rotation, rotate-half pairs, the tcgen05 kernel
+// (M above the small-M threshold, the caller checks).
+void w4a16_gemm_rope_kv(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t N,
+                        int64_t group_size, torch::Tensor ws, torch::Tensor counters,
+                        torch::Tensor status, torch::Tensor positions, torch::Tensor cos_sin,
+                        torch::Tensor slots, torch::Tensor k_cache, torch::Tensor v_cache,
+                        int64_t layer, int64_t hq, int64_t hkv) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(1) == 1, "x");
+  const int M = (int)x.size(0);
+  const int K = (int)x.size(1);
+  TORCH_CHECK(K % 128 == 0 && N % 128 == 0 && N == (hq + 2 * hkv) * 128,
+              "rope_kv: N must be (hq + 2 hkv) * 128");
+  TORCH_CHECK(k_cache.dim() == 5 && k_cache.size(4) == 128 && k_cache.size(3) == 16 &&
+                  k_cache.size(2) == hkv && k_cache.is_contiguous() && v_cache.is_contiguous() &&
+                  v_cache.sizes() == k_cache.sizes(),
+              "rope_kv: caches [layers, blocks, hkv, 16, 128]");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.size(1) == 128 &&
+                  cos_sin.is_contiguous(),
+              "rope_kv: cos_sin fp32 [max_pos, 128]");
+  TORCH_CHECK(positions.numel() >= M && slots.numel() >= M &&
+                  positions.scalar_type() == at::kInt && slots.scalar_type() == at::kInt,
+              "rope_kv: int32 positions / slots");
+  TORCH_CHECK(out.size(0) == M && out.size(1) >= hq * 128 && out.stride(1) == 1, "rope_kv: out");
+  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+              "x must be 16-byte aligned");
+  const int64_t blob_bytes =
+      (int64_t)(N / 128) * (K / 128) * (8192 + 128 * (128 / group_size) * 2);
+  TORCH_CHECK(wblob.numel() == blob_bytes, "weight blob has wrong size");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(x.device());
+  GemmPlanInfo p = plan_gemm(M, (int)N, K, 0);
+  if (p.splits > 1) {
+    TORCH_CHECK(ws.numel() >= (int64_t)p.splits * p.token_tiles * p.MT * N, "workspace too small");
+    TORCH_CHECK(counters.numel() >= (int64_t)p.token_tiles * p.row_tiles, "counters too small");
+  }
+  GemmArgs a{};
+  a.wblob = wblob.data_ptr<uint8_t>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.ws = p.splits > 1 ? ws.data_ptr<float>() : nullptr;
+  a.counters = p.splits > 1 ? counters.data_ptr<int>() : nullptr;
+  a.status = status.data_ptr<int>();
+  a.M = M;
+  a.N = (int)N;
+  a.K = K;
+  a.ldo = (int)out.stride(0);
+  a.kb_per_split = p.kbps;
+  a.splits = p.splits;
+  a.trace = g_gemm_trace;
+  a.pdl = pdl_flag();
+  const int64_t layer_elems = k_cache.size(1) * hkv * 16 * 128;
+  a.rope_on = 1;
+  a.rope_hq = (int)hq;
+  a.rope_hkv = (int)hkv;
+  a.rope_nb = (int)k_cache.size(1);
+  a.rope_pos = positions.data_ptr<int>();
+  a.rope_cs = cos_sin.data_ptr<float>();
+  a.rope_slots = slots.data_ptr<int>();
+  a.rope_kc = reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr()) + layer * layer_elems;
+  a.rope_vc = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr()) + layer * layer_elems;
+  CUtensorMap tmap = make_tmap_2d_bf16(x.data_ptr(), (uint64_t)K, (uint64_t)M,
+                                       (uint64_t)x.stride(0) * 2, 64, (uint32_t)p.MT,
+                                       CU_TENSOR_MAP_SWIZZLE_128B);
+  dim3 grid(p.row_tiles, p.splits, p.token_tiles);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  if (group_size == 128) dispatch_mt<128, kEpiStore>(p.MT, tmap, a, grid, stream);
+  else dispatch_mt<32, kEpiStore>(p.MT, tmap, a, grid, stream);
 }
 
 // Row-parallel GEMM of one tensor-parallel rank with the push epilogue (see
