@@ -140,6 +140,10 @@ def choose_parallelism(model: str, gpus: int, batch: int, context: int,
             continue
         if ep > 1 and not cfg.is_moe:
             continue
+        if cfg.is_moe and tp > 1:
+            # The MoE engines shard experts (EP, data-parallel attention)
+            # and layers (PP); their attention is not tensor-parallel.
+            continue
         if cfg.is_moe and cfg.num_experts % ep:
             continue
         per_gpu_w = mb["total"] / (pp * tp * ep)
