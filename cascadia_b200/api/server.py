@@ -279,8 +279,7 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
             health.ok = False
             return JSONResponse({"error": error}, status_code=500)
         health.ok = True
-        usage = {"prompt_tokens": prompt_toks, "completion_tokens": completion,
-                 "total_tokens": prompt_toks + completion}
+        usage = _usage(prompt_toks, completion, getattr(task, "_cached", 0))
         if chat:
             msg: Dict[str, Any] = {"role": "assistant", "content": text}
             calls = parse_tool_calls(tool_call_scan_text(text, task.enable_thinking)) \
@@ -300,9 +299,17 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
                              "logprobs": _lp_json(lps)}],
                 "usage": usage}
 
+    def _usage(prompt_toks: int, completion: int, cached: int) -> dict:
+        u = {"prompt_tokens": prompt_toks, "completion_tokens": completion,
+             "total_tokens": prompt_toks + completion}
+        if cached:
+            u["prompt_tokens_details"] = {"cached_tokens": cached}
+        return u
+
     async def _collect(task, stream):
         text, finish, completion, prompt_toks, error = "", "stop", 0, 0, None
         lps = []
+        task._cached = 0
         stops = task.sampling.stop
         async for c in stream:
             if c.error is not None:
@@ -315,6 +322,8 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
             stats.add_tokens(c.token_count())
             if c.prompt_tokens:
                 prompt_toks = c.prompt_tokens
+            if c.cached_tokens:
+                task._cached = c.cached_tokens
             if c.finish_reason is not None:
                 finish = c.finish_reason.as_openai_str()
             cut = _apply_stop(text, stops)
@@ -329,7 +338,7 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
     async def _sse(task, stream, chat: bool, include_usage: bool, tools_active: bool):
         model = cfg.model_name
         obj = "chat.completion.chunk" if chat else "text_completion"
-        completion = prompt_toks = 0
+        completion = prompt_toks = cached = 0
         stops = task.sampling.stop
         sent = ""       # text already emitted
         pending = ""    # text held back (possible stop-sequence prefix)
@@ -379,6 +388,8 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
                     lp_pending.append(c.logprobs)
                 if c.prompt_tokens:
                     prompt_toks = c.prompt_tokens
+                if c.cached_tokens:
+                    cached = c.cached_tokens
                 if c.finish_reason is not None:
                     finish = c.finish_reason.as_openai_str()
                 if tools_active:
@@ -422,9 +433,7 @@ def make_app(runner, config: Optional[ApiConfig] = None, stats: Optional[ApiStat
             health.ok = True
             if include_usage:
                 yield frame({"id": task.task_id, "object": obj, "created": _now(), "model": model,
-                             "choices": [], "usage": {
-                                 "prompt_tokens": prompt_toks, "completion_tokens": completion,
-                                 "total_tokens": prompt_toks + completion}})
+                             "choices": [], "usage": _usage(prompt_toks, completion, cached)})
             finished = True
             yield b"data: [DONE]\n\n"
         finally:

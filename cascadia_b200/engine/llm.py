@@ -260,14 +260,25 @@ class LLMEngine(Engine):
             self._pending_lp = self._logprobs(
                 [(i, s) for i, s in enumerate(seqs) if not s.in_prefill], logits, toks)
             return toks
+        # Rows whose full logits come back from the last stage: sampled
+        # rows, and rows whose task asked for logprobs.
         want = [i for i, s in enumerate(seqs)
-                if not s.in_prefill and (s.task.temperature > 0 or self._has_penalty(s))]
+                if not s.in_prefill and (s.task.temperature > 0 or self._has_penalty(s)
+                                         or s.task.logprobs > 0)]
         toks, logits = self.pipeline.forward_tokens(batch, hidden, want)
         toks = list(toks)
         if want:
-            picked = self._pick_full([seqs[i] for i in want], logits.to(self.dev))
-            for i, t in zip(want, picked):
-                toks[i] = t
+            logits = logits.to(self.dev)
+            samp = [k for k, i in enumerate(want)
+                    if seqs[i].task.temperature > 0 or self._has_penalty(seqs[i])]
+            if samp:
+                picked = self._pick_full([seqs[want[k]] for k in samp],
+                                         logits.index_select(0, torch.tensor(
+                                             samp, dtype=torch.long, device=self.dev)))
+                for k, t in zip(samp, picked):
+                    toks[want[k]] = t
+            self._pending_lp = self._logprobs([(k, seqs[i]) for k, i in enumerate(want)],
+                                              logits, [toks[i] for i in want])
         return toks
 
     # ------------------------------------------------------------ decode
@@ -517,7 +528,7 @@ class LLMEngine(Engine):
             c.logprobs = lp
             out.append((tid, c))
         fin = Chunk.final_marker(tid, "").with_finish_reason(finish).with_prompt_tokens(
-            len(s.prompt_ids))
+            len(s.prompt_ids)).with_cached_tokens(getattr(s, "cached_prefix", 0))
         task_done(tid, getattr(s, "submitted_at", 0.0) or 0.0, s.first_token_at or 0.0,
                   time.monotonic(), len(s.output_ids), len(s.prompt_ids))
         out.append((tid, fin))

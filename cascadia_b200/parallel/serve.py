@@ -198,9 +198,15 @@ def build_pp_stage(args, ctx: DistContext):
     st = ShardPlan.uniform(name, nl, 1, 1, 1, ctx.world).stages[ctx.rank]
     first, last = ctx.rank == 0, ctx.rank == ctx.world - 1
     shard = ShardSpec(name, st.layer_start, st.layer_end, nl, str(ctx.device), first, last)
+    # The first stage owns the scheduler and the prefix cache.  Every stage
+    # addresses the same block ids (tables and slots travel in the batch
+    # meta), so a cached prefix's K/V rows stay valid in every stage's pool
+    # as long as the first stage keeps the blocks referenced: no
+    # cache / restore frames between stages are needed.
     builder = LLMBuilder(args.model, device=str(ctx.device), kv_blocks=args.kv_blocks or 4096,
                          max_running=args.max_running, max_model_len=args.max_model_len,
-                         use_graph=False, seed=args.seed, tokenizer_path=args.tokenizer)
+                         use_graph=False, seed=args.seed, tokenizer_path=args.tokenizer,
+                         prefix_cache_blocks=args.kv_prefix_cache_size if first else 0)
     for p in builder.load(shard):
         log.info("rank %d load: %s", ctx.rank, p.message)
     model = builder.model

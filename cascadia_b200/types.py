@@ -94,6 +94,7 @@ class Chunk:
     logprobs: Optional[TokenLogprobs] = None
     n_tokens: Optional[int] = None
     prompt_tokens: Optional[int] = None
+    cached_tokens: Optional[int] = None   # prompt tokens served from the prefix cache
     error: Optional[str] = None
     finish_reason: Optional[FinishReason] = None
 
@@ -111,6 +112,10 @@ class Chunk:
 
     def with_prompt_tokens(self, n: int) -> "Chunk":
         self.prompt_tokens = n
+        return self
+
+    def with_cached_tokens(self, n: int) -> "Chunk":
+        self.cached_tokens = n
         return self
 
     def with_finish_reason(self, r: FinishReason) -> "Chunk":
@@ -131,7 +136,7 @@ class Chunk:
         d: Dict[str, Any] = {"task_id": self.task_id, "token_id": self.token_id,
                              "text": self.text, "is_final": self.is_final,
                              "logprobs": asdict(self.logprobs) if self.logprobs else None}
-        for k in ("n_tokens", "prompt_tokens", "error"):
+        for k in ("n_tokens", "prompt_tokens", "cached_tokens", "error"):
             v = getattr(self, k)
             if v is not None:
                 d[k] = v

@@ -134,3 +134,24 @@ def test_gemma4_pp2_serving_equals_one_process_cpu():
     pp2 = _run(args + ["--pp", "2"], nproc=2)
     assert one["error"] is None and len(one["token_ids"]) == 8
     assert pp2["token_ids"] == one["token_ids"]
+
+
+def test_pp2_prefix_cache_hit_matches_one_process_cpu():
+    """A pipeline served with the prefix cache: the second request reuses
+    the first's cached prefix blocks on both stages (reported as cached
+    prompt tokens) and still yields the one-process tokens."""
+    base = list(range(20, 60))  # 40 shared tokens = 2 full KV blocks
+    prompts = [base + [7, 8, 9], base + [90, 91]]
+    args = ["--device", "cpu", "--model", "tiny-llama", "--kv-blocks", "256",
+            "--max-model-len", "512", "--log-level", "warning", "--dist-timeout", "60",
+            "--kv-prefix-cache-size", "64"]
+    got = _serve_and_ask(args + ["--pp", "2"], 2, prompts, 5)
+    for ids, j in zip(prompts, got):
+        ref = _run(["--device", "cpu", "--model", "tiny-llama", "--kv-blocks", "256",
+                    "--max-model-len", "512", "--prompt", "x",
+                    "--prompt-ids", ",".join(map(str, ids)), "--max-tokens", "5",
+                    "--log-level", "warning"])
+        got_ids = [e["token_id"] for e in j["choices"][0]["logprobs"]["content"]]
+        assert got_ids == ref["token_ids"]
+    assert "prompt_tokens_details" not in got[0]["usage"]
+    assert got[1]["usage"]["prompt_tokens_details"]["cached_tokens"] >= 32
