@@ -36,7 +36,7 @@ def main():
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--copies", type=int, default=4, help="weight copies rotated per shape")
     p.add_argument("--splits", type=int, default=0,
-                   help="0 auto; > 0 split-K kernel with that split; -1 stream kernel; "
+                   help="0 auto; > 0 split-K kernel with that split; "
                         "-2 small-M kernel")
     p.add_argument("--graph", type=int, default=1, help="time a CUDA graph of the reps launches")
     p.add_argument("--tp", type=int, default=1,
@@ -155,25 +155,18 @@ def main():
         res[name] = {"us": round(med, 2), "GBps": round(nbytes / med / 1e3, 1),
                      "frac_of_measured_hbm": round(nbytes / med / 1e3 / peak, 3),
                      "plan": plan,
-                     "path": {0: "split-K tcgen05", 1: "stream tcgen05",
-                              2: "small-M"}[plan[0]]}
+                     "path": {0: "split-K tcgen05", 2: "small-M"}[plan[0]]}
         print(name, json.dumps(res[name]), flush=True)
-        if a.trace and plan[0] in (0, 1):
+        if a.trace and plan[0] == 0:
             buf = torch.zeros(1 << 20, dtype=torch.int64, device=dev)
             ops.ext().w4a16_set_trace(buf)
             run(0)
             torch.cuda.synchronize()
             ops.ext().w4a16_set_trace(None)
-            if plan[0] == 0:
-                _, mt, sp, _, tt, rt = plan
-                n = rt * max(sp, 1) * tt
-                names = ["setup", "first_w", "issued", "last_mma", "acc_ready", "partials",
-                         "end"]
-            else:
-                n = plan[2]
-                names = ["tmem", "first_stage", "first_mma", "last_mma", "unit0_out",
-                         "last_unit_out", "end"]
-            width = 8 if plan[0] == 0 else 24
+            _, mt, sp, _, tt, rt = plan
+            n = rt * max(sp, 1) * tt
+            names = ["setup", "first_w", "issued", "last_mma", "acc_ready", "partials", "end"]
+            width = 8
             tr = buf[:n * width].view(n, width).double().cpu()
             t0 = tr[:, 0].min()
             rel = tr - tr[:, :1]
@@ -183,15 +176,6 @@ def main():
                 col = rel[:, i + 1] / 1000
                 q = torch.quantile(col, torch.tensor([0.1, 0.5, 0.9, 1.0], dtype=col.dtype))
                 print(f"    {nm:14s} p10/p50/p90/max us:", [round(float(v), 2) for v in q])
-            if width == 24:  # time spent waiting, per role (medians over CTAs, us)
-                waits = ["mma_wait_stage", "mma_wait_a", "mma_wait_acc", "deq_wait_stage",
-                         "deq_wait_aempty", "deq_work", "prod_wait_empty"]
-                print("    waits (kcycles p50/max):", {w: (round(float(tr[:, 8 + i].median()) / 1000, 1),
-                                                             round(float(tr[:, 8 + i].max()) / 1000, 1))
-                                                          for i, w in enumerate(waits)})
-                print("    issuer 0 clock cycles (p50): 8-MMA issue", float(tr[:, 16].median()),
-                      "job commit", float(tr[:, 17].median()), "step commits",
-                      float(tr[:, 18].median()), "loop total", float(tr[:, 19].median()))
     print("status", ops.read_status(dev))
 
 

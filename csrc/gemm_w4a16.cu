@@ -37,7 +37,6 @@
 #include <cstdlib>
 #include <mutex>
 
-#include "gemm_stream.h"
 #include "gemv_w4a16.h"
 
 #include "common.cuh"
@@ -763,26 +762,22 @@ void set_pdl(bool on) { pdl_flag() = on ? 1 : 0; }
 bool pdl_enabled() { return pdl_flag() != 0; }
 
 // Which kernel runs a GEMM.  `forced`: 0 chooses; > 0 the split-K kernel
-// with that many k-splits; -1 the persistent stream kernel; -2 the small-M
-// kernel (tests and microbenchmarks compare the kernels on one shape).
-enum GemmPath : int { kPathSplitK = 0, kPathStream = 1, kPathSmallM = 2 };
+// with that many k-splits; -2 the small-M kernel (tests and microbenchmarks
+// compare the kernels on one shape).
+enum GemmPath : int { kPathSplitK = 0, kPathSmallM = 2 };
 
 static GemmPath choose_path(int64_t M, int64_t N, int64_t K, int64_t forced) {
+  (void)N;
+  (void)K;
   if (forced > 0) return kPathSplitK;
-  const bool stream_ok = stream_eligible((int)M, (int)N, (int)K);
-  if (forced == -1) return stream_ok ? kPathStream : kPathSplitK;
   if (forced == -2) return gemv_eligible(M) ? kPathSmallM : kPathSplitK;
   if (M <= gemv_max_m() && gemv_eligible(M)) return kPathSmallM;
-  // The stream kernel is selected explicitly for now: measured on B200 at
-  // M = 64 its main loop runs ~0.6 us per 128x128 k-block per SM, like the
-  // split-K kernel, and the split-K grid balances the large shapes better.
   return kPathSplitK;
 }
 
 int64_t w4a16_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t forced_splits) {
   switch (choose_path(M, N, K, forced_splits)) {
     case kPathSmallM: return gemv_workspace_floats(M, N, K, 0);
-    case kPathStream: return stream_plan((int)M, (int)N, (int)K, num_sms()).ws_floats;
     default: break;
   }
   GemmPlanInfo p = plan_gemm((int)M, (int)N, (int)K, (int)forced_splits);
@@ -791,8 +786,8 @@ int64_t w4a16_workspace_floats(int64_t M, int64_t N, int64_t K, int64_t forced_s
 }
 
 // Counters any path may use for an [M, N] output (zero between launches):
-// split-K one per (token tile, row tile), the stream kernel four per row
-// tile, the small-M kernel one per row tile.
+// split-K one per (token tile, row tile), the small-M kernel one per row
+// tile (at least four per row tile are reserved).
 int64_t w4a16_counter_count(int64_t M, int64_t N) {
   const int MT = pick_mt((int)M);
   return (int64_t)std::max<int64_t>((M + MT - 1) / MT, 4) * (N / 128);
@@ -829,17 +824,6 @@ void w4a16_gemm(torch::Tensor x, torch::Tensor wblob, torch::Tensor out, int64_t
                 residual.has_value() ? residual->stride(0) : 0, M, (int)N, K, (int)group_size,
                 (int)epilogue, ws.data_ptr<float>(), counters.data_ptr<int>(),
                 status.data_ptr<int>(), 0, at::cuda::getCurrentCUDAStream());
-    return;
-  }
-  if (path == kPathStream) {
-    const StreamPlan sp = stream_plan(M, (int)N, K, num_sms());
-    TORCH_CHECK(ws.numel() >= sp.ws_floats, "workspace too small");
-    TORCH_CHECK(counters.numel() >= sp.counters, "counters too small");
-    stream_launch(x.data_ptr(), x.stride(0), wblob.data_ptr<uint8_t>(), out.data_ptr(),
-                  out.stride(0), residual.has_value() ? residual->data_ptr() : nullptr,
-                  residual.has_value() ? residual->stride(0) : 0, M, (int)N, K, (int)group_size,
-                  (int)epilogue, ws.data_ptr<float>(), counters.data_ptr<int>(),
-                  status.data_ptr<int>(), at::cuda::getCurrentCUDAStream(), g_gemm_trace);
     return;
   }
   GemmPlanInfo p = plan_gemm(M, (int)N, K, (int)forced_splits);
@@ -1074,14 +1058,9 @@ void w4a16_gemm_grouped(torch::Tensor x, torch::Tensor wblob, torch::Tensor out,
 }
 
 // [path, MT, a, b, c, d]: split-K (0): splits, k-blocks per split, token
-// tiles, row tiles; stream (1): CTAs, tiles per pair, k-blocks per step,
-// steps; small-M (2): zeros.
+// tiles, row tiles; small-M (2): zeros.
 std::vector<int64_t> w4a16_plan(int64_t M, int64_t N, int64_t K, int64_t forced_splits) {
   const GemmPath path = choose_path(M, N, K, forced_splits);
-  if (path == kPathStream) {
-    const StreamPlan p = stream_plan((int)M, (int)N, (int)K, num_sms());
-    return {1, p.MT, p.ctas, p.tpp, p.kstep, (int64_t)p.pairs * p.ksteps};
-  }
   if (path == kPathSmallM) return {2, 0, 0, 0, 0, 0};
   GemmPlanInfo p = plan_gemm((int)M, (int)N, (int)K, (int)forced_splits);
   return {0, p.MT, p.splits, p.kbps, p.token_tiles, p.row_tiles};
@@ -1091,7 +1070,7 @@ std::vector<int64_t> w4a16_plan(int64_t M, int64_t N, int64_t K, int64_t forced_
 
 // ------------------------------------------------------------------ no-alloc entry point
 // The C entry point declared in gemm_w4a16_noalloc.h: the kernel that
-// w4a16_gemm picks for the shape (small-M, persistent stream or split-K),
+// w4a16_gemm picks for the shape (small-M or split-K),
 // with its scratch (fp32 partials, counters and a status word) in a fixed
 // file-scope device array instead of caller tensors.
 #include "gemm_w4a16_noalloc.h"
@@ -1154,8 +1133,7 @@ cudaError_t na_setup(int dev, unsigned char** base, std::string* why) {
   const cudaError_t attrs[] = {
       na_set_attrs<128, cb::kEpiStore>(), na_set_attrs<128, cb::kEpiSilu>(),
       na_set_attrs<128, cb::kEpiResid>(), na_set_attrs<32, cb::kEpiStore>(),
-      na_set_attrs<32, cb::kEpiSilu>(),  na_set_attrs<32, cb::kEpiResid>(),
-      cb::stream_set_attrs()};
+      na_set_attrs<32, cb::kEpiSilu>(),  na_set_attrs<32, cb::kEpiResid>()};
   for (cudaError_t a : attrs)
     if (a != cudaSuccess) {
       *why = "cudaFuncSetAttribute";
@@ -1202,10 +1180,6 @@ extern "C" __attribute__((visibility("default"))) int cb_w4a16_gemm_noalloc(
   if (path == kPathSmallM) {
     ws_floats = gemv_workspace_floats(M, N, K, 0);
     counters = ws_floats > 0 ? N / 128 : 0;
-  } else if (path == kPathStream) {
-    const StreamPlan sp = stream_plan(M, N, K, num_sms());
-    ws_floats = sp.ws_floats;
-    counters = sp.counters;
   } else {
     p = plan_gemm(M, N, K, 0);
     ws_floats = p.splits > 1 ? (long long)p.splits * p.token_tiles * p.MT * N : 0;
@@ -1257,12 +1231,6 @@ extern "C" __attribute__((visibility("default"))) int cb_w4a16_gemm_noalloc(
       gemv_launch(x, ldx, static_cast<const uint8_t*>(wblob), out, ldo,
                   epilogue == kEpiResid ? residual : nullptr, epilogue == kEpiResid ? ldr : 0, M,
                   N, K, group_size, epilogue, ws, ctr, st, 0, s);
-      return CB_NOALLOC_OK;
-    }
-    if (path == kPathStream) {
-      stream_launch(x, ldx, static_cast<const uint8_t*>(wblob), out, ldo,
-                    epilogue == kEpiResid ? residual : nullptr, epilogue == kEpiResid ? ldr : 0,
-                    M, N, K, group_size, epilogue, ws, ctr, st, s);
       return CB_NOALLOC_OK;
     }
     GemmArgs a{};

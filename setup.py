@@ -21,7 +21,6 @@ CSRC = os.path.join(HERE, "csrc")
 SOURCES = [
     "bindings.cpp",
     "gemm_w4a16.cu",
-    "gemm_stream.cu",
     "gemm_bf16.cu",
     "hc.cu",
     "attention.cu",
