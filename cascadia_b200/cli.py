@@ -139,11 +139,32 @@ def _run_distributed(args):
     pp = args.pp
     if tp * pp != ctx.world:
         raise SystemExit(f"--tp {tp} x --pp {pp} must equal the {ctx.world} ranks")
-    if tp > 1 and pp > 1:
-        raise SystemExit("serving combines TP or PP per job: use --tp N or --pp N")
     code = 0
     try:
-        if pp == 1:
+        if tp > 1 and pp > 1:
+            from .parallel.serve import build_pp_tp_stage
+
+            engine, worker, name, control0 = build_pp_tp_stage(args, ctx, pp, tp)
+            if worker is not None:
+                r = Runner(None, model_id=name, device=str(ctx.device))
+                r.start_with_engine(worker, drive=False)
+                code = 1 if r.run_relay_loop() is RelayExit.CONNECTION_FATAL else 0
+                return
+            if ctx.rank != 0:
+                # A replica of the first stage's scheduler; its pipeline
+                # head tells its downstream counterparts to stop afterwards.
+                follower_loop(engine, control0)
+                engine.pipeline.shutdown()
+                return
+            eng = ReplicatedEngine(engine, control0)
+            runner = Runner(None, model_id=name, device=str(ctx.device))
+            runner.start_with_engine(eng)
+            try:
+                _serve_or_prompt(runner, args, name)
+            finally:
+                runner.close()
+                engine.pipeline.shutdown()
+        elif pp == 1:
             engine, name = build_tp_engine(args, ctx)
             if ctx.rank != 0:
                 follower_loop(engine, ctx.control)

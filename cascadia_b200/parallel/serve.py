@@ -24,6 +24,9 @@ layers; the other ranks are :class:`~cascadia_b200.parallel.pp.PipelineWorker`
 stages that receive the hidden rows and the batch meta over NCCL p2p
 (:class:`~cascadia_b200.parallel.pp.NcclChannel`) instead of TCP.
 
+Both (``--pp P --tp T``): P stages of T tensor-parallel ranks each
+(:func:`build_pp_tp_stage`).
+
 Failure handling: the device status word that a kernel's bounded wait sets
 is combined over the TP ranks (max) before the engine decides to fail a
 batch, so every rank drops the same sequences.  A rank that dies makes the
@@ -218,6 +221,64 @@ def build_pp_stage(args, ctx: DistContext):
     engine = builder.build()
     engine.pipeline = PipelineHead(model, ch)
     return engine, None, name
+
+
+def build_pp_tp_stage(args, ctx: DistContext, pp: int, tp: int):
+    """Pipeline stages of tensor-parallel groups (``--pp P --tp T``, P * T
+    ranks): global rank g is TP rank g % T of stage g // T.  Each stage's T
+    ranks hold 1/T of that stage's layers and run their all-reduces in the
+    stage's own group; TP rank t of stage s exchanges hidden rows with TP
+    rank t of the neighbouring stages (every TP rank of a stage holds the
+    full hidden rows after its all-reduce).  The first stage's T ranks run
+    replicas of the scheduler (events broadcast on the first stage's gloo
+    group, as with ``--tp``); the other stages run relay workers.
+
+    Returns (engine, worker, name, control): the engine on the first
+    stage's ranks, the worker elsewhere; `control` is the first stage's
+    gloo group (None off the first stage)."""
+    from ..engine.llm import LLMBuilder
+    from ..models.llama import TPGroup
+    from ..types import ShardPlan, ShardSpec
+    from .pp import NcclChannel, PipelineHead, PipelineWorker
+
+    stage, t = ctx.rank // tp, ctx.rank % tp
+    timeout = datetime.timedelta(seconds=max(60.0, float(getattr(args, "dist_timeout", 300))))
+    # Every rank creates every group, in the same order.
+    stage_groups = [dist.new_group(ranks=list(range(s * tp, (s + 1) * tp)), timeout=timeout)
+                    for s in range(pp)]
+    control0 = dist.new_group(ranks=list(range(tp)), backend="gloo", timeout=timeout)
+    group = stage_groups[stage]
+    name = args.served_model_name or os.path.basename(str(args.model).rstrip("/"))
+    nl = _num_layers(args.model)
+    st = ShardPlan.uniform(name, nl, 1, 1, 1, pp).stages[stage]
+    first, last = stage == 0, stage == pp - 1
+    shard = ShardSpec(name, st.layer_start, st.layer_end, nl, str(ctx.device), first, last)
+    tpg = TPGroup(t, tp, group)
+    # A fixed pool size on every rank: later stages write the blocks the
+    # first stage allocates.
+    builder = LLMBuilder(args.model, device=str(ctx.device), kv_blocks=args.kv_blocks or 4096,
+                         max_running=args.max_running, max_model_len=args.max_model_len,
+                         use_graph=False, seed=args.seed, tp=tpg,
+                         tokenizer_path=args.tokenizer,
+                         prefix_cache_blocks=args.kv_prefix_cache_size if first else 0)
+    if ctx.device.type == "cuda":
+        from ..models.config import get_config
+        from .tp import FusedTP
+
+        if not os.path.isdir(args.model):
+            tpg.fused = FusedTP(group, t, tp, ctx.device, get_config(args.model).hidden_size,
+                                max(64, args.max_running))
+    for p in builder.load(shard):
+        log.info("rank %d (stage %d, tp %d) load: %s", ctx.rank, stage, t, p.message)
+    model = builder.model
+    ch = NcclChannel(ctx.rank, ctx.world, ctx.device, model.payload_in_width)
+    ch.prev = ctx.rank - tp if not first else None
+    ch.next = ctx.rank + tp if not last else None
+    if not first:
+        return None, PipelineWorker(model, ch, is_last=last), name, None
+    engine = builder.build()
+    engine.pipeline = PipelineHead(model, ch)
+    return engine, None, name, control0
 
 
 def _num_layers(model: str) -> int:

@@ -55,6 +55,14 @@ def test_tp2_and_pp2_equal_one_process_cpu():
     assert pp2["token_ids"] == one["token_ids"]
 
 
+def test_pp2_x_tp2_equals_one_process_cpu():
+    """Two pipeline stages of two tensor-parallel ranks each (4 ranks)."""
+    one = _run(CPU_ARGS)
+    both = _run(CPU_ARGS + ["--pp", "2", "--tp", "2"], nproc=4)
+    assert both["error"] is None
+    assert both["token_ids"] == one["token_ids"]
+
+
 def _serve_and_ask(args, nproc, prompt_ids, max_tokens, timeout=240):
     import requests
 
