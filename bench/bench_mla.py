@@ -29,6 +29,7 @@ def main():
     p.add_argument("--heads", type=int, default=64)
     p.add_argument("--layers", type=int, default=4)
     p.add_argument("--reps", type=int, default=20)
+    p.add_argument("--splits", type=int, default=0, help="context splits (0: the planner's)")
     a = p.parse_args()
     dev = torch.device("cuda")
     B, C, H, L = a.batch, a.ctx, a.heads, a.layers
@@ -39,6 +40,8 @@ def main():
     q = (torch.randn(B, H, 576, device=dev) * 0.5).to(torch.bfloat16)
     out = torch.empty(B, H, 512, dtype=torch.bfloat16, device=dev)
     splits, bps = mla_split_plan(B, H, nb)
+    if a.splits > 0:
+        splits, bps = a.splits, -(-nb // a.splits)
     part_o = torch.empty(B * H * splits * 512, dtype=torch.float32, device=dev)
     part_ml = torch.empty(B * H * splits * 2, dtype=torch.float32, device=dev)
     st = ops.status_buffer(dev)
