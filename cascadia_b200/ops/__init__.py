@@ -231,6 +231,10 @@ def w4a16_gemm_rope_kv(x, blob, n, group_size, out, positions, cos_sin, slots, k
     """The q/k/v projection with RoPE + paged-KV write in its epilogue: out
     gets the rotated q heads; K and V go straight into the caches."""
     m, k = x.shape
+    if _dbg.ENABLED and not torch.cuda.is_current_stream_capturing():
+        _dbg.check_range("kv slots", slots[:m], 0, k_cache.shape[1] * 16, allow=(-1,))
+        _dbg.check_range("positions", positions[:m], 0, cos_sin.shape[0])
+        _dbg.check_range("layer", torch.tensor([layer]), 0, k_cache.shape[0])
     e = ext()
     ws = workspace or default_workspace(x.device)
     ws.ensure(e.w4a16_workspace_floats(m, n, k, 0), e.w4a16_counter_count(m, n))
