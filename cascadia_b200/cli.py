@@ -38,17 +38,30 @@ def _parse_hostport(s: str, default_host="127.0.0.1"):
     return (host or default_host), int(port)
 
 
+def _env(name: str, default, cast=str):
+    """Flag default from CASCADIA_<NAME> when set (command line > env >
+    built-in default)."""
+    v = os.environ.get("CASCADIA_" + name)
+    if v is None or v == "":
+        return default
+    try:
+        return cast(v)
+    except ValueError:
+        raise SystemExit(f"CASCADIA_{name}={v!r} is not a valid {cast.__name__}")
+
+
 def _common(p: argparse.ArgumentParser):
-    p.add_argument("--model", required=False, default="tiny-llama",
-                   help="shard directory or model preset (random-init weights)")
-    p.add_argument("--served-model-name", default=None)
-    p.add_argument("--engine", default="llama", choices=sorted(ENGINES))
-    p.add_argument("--device", default="cuda")
-    p.add_argument("--max-model-len", type=int, default=8192)
-    p.add_argument("--max-running", type=int, default=64)
-    p.add_argument("--kv-blocks", type=int, default=0)
-    p.add_argument("--kv-fraction", type=float, default=0.5)
-    p.add_argument("--kv-prefix-cache-size", type=int, default=0,
+    p.add_argument("--model", required=False, default=_env("MODEL", "tiny-llama"),
+                   help="shard directory or model preset (random-init weights); "
+                        "env CASCADIA_MODEL")
+    p.add_argument("--served-model-name", default=_env("SERVED_MODEL_NAME", None))
+    p.add_argument("--engine", default=_env("ENGINE", "llama"), choices=sorted(ENGINES))
+    p.add_argument("--device", default=_env("DEVICE", "cuda"))
+    p.add_argument("--max-model-len", type=int, default=_env("MAX_MODEL_LEN", 8192, int))
+    p.add_argument("--max-running", type=int, default=_env("MAX_RUNNING", 64, int))
+    p.add_argument("--kv-blocks", type=int, default=_env("KV_BLOCKS", 0, int))
+    p.add_argument("--kv-fraction", type=float, default=_env("KV_FRACTION", 0.5, float))
+    p.add_argument("--kv-prefix-cache-size", type=int, default=_env("KV_PREFIX_CACHE_SIZE", 0, int),
                    help="blocks kept for prefix reuse (0 disables)")
     p.add_argument("--no-cuda-graph", action="store_true")
     p.add_argument("--seed", type=int, default=0)
@@ -104,12 +117,50 @@ def _builder(args, tp=None):
                       draft_model=args.draft_model)
 
 
+def validate_run_flags(args) -> None:
+    """Reject flag combinations that cannot run, before any model loads
+    (the reference's validate_worker_runtime_flags does the same for its
+    worker, crates/cascadia-cli/src/lib.rs:1493-1589)."""
+    def bad(msg):
+        raise SystemExit(f"invalid flags: {msg}")
+
+    if args.max_model_len <= 0 or args.max_running <= 0:
+        bad("--max-model-len and --max-running must be positive")
+    if args.kv_blocks < 0 or args.kv_prefix_cache_size < 0:
+        bad("--kv-blocks and --kv-prefix-cache-size must be >= 0")
+    if not 0.0 < args.kv_fraction <= 1.0:
+        bad("--kv-fraction must be in (0, 1]")
+    if args.kv_blocks and args.kv_prefix_cache_size >= args.kv_blocks:
+        bad("--kv-prefix-cache-size must be smaller than --kv-blocks")
+    tp, pp = getattr(args, "tp", 1), getattr(args, "pp", 1)
+    if tp < 1 or pp < 1:
+        bad("--tp and --pp must be >= 1")
+    if args.engine in ("mock", "dsv4") and (tp > 1 or pp > 1):
+        bad(f"--engine {args.engine} serves on one device (expert parallelism runs through "
+            "bench.py)")
+    if args.spec is not None and pp > 1:
+        bad("--spec runs on a single stage (distributed speculative decoding across stages "
+            "is --engine spec)")
+    if args.spec == "draft" and not args.draft_model:
+        bad("--spec draft needs --draft-model")
+    if tp > 1 and not os.path.isdir(str(args.model)):
+        from .models.config import PRESETS
+
+        cfg = PRESETS.get(args.model)
+        if cfg is not None and (cfg.num_heads % tp or cfg.num_kv_heads % tp):
+            bad(f"--tp {tp} must divide the model's {cfg.num_heads} heads and "
+                f"{cfg.num_kv_heads} KV heads")
+    if getattr(args, "prompt_ids", None) and not getattr(args, "prompt", None):
+        bad("--prompt-ids needs --prompt (the one-shot prompt mode)")
+
+
 def cmd_run(args):
     """Serve the model: one process on one device, or, under
     ``torch.distributed.run``, one rank per GPU with ``--tp`` or ``--pp``."""
     from .runtime.runner import Runner
     from .types import PeerLayout, ShardSpec
 
+    validate_run_flags(args)
     _init_logging(args.log_level)
     if int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.tp > 1 or args.pp > 1:
         return _run_distributed(args)
