@@ -132,9 +132,19 @@ def validate_run_flags(args) -> None:
         bad("--kv-fraction must be in (0, 1]")
     if args.kv_blocks and args.kv_prefix_cache_size >= args.kv_blocks:
         bad("--kv-prefix-cache-size must be smaller than --kv-blocks")
-    tp, pp = getattr(args, "tp", 1), getattr(args, "pp", 1)
-    if tp < 1 or pp < 1:
-        bad("--tp and --pp must be >= 1")
+    tp, pp, ep = getattr(args, "tp", 1), getattr(args, "pp", 1), getattr(args, "ep", 1)
+    if tp < 1 or pp < 1 or ep < 1:
+        bad("--tp, --pp and --ep must be >= 1")
+    if ep > 1:
+        from .models.config import PRESETS
+
+        cfg = PRESETS.get(args.model)
+        if tp > 1 or pp > 1:
+            bad("--ep serves the whole model per rank group: no --tp / --pp with it")
+        if cfg is None or not cfg.is_moe:
+            bad("--ep needs a sparse-MoE model preset")
+        elif cfg.num_experts % ep:
+            bad(f"--ep {ep} must divide the model's {cfg.num_experts} experts")
     if args.engine in ("mock", "dsv4") and (tp > 1 or pp > 1):
         bad(f"--engine {args.engine} serves on one device (expert parallelism runs through "
             "bench.py)")
@@ -162,7 +172,8 @@ def cmd_run(args):
 
     validate_run_flags(args)
     _init_logging(args.log_level)
-    if int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.tp > 1 or args.pp > 1:
+    if (int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.tp > 1 or args.pp > 1
+            or args.ep > 1):
         return _run_distributed(args)
     name = args.served_model_name or os.path.basename(str(args.model).rstrip("/"))
     runner = Runner(_builder(args), model_id=name, device=args.device)
@@ -186,6 +197,27 @@ def _run_distributed(args):
 
     ctx = DistContext.from_env("cuda" if args.device.startswith("cuda") else "cpu",
                                timeout_s=args.dist_timeout)
+    if getattr(args, "ep", 1) > 1:
+        from .parallel.serve import build_ep_engine
+
+        if args.ep != ctx.world:
+            raise SystemExit(f"--ep {args.ep} must equal the {ctx.world} ranks")
+        try:
+            engine, name = build_ep_engine(args, ctx)
+            if ctx.rank != 0:
+                follower_loop(engine, ctx.control)
+                return
+            eng = ReplicatedEngine(engine, ctx.control)
+            runner = Runner(None, model_id=name, device=str(ctx.device))
+            runner.start_with_engine(eng)
+            try:
+                _serve_or_prompt(runner, args, name)
+            finally:
+                runner.close()
+        finally:
+            if dist.is_initialized():
+                dist.destroy_process_group()
+        return
     tp = args.tp if args.tp > 1 else (1 if args.pp > 1 else ctx.world)
     pp = args.pp
     if tp * pp != ctx.world:
@@ -427,6 +459,8 @@ def main(argv=None):
     r.add_argument("--api", default="0.0.0.0:8000")
     r.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks (torchrun)")
     r.add_argument("--pp", type=int, default=1, help="pipeline stages over NCCL (torchrun)")
+    r.add_argument("--ep", type=int, default=1,
+                   help="expert-parallel ranks for sparse-MoE models (torchrun)")
     r.add_argument("--dist-timeout", type=float, default=300.0,
                    help="process-group timeout, seconds")
     r.add_argument("--prompt", default=None,

@@ -193,11 +193,15 @@ class LLMEngine(Engine):
         BatchAborted, crates/cascadia-engine/src/lib.rs:56-72)."""
         code = ops.read_status(self.dev)
         tp = getattr(self.model, "tp", None)
-        if tp is not None and tp.size > 1:
+        ep = getattr(self.model, "ep", None)
+        group = tp.group if (tp is not None and tp.size > 1) else (
+            ep.group if (ep is not None and ep.world > 1) else None)
+        if group is not None or (ep is not None and ep.world > 1):
             # Every replica must fail the same batch: the worst status of the
-            # TP ranks decides (one tiny collective per iteration).
-            t = torch.tensor([code], dtype=torch.int32, device=self.dev)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=tp.group)
+            # TP (or EP) ranks decides (one tiny collective per iteration).
+            t = torch.tensor([code], dtype=torch.int32,
+                             device=self.dev if self.dev.type == "cuda" else "cpu")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX, group=group)
             code = int(t.item())
         if code == 0:
             return False
@@ -544,7 +548,10 @@ class LLMBuilder(Builder):
                  kv_fraction: float = 0.5, max_running: int = 64, max_model_len: int = 8192,
                  prefix_cache_blocks: int = 0, use_graph: bool = True, seed: int = 0,
                  tp=None, tokenizer_path: Optional[str] = None, spec: Optional[str] = None,
-                 spec_k: int = 4, draft_model: Optional[str] = None, draft_kv_blocks: int = 0):
+                 spec_k: int = 4, draft_model: Optional[str] = None, draft_kv_blocks: int = 0,
+                 ep=None, max_prefill_tokens: int = 8192):
+        self.ep = ep  # parallel.ep.ExpertParallel: this rank's share of the experts
+        self.max_prefill_tokens = max_prefill_tokens
         self.spec = spec
         self.spec_k = spec_k
         self.draft_name = draft_model
@@ -618,12 +625,13 @@ class LLMBuilder(Builder):
                 tok_dir = os.path.join(self.model_name, "tokenizer")
         else:
             cfg = get_config(self.model_name)
+            extra = {"ep": self.ep} if self.ep is not None else {}
             self.model = self.model_class(cfg)(cfg, self.device, tp=self.tp,
                                                layer_start=shard.layer_start,
                                                layer_end=shard.layer_end,
                                                has_embed=shard.is_first_stage,
-                                               has_head=shard.is_last_stage).init_random(
-                                                   seed=self.seed)
+                                               has_head=shard.is_last_stage,
+                                               **extra).init_random(seed=self.seed)
             tok_dir = self.tokenizer_path
         cfg = self.model.cfg
         self.tokenizer = load_tokenizer(tok_dir, cfg.vocab_size, cfg.eos_token_ids[0])
@@ -682,6 +690,7 @@ class LLMBuilder(Builder):
         if self.model is None:
             raise NotLoaded()
         return LLMEngine(self.model, self.tokenizer, max_running=self.max_running,
+                         max_prefill_tokens=self.max_prefill_tokens,
                          max_model_len=self.max_model_len, use_graph=self.use_graph,
                          prefix_cache_blocks=self.prefix_cache_blocks,
                          model_id=self.model_name, spec=self.spec, draft_model=self.draft,

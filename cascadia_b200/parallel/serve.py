@@ -223,6 +223,35 @@ def build_pp_stage(args, ctx: DistContext):
     return engine, None, name
 
 
+def build_ep_engine(args, ctx: DistContext):
+    """Expert-parallel serving of a sparse-MoE model (``--ep N``): every rank
+    holds 1/N of each layer's routed experts (the model no longer needs to
+    fit one GPU) and a replica of everything else.  The scheduler is
+    replicated as with ``--tp`` (rank 0's events broadcast, every rank steps
+    the same batch), so each rank's MoE layers dispatch the same token rows
+    to the experts' owners and get back the combined rows.  The expert work
+    is not divided (every rank sends every row), the memory is."""
+    from ..engine.llm import LLMBuilder
+    from ..models.config import get_config
+    from ..types import PeerLayout, ShardSpec
+    from .ep import ExpertParallel
+
+    cfg = get_config(args.model)
+    name = args.served_model_name or os.path.basename(str(args.model).rstrip("/"))
+    max_tokens = 2048
+    ep = ExpertParallel(dist.group.WORLD, ctx.rank, ctx.world, ctx.device, cfg.num_experts,
+                        cfg.hidden_size, cfg.num_experts_per_tok, max_tokens=max_tokens)
+    builder = LLMBuilder(args.model, device=str(ctx.device), kv_blocks=args.kv_blocks or 4096,
+                         max_running=min(args.max_running, max_tokens),
+                         max_model_len=args.max_model_len, use_graph=False, seed=args.seed,
+                         tokenizer_path=args.tokenizer, ep=ep, max_prefill_tokens=max_tokens)
+    builder.connect(PeerLayout())
+    nl = cfg.num_layers
+    for p in builder.load(ShardSpec(name, 0, nl, nl, str(ctx.device), True, True)):
+        log.info("rank %d load: %s", ctx.rank, p.message)
+    return builder.build(), name
+
+
 def build_pp_tp_stage(args, ctx: DistContext, pp: int, tp: int):
     """Pipeline stages of tensor-parallel groups (``--pp P --tp T``, P * T
     ranks): global rank g is TP rank g % T of stage g // T.  Each stage's T

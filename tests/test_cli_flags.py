@@ -9,7 +9,7 @@ from cascadia_b200 import cli
 
 def _args(**kw):
     base = dict(model="tiny-llama", engine="llama", max_model_len=512, max_running=8,
-                kv_blocks=0, kv_prefix_cache_size=0, kv_fraction=0.5, tp=1, pp=1, spec=None,
+                kv_blocks=0, kv_prefix_cache_size=0, kv_fraction=0.5, tp=1, pp=1, ep=1, spec=None,
                 draft_model=None, prompt=None, prompt_ids=None)
     base.update(kw)
     return argparse.Namespace(**base)
@@ -41,6 +41,9 @@ def test_env_fallback_and_precedence(monkeypatch):
     (dict(spec="draft"), "draft-model"),
     (dict(model="llama-3.1-8b", tp=3), "must divide"),
     (dict(prompt_ids="1,2"), "needs --prompt"),
+    (dict(ep=2), "sparse-MoE"),
+    (dict(model="tiny-moe", ep=3), "must divide"),
+    (dict(model="tiny-moe", ep=2, tp=2), "no --tp"),
 ])
 def test_bad_combinations_rejected(kw, msg):
     with pytest.raises(SystemExit) as e:

@@ -163,3 +163,13 @@ def test_pp2_prefix_cache_hit_matches_one_process_cpu():
         assert got_ids == ref["token_ids"]
     assert "prompt_tokens_details" not in got[0]["usage"]
     assert got[1]["usage"]["prompt_tokens_details"]["cached_tokens"] >= 32
+
+
+def test_ep2_serving_equals_one_process_cpu():
+    """A sparse-MoE model served with its experts split over two ranks (gloo,
+    the all-to-all path): the same greedy tokens as one process."""
+    args = [a if a != "tiny-llama" else "tiny-moe" for a in CPU_ARGS]
+    one = _run(args)
+    ep2 = _run(args + ["--ep", "2"], nproc=2)
+    assert one["error"] is None and len(one["token_ids"]) == 8
+    assert ep2["token_ids"] == one["token_ids"]
