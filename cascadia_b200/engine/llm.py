@@ -194,9 +194,10 @@ class LLMEngine(Engine):
         code = ops.read_status(self.dev)
         tp = getattr(self.model, "tp", None)
         ep = getattr(self.model, "ep", None)
-        group = tp.group if (tp is not None and tp.size > 1) else (
-            ep.group if (ep is not None and ep.world > 1) else None)
-        if group is not None or (ep is not None and ep.world > 1):
+        tp_on = tp is not None and tp.size > 1
+        ep_on = ep is not None and ep.world > 1
+        group = tp.group if tp_on else (ep.group if ep_on else None)
+        if tp_on or ep_on:
             # Every replica must fail the same batch: the worst status of the
             # TP (or EP) ranks decides (one tiny collective per iteration).
             t = torch.tensor([code], dtype=torch.int32,
